@@ -1,0 +1,592 @@
+// Grouped FP8 block-scale GEMMs of the MoE layer on sm_100a tensor cores.
+//
+// Orientation ("swap-AB"): the MMA's M side is 128 weight rows of one
+// expert, its N side is a tile of BN permuted token rows, both operands are
+// e4m3 and K-major in shared memory with the 128-byte swizzle. One 128-wide
+// K block is four tcgen05.mma (K = 32 each) into a fresh TMEM accumulator;
+// the epilogue warps then fold it into fp32 registers with the block scale of
+// that K block (weight scale, a scalar for the whole tile, times the
+// activation scale, one per token column). That promotion is what the
+// reference does for GEMM1 (solution/cuda/kernel.cu:784-832); here it runs
+// out of a double-buffered TMEM accumulator, so the MMA of block k+1 overlaps
+// the promotion of block k.
+//
+// Roles (one CTA per SM, persistent over a static tile list):
+//   warp 0        TMA producer: weight tiles (2-D TMA), token rows (TMA
+//                 gather4 for GEMM1, 2-D TMA for GEMM2), scales (cp.async)
+//   warp 1        TMEM owner and single-thread MMA issuer
+//   warp 2        scale combiner: weight scale x activation scale per column
+//   warps 3..6    epilogue: TMEM -> registers, promotion, final epilogue
+//
+// GEMM1 computes, for 128 intermediate rows i of block `blk`, both
+//   up[i]   = W13[e, blk*128 + i, :]        . A[tok, :]
+//   gate[i] = W13[e, 2048 + blk*128 + i, :] . A[tok, :]
+// and its fused epilogue writes C = silu(gate) * up (reference semantics,
+// solution/cuda/kernel.h:207) as two e4m3 operands C = s * (hi + lo) with
+// s = amax/448 per (row, 128-block) -- the residual lo keeps ~8 significant
+// bits, so GEMM2 sees C at close to bf16 precision while staying on the
+// e4m3 tensor-core path.
+// GEMM2 computes O[h] = W2[e, h, :] . C[row, :] (hi and lo accumulate into
+// one TMEM accumulator) and red.adds w * O into the fp32 output rows.
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cstdint>
+
+#include "gemm_sm100.h"
+#include "moe_kernels.cuh"
+#include "moe_ptx.cuh"
+#include "moe_shapes.cuh"
+
+namespace moe {
+
+template <int kKind, int BN, int kStages>
+struct GemmTraits {
+  static constexpr bool kIsG1 = kKind != kGemm2;
+  static constexpr int kNumA = kIsG1 ? 2 : 1;     // weight tiles per stage (up+gate / W2)
+  static constexpr int kNumB = kIsG1 ? 1 : 2;     // token tiles per stage (A rows / hi+lo)
+  static constexpr int kATileBytes = 128 * 128;
+  static constexpr int kBTileBytes = BN * 128;
+  static constexpr int kStageBytes = kNumA * kATileBytes + kNumB * kBTileBytes;
+  static constexpr int kKBlocks = kIsG1 ? kHiddenBlocks : kInterBlocks;
+  static constexpr int kRowBlocks = kIsG1 ? kInterBlocks : kHiddenBlocks;
+  static constexpr int kAccCols = kNumA * BN;     // fp32 TMEM columns per accumulator buffer
+  static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32
+                                   : (2 * kAccCols <= 64) ? 64
+                                   : (2 * kAccCols <= 128) ? 128
+                                   : (2 * kAccCols <= 256) ? 256 : 512;
+  static constexpr int kScaleSlots = 8;
+  // scale slot: raw[BN] | wscale[4] | combined[kNumA][BN]
+  static constexpr int kSlotFloats = BN + 4 + kNumA * BN;
+  static constexpr int kEpiWarps = 4;
+  static constexpr int kThreads = (3 + kEpiWarps) * 32;
+  static constexpr int kColsPerLane = BN >= 32 ? BN / 32 : 1;
+  static constexpr uint32_t kIdesc = idesc_e4m3_f32<128, BN>();
+
+  // shared memory layout (offsets from the 1024-aligned base)
+  static constexpr int kOffStages = 0;
+  static constexpr int kOffRing = kStages * kStageBytes;
+  static constexpr int kOffBars = kOffRing + kScaleSlots * kSlotFloats * 4;
+  static constexpr int kNumBars = 2 * kStages + 4 + 3 * kScaleSlots;
+  static constexpr int kOffMisc = kOffBars + kNumBars * 8;
+  // misc: tmem base (4) | abort (4) | unit_pre[33] | seg[33] | epilogue scratch
+  static constexpr int kOffUnitPre = kOffMisc + 16;
+  static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
+  static constexpr int kOffEpi = kOffSeg + 34 * 4;
+  // epilogue scratch: red[4][BN] | inv[BN] | tok[BN] | w[BN]
+  static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
+  static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;  // + alignment slack
+
+  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "BN");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+struct Tile {
+  int e, blk, ks, tt, row0, nvalid, kb0, kb1;
+};
+
+template <int BN, int kKBlocks>
+__device__ __forceinline__ void decode_tile(int u, const int* s_unit_pre, const int* s_seg,
+                                            int splits, Tile& t) {
+  int e = 0;
+#pragma unroll 1
+  while (s_unit_pre[e + 1] <= u) ++e;
+  const int cnt = s_seg[e + 1] - s_seg[e];
+  const int nt = (cnt + BN - 1) / BN;
+  int local = u - s_unit_pre[e];
+  t.e = e;
+  t.tt = local % nt;
+  local /= nt;
+  t.ks = local % splits;
+  t.blk = local / splits;
+  t.row0 = s_seg[e] + t.tt * BN;
+  t.nvalid = min(BN, cnt - t.tt * BN);
+  t.kb0 = t.ks * kKBlocks / splits;
+  t.kb1 = (t.ks + 1) * kKBlocks / splits;
+}
+
+// Column-wise max over the 32 lanes of a warp for 32 columns: after the
+// butterfly lane l holds the max of column l (31 shuffles instead of 160).
+__device__ __forceinline__ float warp_colmax32(const float (&v)[32], int lane) {
+  float a[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const bool hi = lane & 16;
+    const float keep = hi ? v[16 + j] : v[j];
+    const float send = hi ? v[j] : v[16 + j];
+    a[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 16));
+  }
+  float b[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const bool hi = lane & 8;
+    const float keep = hi ? a[8 + j] : a[j];
+    const float send = hi ? a[j] : a[8 + j];
+    b[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 8));
+  }
+  float c[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const bool hi = lane & 4;
+    const float keep = hi ? b[4 + j] : b[j];
+    const float send = hi ? b[j] : b[4 + j];
+    c[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 4));
+  }
+  float d[2];
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const bool hi = lane & 2;
+    const float keep = hi ? c[2 + j] : c[j];
+    const float send = hi ? c[j] : c[2 + j];
+    d[j] = fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 2));
+  }
+  const bool hi = lane & 1;
+  const float keep = hi ? d[1] : d[0];
+  const float send = hi ? d[0] : d[1];
+  return fmaxf(keep, __shfl_xor_sync(0xffffffffu, send, 1));
+}
+
+__device__ __forceinline__ float silu_mul(float gate, float up) {
+  return gate / (1.0f + expf(-gate)) * up;
+}
+
+template <int kKind, int BN, int kStages>
+__global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_b0,
+                    const __grid_constant__ CUtensorMap tm_b1, const GemmParams p) {
+  using Tr = GemmTraits<kKind, BN, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  float* ring = reinterpret_cast<float*>(smem + Tr::kOffRing);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Tr::kOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* accf_bar = bars + 2 * kStages;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* sraw_bar = acce_bar + 2;
+  uint64_t* sfull_bar = sraw_bar + Tr::kScaleSlots;
+  uint64_t* sempty_bar = sfull_bar + Tr::kScaleSlots;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + Tr::kOffMisc);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + Tr::kOffMisc + 4);
+  int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
+  int* s_seg = reinterpret_cast<int*>(smem + Tr::kOffSeg);
+  float* s_red = reinterpret_cast<float*>(smem + Tr::kOffEpi);   // [4][BN]
+  float* s_inv = s_red + 4 * BN;                                 // [BN]
+  int* s_ctok = reinterpret_cast<int*>(s_inv + BN);              // [BN]
+  float* s_cw = reinterpret_cast<float*>(s_ctok + BN);           // [BN]
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int splits = p.splits;
+
+  // ---------------------------------------------------------------- setup
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_b0);
+    if (!Tr::kIsG1) prefetch_tmap(&tm_b1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&accf_bar[b]), 1);
+      mbar_init(smem_u32(&acce_bar[b]), Tr::kEpiWarps);
+    }
+    for (int s = 0; s < Tr::kScaleSlots; ++s) {
+      mbar_init(smem_u32(&sraw_bar[s]), 32);
+      mbar_init(smem_u32(&sfull_bar[s]), 1);
+      mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(s_tmem), Tr::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 2) {
+    // per-expert tile counts -> prefix over experts of the work units
+    const int lo = p.seg_off[lane];
+    const int hi = p.seg_off[lane + 1];
+    const int cnt = hi - lo;
+    const int units = ((cnt + BN - 1) / BN) * Tr::kRowBlocks * splits;
+    int incl = units;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    s_unit_pre[lane + 1] = incl;
+    s_seg[lane] = lo;
+    if (lane == 31) s_seg[32] = hi;
+    if (lane == 0) s_unit_pre[0] = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total_units = s_unit_pre[kExpertsLocal];
+
+  if (warp == 0) {
+    // ======================================================== TMA producer
+    int stage = 0;
+    uint32_t ph = 0;
+    int slot = 0;
+    uint32_t sph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      Tile t;
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      int gid[4] = {0, 0, 0, 0};
+      int ctok[Tr::kColsPerLane];
+      int arow0, arow1 = 0, wrow0, wrow1 = 0;
+      if constexpr (Tr::kIsG1) {
+        if (lane < BN / 4) {
+#pragma unroll
+          for (int r = 0; r < 4; ++r) gid[r] = p.perm_tok[t.row0 + min(4 * lane + r, t.nvalid - 1)];
+        }
+#pragma unroll
+        for (int i = 0; i < Tr::kColsPerLane; ++i) {
+          const int c = lane + 32 * i;
+          ctok[i] = (c < BN) ? p.perm_tok[t.row0 + min(c, t.nvalid - 1)] : 0;
+        }
+        arow0 = t.e * kGemm1Out + t.blk * kBlk;
+        arow1 = arow0 + kInter;
+        wrow0 = (t.e * kGemm1OutBlocks + t.blk) * kHiddenBlocks;
+        wrow1 = (t.e * kGemm1OutBlocks + kInterBlocks + t.blk) * kHiddenBlocks;
+      } else {
+        arow0 = t.e * kHidden + t.blk * kBlk;
+        wrow0 = (t.e * kHiddenBlocks + t.blk) * kInterBlocks;
+      }
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer) ||
+            !mbar_wait(smem_u32(&sempty_bar[slot]), sph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        uint8_t* st = smem + Tr::kOffStages + stage * Tr::kStageBytes;
+        const uint32_t fb = smem_u32(&full_bar[stage]);
+        const int kx = kb * kBlk;
+        if (lane == 0) {
+          mbar_arrive_expect_tx(fb, Tr::kStageBytes);
+          tma_load_2d(smem_u32(st), &tm_w, fb, kx, arow0);
+          if constexpr (Tr::kIsG1) {
+            tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
+          } else {
+            tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_b0, fb, kx, t.row0);
+            tma_load_2d(smem_u32(st + Tr::kATileBytes + Tr::kBTileBytes), &tm_b1, fb, kx, t.row0);
+          }
+        }
+        if constexpr (Tr::kIsG1) {
+          if (lane < BN / 4) {
+            tma_gather4(smem_u32(st + 2 * Tr::kATileBytes + lane * 512), &tm_b0, fb, kx, gid[0],
+                        gid[1], gid[2], gid[3]);
+          }
+        }
+        // scales for this K block
+        float* sp = ring + slot * Tr::kSlotFloats;
+#pragma unroll
+        for (int i = 0; i < Tr::kColsPerLane; ++i) {
+          const int c = lane + 32 * i;
+          if (c < BN) {
+            const float* src;
+            if constexpr (Tr::kIsG1) {
+              src = p.act_scale + static_cast<int64_t>(kb) * p.num_tokens + ctok[i];
+            } else {
+              src = p.act_scale + static_cast<int64_t>(kb) * p.cap + min(t.row0 + c, p.cap - 1);
+            }
+            cp_async_4(smem_u32(sp + c), src);
+          }
+        }
+        if (lane == 0) {
+          cp_async_4(smem_u32(sp + BN), p.w_scale + wrow0 + kb);
+          if constexpr (Tr::kIsG1) cp_async_4(smem_u32(sp + BN + 1), p.w_scale + wrow1 + kb);
+        }
+        cp_async_arrive_noinc(smem_u32(&sraw_bar[slot]));
+        if (++stage == kStages) { stage = 0; ph ^= 1; }
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ========================================================== MMA issuer
+    int stage = 0;
+    uint32_t ph = 0;
+    int abuf = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      Tile t;
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
+            !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t st = smem_u32(smem + Tr::kOffStages + stage * Tr::kStageBytes);
+          const uint32_t d = tmem_base + abuf * Tr::kAccCols;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            if constexpr (Tr::kIsG1) {
+              const uint64_t bdesc = sw128_kmajor_desc(st + 2 * Tr::kATileBytes + 32 * k);
+              umma_f8(d, sw128_kmajor_desc(st + 32 * k), bdesc, Tr::kIdesc, k > 0);
+              umma_f8(d + BN, sw128_kmajor_desc(st + Tr::kATileBytes + 32 * k), bdesc, Tr::kIdesc,
+                      k > 0);
+            } else {
+              const uint64_t adesc = sw128_kmajor_desc(st + 32 * k);
+              umma_f8(d, adesc, sw128_kmajor_desc(st + Tr::kATileBytes + 32 * k), Tr::kIdesc, k > 0);
+              umma_f8(d, adesc, sw128_kmajor_desc(st + Tr::kATileBytes + Tr::kBTileBytes + 32 * k),
+                      Tr::kIdesc, 1);
+            }
+          }
+          umma_commit(smem_u32(&empty_bar[stage]));
+          umma_commit(smem_u32(&accf_bar[abuf]));
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; ph ^= 1; }
+        if (++abuf == 2) { abuf = 0; aph ^= 1; }
+      }
+    }
+  } else if (warp == 2) {
+    // ======================================================= scale combiner
+    int slot = 0;
+    uint32_t sph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      Tile t;
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&sraw_bar[slot]), sph, s_abort, p.status, kStatusTimeoutScale)) {
+          ok = false;
+          break;
+        }
+        float* sp = ring + slot * Tr::kSlotFloats;
+        const float w0 = sp[BN];
+        const float w1 = Tr::kIsG1 ? sp[BN + 1] : 0.f;
+#pragma unroll
+        for (int i = 0; i < Tr::kColsPerLane; ++i) {
+          const int c = lane + 32 * i;
+          if (c < BN) {
+            const float a = sp[c];
+            sp[BN + 4 + c] = a * w0;
+            if constexpr (Tr::kIsG1) sp[BN + 4 + BN + c] = a * w1;
+          }
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sfull_bar[slot]));
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+      }
+    }
+  } else {
+    // ============================================================ epilogue
+    const int q = warp & 3;                   // TMEM lane quarter of this warp
+    const int row_in_tile = q * 32 + lane;    // weight row inside the 128-row block
+    const int et = (warp - 3) * 32 + lane;    // 0..127 inside the epilogue group
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    int slot = 0;
+    uint32_t sph = 0;
+    int abuf = 0;
+    uint32_t aph = 0;
+    bool ok = true;
+    float acc0[BN];
+    float acc1[Tr::kIsG1 ? BN : 1];
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      Tile t;
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      // per-column data for the final epilogue, loaded early
+      int my_tok = 0;
+      float my_w = 0.f;
+      if constexpr (kKind == kGemm2) {
+        if (et < BN && et < t.nvalid) {
+          my_tok = p.perm_tok[t.row0 + et];
+          my_w = p.perm_w[t.row0 + et];
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < BN; ++c) acc0[c] = 0.f;
+      if constexpr (Tr::kIsG1) {
+#pragma unroll
+        for (int c = 0; c < BN; ++c) acc1[c] = 0.f;
+      }
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue) ||
+            !mbar_wait(smem_u32(&accf_bar[abuf]), aph, s_abort, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const float* comb0 = ring + slot * Tr::kSlotFloats + BN + 4;
+        const uint32_t taddr = lane_base + abuf * Tr::kAccCols;
+        if constexpr (BN == 16) {
+          uint32_t v[16];
+          tmem_ld16(taddr, v);
+          uint32_t g[16];
+          if constexpr (Tr::kIsG1) tmem_ld16(taddr + BN, g);
+          tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) acc0[c] = fmaf(__uint_as_float(v[c]), comb0[c], acc0[c]);
+          if constexpr (Tr::kIsG1) {
+#pragma unroll
+            for (int c = 0; c < 16; ++c)
+              acc1[c] = fmaf(__uint_as_float(g[c]), comb0[BN + c], acc1[c]);
+          }
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < BN / 32; ++ch) {
+            uint32_t v[32];
+            tmem_ld32(taddr + ch * 32, v);
+            if constexpr (Tr::kIsG1) {
+              uint32_t g[32];
+              tmem_ld32(taddr + BN + ch * 32, g);
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c) {
+                acc0[ch * 32 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 32 + c], acc0[ch * 32 + c]);
+                acc1[ch * 32 + c] =
+                    fmaf(__uint_as_float(g[c]), comb0[BN + ch * 32 + c], acc1[ch * 32 + c]);
+              }
+            } else {
+              tmem_wait_ld();
+#pragma unroll
+              for (int c = 0; c < 32; ++c)
+                acc0[ch * 32 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 32 + c], acc0[ch * 32 + c]);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&acce_bar[abuf]));
+          mbar_arrive(smem_u32(&sempty_bar[slot]));
+        }
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+        if (++abuf == 2) { abuf = 0; aph ^= 1; }
+      }
+      if (!ok) break;
+
+      // ------------------------------------------------- final epilogue
+      if constexpr (kKind == kGemm1Fused) {
+        // h = silu(gate) * up, kept in acc0
+#pragma unroll
+        for (int c = 0; c < BN; ++c) acc0[c] = silu_mul(acc1[c], acc0[c]);
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+#pragma unroll
+        for (int g = 0; g < (BN + 31) / 32; ++g) {
+          float v[32];
+#pragma unroll
+          for (int c = 0; c < 32; ++c) v[c] = (g * 32 + c < BN) ? fabsf(acc0[min(g * 32 + c, BN - 1)]) : 0.f;
+          const float m = warp_colmax32(v, lane);
+          if (g * 32 + lane < BN) s_red[q * BN + g * 32 + lane] = m;
+        }
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        if (et < BN) {
+          const float amax = fmaxf(fmaxf(s_red[et], s_red[BN + et]), fmaxf(s_red[2 * BN + et], s_red[3 * BN + et]));
+          s_inv[et] = amax > 0.f ? 448.0f / amax : 0.f;
+          if (et < t.nvalid) p.c_scale[static_cast<int64_t>(t.blk) * p.cap + t.row0 + et] = amax * (1.0f / 448.0f);
+        }
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        const int col = t.blk * kBlk + row_in_tile;
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          if (c < t.nvalid) {
+            const float x = acc0[c] * s_inv[c];
+            const __nv_fp8_e4m3 qh(x);
+            const float r = x - static_cast<float>(qh);
+            const __nv_fp8_e4m3 ql(r);
+            const int64_t off = static_cast<int64_t>(t.row0 + c) * kInter + col;
+            p.c_hi[off] = qh.__x;
+            p.c_lo[off] = ql.__x;
+          }
+        }
+      } else if constexpr (kKind == kGemm1Split) {
+        const int col = t.blk * kBlk + row_in_tile;
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          if (c < t.nvalid) {
+            float* dst = p.g1_acc + static_cast<int64_t>(t.row0 + c) * kGemm1Out + col;
+            red_add_f32(dst, acc0[c]);
+            red_add_f32(dst + kInter, acc1[c]);
+          }
+        }
+      } else {
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        if (et < BN) {
+          s_ctok[et] = my_tok;
+          s_cw[et] = my_w;
+        }
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        const int col = t.blk * kBlk + row_in_tile;
+#pragma unroll
+        for (int c = 0; c < BN; ++c) {
+          if (c < t.nvalid) {
+            red_add_f32(p.y_acc + static_cast<int64_t>(s_ctok[c]) * kHidden + col, acc0[c] * s_cw[c]);
+          }
+        }
+      }
+    }
+  }
+
+  // --------------------------------------------------------------- teardown
+  if (*s_abort) {
+    // Let copies that may still be in flight land before the CTA retires.
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Tr::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+template <int kKind, int BN, int kStages>
+static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const CUtensorMap& b1,
+                              const GemmParams& p, int grid, cudaStream_t stream) {
+  using Tr = GemmTraits<kKind, BN, kStages>;
+  auto kern = moe_gemm_kernel<kKind, BN, kStages>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  if (err != cudaSuccess) return err;
+  kern<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(w, b0, b1, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtensorMap& b0,
+                            const CUtensorMap& b1, const GemmParams& p, int grid,
+                            cudaStream_t stream) {
+  switch (kind) {
+    case kGemm1Fused:
+      if (bn == 64) return launch_one<kGemm1Fused, 64, 5>(w, b0, b1, p, grid, stream);
+      if (bn == 32) return launch_one<kGemm1Fused, 32, 6>(w, b0, b1, p, grid, stream);
+      break;
+    case kGemm1Split:
+      if (bn == 16) return launch_one<kGemm1Split, 16, 6>(w, b0, b1, p, grid, stream);
+      if (bn == 32) return launch_one<kGemm1Split, 32, 6>(w, b0, b1, p, grid, stream);
+      break;
+    case kGemm2:
+      if (bn == 128) return launch_one<kGemm2, 128, 4>(w, b0, b1, p, grid, stream);
+      if (bn == 64) return launch_one<kGemm2, 64, 6>(w, b0, b1, p, grid, stream);
+      if (bn == 16) return launch_one<kGemm2, 16, 10>(w, b0, b1, p, grid, stream);
+      break;
+    default:
+      break;
+  }
+  return cudaErrorInvalidValue;
+}
+
+bool gemm_config_supported(int kind, int bn) {
+  switch (kind) {
+    case kGemm1Fused: return bn == 64 || bn == 32;
+    case kGemm1Split: return bn == 16 || bn == 32;
+    case kGemm2: return bn == 128 || bn == 64 || bn == 16;
+    default: return false;
+  }
+}
+
+}  // namespace moe

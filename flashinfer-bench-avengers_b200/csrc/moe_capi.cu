@@ -1,0 +1,388 @@
+// C ABI of the fused MoE layer (declared in include/moe_b200.h).
+//
+// Host orchestration replacing solution/cuda/main.cpp:13-142. Differences
+// by design:
+//   * destination-passing: output and workspace come from the caller, no
+//     allocation inside the call;
+//   * no host synchronisation: expert segment sizes never leave the device
+//     (the reference copies counts to the host, main.cpp:92-103), so a call
+//     can be captured in a CUDA graph;
+//   * one launch per stage for all 32 experts (the reference loops over
+//     experts on the host for GEMM2, main.cpp:112-139).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <algorithm>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/moe_b200.h"
+#include "gemm_sm100.h"
+#include "moe_kernels.cuh"
+#include "moe_shapes.cuh"
+
+namespace moe {
+namespace {
+
+constexpr size_t kAlign = 256;
+
+size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
+
+// Execution plan for one call, a function of T only (so workspace size and
+// launch shapes are known without reading device data).
+struct Plan {
+  bool split_g1;   // decode: K-split GEMM1 + separate SwiGLU
+  int g1_bn;
+  int g1_splits;
+  int g2_bn;
+  int g2_splits;
+};
+
+Plan choose_plan(int64_t T) {
+  Plan p{};
+  if (T <= 64) {
+    p.split_g1 = true;
+    p.g1_bn = 16;
+    p.g1_splits = T <= 16 ? 8 : 4;
+    p.g2_bn = 16;
+    p.g2_splits = T <= 16 ? 2 : 1;
+  } else {
+    p.split_g1 = false;
+    p.g1_bn = 64;
+    p.g1_splits = 1;
+    p.g2_bn = T >= 1024 ? 128 : 64;
+    p.g2_splits = 1;
+  }
+  return p;
+}
+
+struct Layout {
+  moe_b200_workspace_layout l;
+};
+
+moe_b200_workspace_layout make_layout(int64_t T) {
+  moe_b200_workspace_layout l;
+  std::memset(&l, 0, sizeof(l));
+  const Plan plan = choose_plan(T);
+  // Permuted-row capacity: every (token, local expert) pair, at least 256
+  // rows so a TMA box never exceeds the tensor extent.
+  const size_t cap = std::max<size_t>(static_cast<size_t>(T) * kTopK, 256);
+  size_t off = 0;
+  l.counts = off;
+  l.status = off + kExpertsLocal * sizeof(int);
+  off = align_up(off + kExpertsLocal * sizeof(int) + sizeof(uint32_t));
+  l.seg_off = off;
+  off = align_up(off + (kExpertsLocal + 1) * sizeof(int));
+  l.topk_idx = off;
+  off = align_up(off + cap * sizeof(int32_t));
+  l.topk_w = off;
+  off = align_up(off + cap * sizeof(float));
+  l.perm_tok = off;
+  off = align_up(off + cap * sizeof(int32_t));
+  l.perm_w = off;
+  off = align_up(off + cap * sizeof(float));
+  l.c_hi = off;
+  off = align_up(off + cap * kInter);
+  l.c_lo = off;
+  off = align_up(off + cap * kInter);
+  l.c_scale = off;
+  off = align_up(off + cap * kInterBlocks * sizeof(float));
+  l.y_acc = off;
+  off = align_up(off + static_cast<size_t>(T) * kHidden * sizeof(float));
+  if (plan.split_g1) {
+    l.g1_acc = off;
+    off = align_up(off + cap * kGemm1Out * sizeof(float));
+  }
+  l.total_bytes = off;
+  l.cap_rows = static_cast<int64_t>(cap);
+  return l;
+}
+
+// ---------------------------------------------------------------- driver
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+    }
+  });
+  return fn;
+}
+
+// 2-D byte matrix [rows, inner] with row pitch `inner`, 128-byte swizzle.
+bool encode_u8_2d(CUtensorMap* m, const void* base, uint64_t inner, uint64_t rows,
+                  uint32_t box_inner, uint32_t box_rows) {
+  EncodeTiledFn fn = get_encode_fn();
+  if (fn == nullptr) return false;
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {inner};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// ---------------------------------------------------------------- device
+struct DeviceInfo {
+  int checked = 0;
+  int ok = 0;
+  int sm_count = 0;
+};
+
+constexpr int kMaxDevices = 64;
+DeviceInfo g_dev[kMaxDevices];
+std::mutex g_dev_mu;
+
+int current_device_info(DeviceInfo* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return MOE_B200_ERR_CUDA;
+  if (dev < 0 || dev >= kMaxDevices) return MOE_B200_ERR_UNSUPPORTED_DEVICE;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.checked) {
+    int major = 0, minor = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      return MOE_B200_ERR_CUDA;
+    }
+    d.ok = (major == 10 && minor == 0) ? 1 : 0;
+    d.sm_count = sms;
+    d.checked = 1;
+  }
+  *out = d;
+  return d.ok ? MOE_B200_OK : MOE_B200_ERR_UNSUPPORTED_DEVICE;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int64_t div_up(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Upper bound on the number of work units of a grouped GEMM, from T only.
+int grid_for(int64_t T, int bn, int row_blocks, int splits, int sm_count) {
+  const int64_t tiles_a = div_up(T * kTopK, bn) + kExpertsLocal;
+  const int64_t tiles_b = static_cast<int64_t>(kExpertsLocal) * div_up(T, bn);
+  const int64_t units = (tiles_a < tiles_b ? tiles_a : tiles_b) * row_blocks * splits;
+  return static_cast<int>(units < sm_count ? units : sm_count);
+}
+
+int launch_route(const float* logits, const void* bias, int bias_dtype, int T, float rsf,
+                 int local_off, int32_t* topk_idx, float* topk_w, int* counts, cudaStream_t s) {
+  RouteParams rp;
+  rp.logits = logits;
+  rp.bias = bias;
+  rp.bias_is_fp32 = bias_dtype == MOE_B200_BIAS_FP32 ? 1 : 0;
+  rp.num_tokens = T;
+  rp.routed_scaling_factor = rsf;
+  rp.local_expert_offset = local_off;
+  rp.topk_idx = topk_idx;
+  rp.topk_w = topk_w;
+  rp.counts = counts;
+  route_kernel<<<static_cast<unsigned>(div_up(T, 8)), 256, 0, s>>>(rp);
+  return cudaGetLastError() == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" {
+
+int moe_b200_abi_version(void) { return 1; }
+
+size_t moe_b200_workspace_bytes(int64_t num_tokens) {
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return 0;
+  return make_layout(num_tokens).total_bytes;
+}
+
+int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out) {
+  if (out == nullptr || num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  *out = make_layout(num_tokens);
+  return MOE_B200_OK;
+}
+
+const char* moe_b200_status_string(int status) {
+  switch (status) {
+    case MOE_B200_OK: return "ok";
+    case MOE_B200_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case MOE_B200_ERR_MISALIGNED: return "misaligned pointer";
+    case MOE_B200_ERR_WORKSPACE_TOO_SMALL: return "workspace too small";
+    case MOE_B200_ERR_UNSUPPORTED_DEVICE: return "current device is not an sm_100 (B200) GPU";
+    case MOE_B200_ERR_DRIVER: return "cuTensorMapEncodeTiled unavailable or rejected a tensor map";
+    case MOE_B200_ERR_CUDA: return "CUDA runtime error";
+    case MOE_B200_ERR_DEVICE_TIMEOUT: return "a kernel gave up a bounded wait (device timeout)";
+    default: return "unknown status";
+  }
+}
+
+int moe_b200_route(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                   int64_t num_tokens, double routed_scaling_factor, int32_t* topk_idx,
+                   float* topk_w, void* stream) {
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MOE_B200_OK;
+  if (!routing_logits || !routing_bias || !topk_idx || !topk_w) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(topk_idx, 16) ||
+      !aligned(topk_w, 16))
+    return MOE_B200_ERR_MISALIGNED;
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st != MOE_B200_OK) return st;
+  return launch_route(routing_logits, routing_bias, routing_bias_dtype, static_cast<int>(num_tokens),
+                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w, nullptr,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream) {
+  if (workspace == nullptr || status == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const moe_b200_workspace_layout l = make_layout(0);
+  uint32_t v = 0;
+  if (cudaMemcpyAsync(&v, static_cast<const uint8_t*>(workspace) + l.status, sizeof(v),
+                      cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  *status = v;
+  return v == 0 ? MOE_B200_OK : MOE_B200_ERR_DEVICE_TIMEOUT;
+}
+
+int moe_b200_run(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                 const void* hidden_states, const float* hidden_states_scale,
+                 const void* gemm1_weights, const float* gemm1_weights_scale,
+                 const void* gemm2_weights, const float* gemm2_weights_scale,
+                 int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
+                 void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  // ---- argument checks (no device work before they pass) -----------------
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MOE_B200_OK;
+  if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale ||
+      !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale ||
+      !output || !workspace)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
+      !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(output, 16) ||
+      !aligned(hidden_states_scale, 4) || !aligned(gemm1_weights_scale, 4) ||
+      !aligned(gemm2_weights_scale, 4) || !aligned(workspace, kAlign))
+    return MOE_B200_ERR_MISALIGNED;
+  const moe_b200_workspace_layout l = make_layout(num_tokens);
+  if (workspace_bytes < l.total_bytes) return MOE_B200_ERR_WORKSPACE_TOO_SMALL;
+  DeviceInfo di;
+  int st = current_device_info(&di);
+  if (st != MOE_B200_OK) return st;
+
+  const int T = static_cast<int>(num_tokens);
+  const int cap = static_cast<int>(l.cap_rows);
+  // Offsets outside [-2^20, 2^20] select no local expert either way.
+  int local_off = 1 << 21;
+  if (local_expert_offset > -(1 << 20) && local_expert_offset < (1 << 20))
+    local_off = static_cast<int>(local_expert_offset);
+  const Plan plan = choose_plan(num_tokens);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + l.counts);
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws + l.status);
+  int* seg_off = reinterpret_cast<int*>(ws + l.seg_off);
+  int32_t* topk_idx = reinterpret_cast<int32_t*>(ws + l.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(ws + l.topk_w);
+  int32_t* perm_tok = reinterpret_cast<int32_t*>(ws + l.perm_tok);
+  float* perm_w = reinterpret_cast<float*>(ws + l.perm_w);
+  uint8_t* c_hi = ws + l.c_hi;
+  uint8_t* c_lo = ws + l.c_lo;
+  float* c_scale = reinterpret_cast<float*>(ws + l.c_scale);
+  float* y_acc = reinterpret_cast<float*>(ws + l.y_acc);
+  float* g1_acc = plan.split_g1 ? reinterpret_cast<float*>(ws + l.g1_acc) : nullptr;
+
+  // ---- tensor maps ---------------------------------------------------------
+  CUtensorMap tm_hidden, tm_w13, tm_w2, tm_chi, tm_clo;
+  if (!encode_u8_2d(&tm_hidden, hidden_states, kHidden, num_tokens, 128, 1) ||
+      !encode_u8_2d(&tm_w13, gemm1_weights, kHidden, static_cast<uint64_t>(kExpertsLocal) * kGemm1Out,
+                    128, 128) ||
+      !encode_u8_2d(&tm_w2, gemm2_weights, kInter, static_cast<uint64_t>(kExpertsLocal) * kHidden, 128,
+                    128) ||
+      !encode_u8_2d(&tm_chi, c_hi, kInter, cap, 128, plan.g2_bn) ||
+      !encode_u8_2d(&tm_clo, c_lo, kInter, cap, 128, plan.g2_bn))
+    return MOE_B200_ERR_DRIVER;
+
+  // ---- launches ------------------------------------------------------------
+  if (cudaMemsetAsync(ws + l.counts, 0, l.seg_off - l.counts, s) != cudaSuccess) return MOE_B200_ERR_CUDA;
+  if (cudaMemsetAsync(y_acc, 0, static_cast<size_t>(T) * kHidden * sizeof(float), s) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
+                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, counts, s);
+  if (st != MOE_B200_OK) return st;
+
+  PermuteParams pp;
+  pp.topk_idx = topk_idx;
+  pp.topk_w = topk_w;
+  pp.counts = counts;
+  pp.num_tokens = T;
+  pp.local_expert_offset = local_off;
+  pp.seg_off = seg_off;
+  pp.perm_tok = perm_tok;
+  pp.perm_w = perm_w;
+  permute_kernel<<<1, 1024, 0, s>>>(pp);
+  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+
+  GemmParams g1;
+  std::memset(&g1, 0, sizeof(g1));
+  g1.seg_off = seg_off;
+  g1.perm_tok = perm_tok;
+  g1.perm_w = perm_w;
+  g1.act_scale = hidden_states_scale;
+  g1.w_scale = gemm1_weights_scale;
+  g1.num_tokens = T;
+  g1.cap = cap;
+  g1.splits = plan.g1_splits;
+  g1.c_hi = c_hi;
+  g1.c_lo = c_lo;
+  g1.c_scale = c_scale;
+  g1.g1_acc = g1_acc;
+  g1.status = status;
+  const int grid1 = grid_for(num_tokens, plan.g1_bn, kInterBlocks, plan.g1_splits, di.sm_count);
+  if (plan.split_g1) {
+    if (cudaMemsetAsync(g1_acc, 0, static_cast<size_t>(cap) * kGemm1Out * sizeof(float), s) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
+    if (launch_moe_gemm(kGemm1Split, plan.g1_bn, tm_w13, tm_hidden, tm_hidden, g1, grid1, s) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
+    swiglu_quant_kernel<<<di.sm_count * 2, 256, 0, s>>>(seg_off, g1_acc, c_hi, c_lo, c_scale, cap);
+    if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  } else {
+    if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_hidden, tm_hidden, g1, grid1, s) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
+  }
+
+  GemmParams g2 = g1;
+  g2.act_scale = c_scale;
+  g2.w_scale = gemm2_weights_scale;
+  g2.splits = plan.g2_splits;
+  g2.y_acc = y_acc;
+  const int grid2 = grid_for(num_tokens, plan.g2_bn, kHiddenBlocks, plan.g2_splits, di.sm_count);
+  if (launch_moe_gemm(kGemm2, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, s) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+
+  const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
+  int fgrid = static_cast<int>(div_up(n4, 256));
+  if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
+  finalize_kernel<<<fgrid, 256, 0, s>>>(y_acc, static_cast<uint16_t*>(output), n4);
+  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  return MOE_B200_OK;
+}
+
+}  // extern "C"

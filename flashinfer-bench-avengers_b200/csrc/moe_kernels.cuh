@@ -1,0 +1,62 @@
+// Parameter blocks and kernel declarations shared by the .cu files.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace moe {
+
+struct RouteParams {
+  const float* logits;      // [T, 256] fp32
+  const void* bias;         // [256] bf16 or fp32
+  int bias_is_fp32;
+  int num_tokens;           // T
+  float routed_scaling_factor;
+  int local_expert_offset;
+  int32_t* topk_idx;        // [T, 8] global expert ids, best first
+  float* topk_w;            // [T, 8]
+  int* counts;              // [32] local-expert histogram (atomics), may be null
+};
+
+struct PermuteParams {
+  const int32_t* topk_idx;  // [T, 8]
+  const float* topk_w;      // [T, 8]
+  const int* counts;        // [32]
+  int num_tokens;
+  int local_expert_offset;
+  int* seg_off;             // [33] segment starts in the permuted row order
+  int32_t* perm_tok;        // [8T] token of each permuted row
+  float* perm_w;            // [8T] routing weight of each permuted row
+};
+
+// The three grouped-GEMM flavours built from one kernel template.
+enum GemmKind : int {
+  kGemm1Fused = 0,  // GEMM1 over the full K, SwiGLU + hi/lo e4m3 split in the epilogue
+  kGemm1Split = 1,  // GEMM1 over a K slice, fp32 red.add into g1_acc
+  kGemm2 = 2,       // GEMM2 (hi + lo operands), weighted fp32 red.add into y_acc
+};
+
+struct GemmParams {
+  const int* seg_off;       // [33]
+  const int32_t* perm_tok;  // [cap]
+  const float* perm_w;      // [cap]
+  const float* act_scale;   // GEMM1: hidden_states_scale [56, T]; GEMM2: c_scale [16, cap]
+  const float* w_scale;     // GEMM1: [32, 32, 56]; GEMM2: [32, 56, 16]
+  int num_tokens;           // T
+  int cap;                  // row capacity of the permuted buffers (8T)
+  int splits;               // K slices per output tile
+  uint8_t* c_hi;            // [cap, 2048] e4m3
+  uint8_t* c_lo;            // [cap, 2048] e4m3
+  float* c_scale;           // [16, cap] written by kGemm1Fused / swiglu_quant
+  float* g1_acc;            // [cap, 4096] fp32 (kGemm1Split)
+  float* y_acc;             // [T, 7168] fp32 (kGemm2)
+  uint32_t* status;         // device status word
+};
+
+__global__ void route_kernel(RouteParams p);
+__global__ void permute_kernel(PermuteParams p);
+__global__ void swiglu_quant_kernel(const int* seg_off, const float* g1_acc, uint8_t* c_hi,
+                                    uint8_t* c_lo, float* c_scale, int cap);
+__global__ void finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4);
+
+}  // namespace moe

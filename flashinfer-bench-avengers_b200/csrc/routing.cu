@@ -1,0 +1,254 @@
+// DeepSeek-V3 no-aux routing and the token permutation that follows it.
+//
+// route_kernel      one warp per token (reference: noaux_routing_topk8_kernel,
+//                   solution/cuda/kernel.cu:2278-2375, which uses one CTA of
+//                   256 threads per token and a serial thread-0 selection).
+// permute_kernel    deterministic per-expert segments without a host sync
+//                   (reference: count/compute_offsets/fill kernels,
+//                   solution/cuda/kernel.cu:86-100 and 2465-2495, whose fill
+//                   order inside a segment depends on atomics).
+#include <cuda_bf16.h>
+#include <cstdint>
+
+#include "moe_kernels.cuh"
+#include "moe_ptx.cuh"
+#include "moe_shapes.cuh"
+
+namespace moe {
+
+namespace {
+
+// Total order used for every top-k in routing: larger value first, and on
+// equal values the smaller expert index first.
+__device__ __forceinline__ bool ranks_before(float va, int ia, float vb, int ib) {
+  return (va > vb) || (va == vb && ia < ib);
+}
+
+}  // namespace
+
+// Lane l of the warp owns experts 8l .. 8l+7, so group g (32 experts) is
+// owned by lanes 4g .. 4g+3.
+__global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t >= p.num_tokens) return;
+
+  // ---- scores -------------------------------------------------------------
+  const float4* lrow = reinterpret_cast<const float4*>(p.logits + static_cast<int64_t>(t) * kExpertsGlobal);
+  float4 l0 = lrow[2 * lane];
+  float4 l1 = lrow[2 * lane + 1];
+  float x[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  float b[8];
+  if (p.bias_is_fp32) {
+    const float4* brow = reinterpret_cast<const float4*>(p.bias);
+    float4 b0 = brow[2 * lane];
+    float4 b1 = brow[2 * lane + 1];
+    b[0] = b0.x; b[1] = b0.y; b[2] = b0.z; b[3] = b0.w;
+    b[4] = b1.x; b[5] = b1.y; b[6] = b1.z; b[7] = b1.w;
+  } else {
+    const uint4 raw = reinterpret_cast<const uint4*>(p.bias)[lane];
+    const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      b[2 * j] = __uint_as_float(w[j] << 16);
+      b[2 * j + 1] = __uint_as_float(w[j] & 0xFFFF0000u);
+    }
+  }
+  float s[8], sb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    s[j] = 1.0f / (1.0f + expf(-x[j]));   // accurate expf and IEEE division
+    sb[j] = s[j] + b[j];
+  }
+
+  // ---- group score: sum of the two largest biased scores ------------------
+  float m1 = -INFINITY, m2 = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float v = sb[j];
+    if (v > m1) { m2 = m1; m1 = v; }
+    else if (v > m2) { m2 = v; }
+  }
+#pragma unroll
+  for (int off = 1; off <= 2; off <<= 1) {
+    const float o1 = __shfl_xor_sync(0xffffffffu, m1, off);
+    const float o2 = __shfl_xor_sync(0xffffffffu, m2, off);
+    const float n1 = fmaxf(m1, o1);
+    const float n2 = fmaxf(fminf(m1, o1), fmaxf(m2, o2));
+    m1 = n1;
+    m2 = n2;
+  }
+  const float my_group_score = m1 + m2;
+  const int my_group = lane >> 2;
+  int rank = 0;
+#pragma unroll
+  for (int g = 0; g < kGroups; ++g) {
+    const float gs = __shfl_sync(0xffffffffu, my_group_score, 4 * g);
+    rank += ranks_before(gs, g, my_group_score, my_group) ? 1 : 0;
+  }
+  const bool keep = rank < kTopKGroups;
+
+  // ---- top-8 experts among the kept groups --------------------------------
+  float cand[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cand[j] = keep ? sb[j] : -INFINITY;
+  uint32_t taken = 0;
+  int sel_idx[kTopK];
+  float sel_s[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    float bs = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int idx = 8 * lane + j;
+      if (!((taken >> j) & 1u) && ranks_before(cand[j], idx, bv, bi)) {
+        bv = cand[j];
+        bi = idx;
+        bs = s[j];
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+      if (ranks_before(ov, oi, bv, bi)) { bv = ov; bi = oi; bs = os; }
+    }
+    if ((bi >> 3) == lane) taken |= 1u << (bi & 7);
+    sel_idx[k] = bi;
+    sel_s[k] = bs;
+  }
+
+  // ---- weights: unbiased scores renormalised over the selection ------------
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) sum += sel_s[k];
+  sum = fmaxf(sum, 1e-20f);
+  if (lane < kTopK) {
+    int my_idx = sel_idx[0];
+    float my_s = sel_s[0];
+#pragma unroll
+    for (int k = 1; k < kTopK; ++k) {
+      if (lane == k) { my_idx = sel_idx[k]; my_s = sel_s[k]; }
+    }
+    const float w = (my_s / sum) * p.routed_scaling_factor;
+    p.topk_idx[t * kTopK + lane] = my_idx;
+    p.topk_w[t * kTopK + lane] = w;
+    if (p.counts != nullptr) {
+      const int le = my_idx - p.local_expert_offset;
+      if (le >= 0 && le < kExpertsLocal) atomicAdd(&p.counts[le], 1);
+    }
+  }
+}
+
+// One CTA of 1024 threads. Tokens are processed in chunks of 1024 (one per
+// thread); inside a chunk a warp ranks its 32 tokens per expert with ballots,
+// warps are ranked with a shuffle scan, so each expert segment lists its
+// tokens in increasing token order.
+__global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
+  __shared__ int s_off[kExpertsLocal + 1];
+  __shared__ int s_run[kExpertsLocal];
+  __shared__ int s_wcnt[32][kExpertsLocal];  // [warp][expert]
+  __shared__ int s_wpre[32][kExpertsLocal];
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  if (warp == 0) {
+    const int c = p.counts[lane];
+    int incl = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    s_off[lane + 1] = incl;
+    s_run[lane] = incl - c;
+    if (lane == 0) s_off[0] = 0;
+    p.seg_off[lane + 1] = incl;
+    if (lane == 0) p.seg_off[0] = 0;
+  }
+  __syncthreads();
+
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  for (int base = 0; base < p.num_tokens; base += 1024) {
+    const int t = base + tid;
+    uint32_t mask = 0;
+    int sidx[kTopK];
+    float sw[kTopK];
+    if (t < p.num_tokens) {
+      const int4* ip = reinterpret_cast<const int4*>(p.topk_idx + t * kTopK);
+      const float4* wp = reinterpret_cast<const float4*>(p.topk_w + t * kTopK);
+      const int4 i0 = ip[0], i1 = ip[1];
+      const float4 w0 = wp[0], w1 = wp[1];
+      const int ii[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const int le = ii[k] - p.local_expert_offset;
+        sidx[k] = le;
+        sw[k] = ww[k];
+        if (le >= 0 && le < kExpertsLocal) mask |= 1u << le;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) { sidx[k] = -1; sw[k] = 0.f; }
+    }
+
+    // Rank inside the warp, per expert. Ranks of the set bits of `mask` are
+    // packed 5 bits each in increasing expert order.
+    uint64_t ranks = 0;
+    int nset = 0;
+#pragma unroll
+    for (int e = 0; e < kExpertsLocal; ++e) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+      if (lane == e) s_wcnt[warp][e] = __popc(bal);
+      if ((mask >> e) & 1u) {
+        ranks |= static_cast<uint64_t>(__popc(bal & lt_mask)) << (5 * nset);
+        ++nset;
+      }
+    }
+    __syncthreads();
+
+    // Warp w scans expert w over the 32 warps of the chunk.
+    {
+      const int e = warp;
+      const int c = s_wcnt[lane][e];
+      int incl = c;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      const int run = s_run[e];
+      s_wpre[lane][e] = run + incl - c;
+      __syncwarp();
+      if (lane == 31) s_run[e] = run + incl;
+    }
+    __syncthreads();
+
+    uint32_t m = mask;
+    int j = 0;
+    while (m) {
+      const int e = __ffs(m) - 1;
+      m &= m - 1;
+      const int r = static_cast<int>((ranks >> (5 * j)) & 31u);
+      ++j;
+      float w = 0.f;
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        if (sidx[k] == e) w = sw[k];
+      }
+      const int pos = s_wpre[warp][e] + r;
+      p.perm_tok[pos] = t;
+      p.perm_w[pos] = w;
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace moe

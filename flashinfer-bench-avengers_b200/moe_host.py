@@ -1,0 +1,257 @@
+"""Host side of the B200 MoE layer: argument checks, workspace management
+and the ctypes binding of libmoe_b200.so (C ABI in include/moe_b200.h).
+
+PyTorch is used only for device memory and the current stream; all
+computation runs in the library's sm_100a kernels. There is no CPU or
+framework fallback: if the library is missing or the device is not an
+sm_100 GPU, the calls raise.
+
+Argument checks mirror the reference's TORCH_CHECKs
+(solution/cuda/main.cpp:25-40) and raise RuntimeError like they do.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+H = 7168
+I = 2048
+E_GLOBAL = 256
+E_LOCAL = 32
+TOP_K = 8
+HIDDEN_BLOCKS = H // 128
+INTER_BLOCKS = I // 128
+GEMM1_OUT_BLOCKS = 2 * I // 128
+MAX_TOKENS = 262144
+
+BIAS_BF16 = 0
+BIAS_FP32 = 1
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libmoe_b200.so")
+
+_lib = None
+_lib_lock = threading.Lock()
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+
+
+class WorkspaceLayout(ctypes.Structure):
+    _fields_ = [
+        ("total_bytes", ctypes.c_size_t),
+        ("counts", ctypes.c_size_t),
+        ("status", ctypes.c_size_t),
+        ("seg_off", ctypes.c_size_t),
+        ("topk_idx", ctypes.c_size_t),
+        ("topk_w", ctypes.c_size_t),
+        ("perm_tok", ctypes.c_size_t),
+        ("perm_w", ctypes.c_size_t),
+        ("c_hi", ctypes.c_size_t),
+        ("c_lo", ctypes.c_size_t),
+        ("c_scale", ctypes.c_size_t),
+        ("y_acc", ctypes.c_size_t),
+        ("g1_acc", ctypes.c_size_t),
+        ("cap_rows", ctypes.c_int64),
+    ]
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Loads (once) the C-ABI library; raises if it has not been built."""
+    global _lib
+    with _lib_lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(
+                f"{path} is missing: build it with `python build.py` in {_HERE} "
+                "(the MoE layer has no fallback implementation)")
+        lib = ctypes.CDLL(path)
+        lib.moe_b200_workspace_bytes.argtypes = [_I64]
+        lib.moe_b200_workspace_bytes.restype = ctypes.c_size_t
+        lib.moe_b200_run.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64,
+                                     ctypes.c_double, _I64, _P, _P, ctypes.c_size_t, _P]
+        lib.moe_b200_run.restype = ctypes.c_int
+        lib.moe_b200_route.argtypes = [_P, _P, ctypes.c_int, _I64, ctypes.c_double, _P, _P, _P]
+        lib.moe_b200_route.restype = ctypes.c_int
+        lib.moe_b200_read_status.argtypes = [_P, ctypes.POINTER(ctypes.c_uint32), _P]
+        lib.moe_b200_read_status.restype = ctypes.c_int
+        lib.moe_b200_status_string.argtypes = [ctypes.c_int]
+        lib.moe_b200_status_string.restype = ctypes.c_char_p
+        lib.moe_b200_get_workspace_layout.argtypes = [_I64, ctypes.POINTER(WorkspaceLayout)]
+        lib.moe_b200_get_workspace_layout.restype = ctypes.c_int
+        lib.moe_b200_abi_version.argtypes = []
+        lib.moe_b200_abi_version.restype = ctypes.c_int
+        _lib = lib
+        return lib
+
+
+def status_string(code: int) -> str:
+    return load_library().moe_b200_status_string(int(code)).decode()
+
+
+def _raise_on(code: int, what: str) -> None:
+    if code != 0:
+        raise RuntimeError(f"{what} failed: {status_string(code)} (status {code})")
+
+
+def workspace_bytes(num_tokens: int) -> int:
+    return int(load_library().moe_b200_workspace_bytes(int(num_tokens)))
+
+
+def workspace_layout(num_tokens: int) -> WorkspaceLayout:
+    out = WorkspaceLayout()
+    _raise_on(load_library().moe_b200_get_workspace_layout(int(num_tokens), ctypes.byref(out)),
+              "moe_b200_get_workspace_layout")
+    return out
+
+
+# One cached workspace per device; it only grows. Calls on the same device
+# and stream reuse it, which is what stream ordering makes safe.
+_workspaces: dict[int, torch.Tensor] = {}
+_ws_lock = threading.Lock()
+
+
+def get_workspace(num_tokens: int, device: torch.device) -> torch.Tensor:
+    need = workspace_bytes(num_tokens)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    with _ws_lock:
+        ws = _workspaces.get(idx)
+        if ws is None or ws.numel() < need:
+            ws = torch.empty(max(need, 1 << 20), dtype=torch.uint8, device=torch.device("cuda", idx))
+            _workspaces[idx] = ws
+        return ws
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                  gemm1_weights_scale, gemm2_weights, gemm2_weights_scale) -> int:
+    tensors = {
+        "routing_logits": routing_logits,
+        "routing_bias": routing_bias,
+        "hidden_states": hidden_states,
+        "hidden_states_scale": hidden_states_scale,
+        "gemm1_weights": gemm1_weights,
+        "gemm1_weights_scale": gemm1_weights_scale,
+        "gemm2_weights": gemm2_weights,
+        "gemm2_weights_scale": gemm2_weights_scale,
+    }
+    for name, t in tensors.items():
+        _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+        _check(t.is_cuda, f"{name} must be CUDA")
+    dev = routing_logits.device
+    for name, t in tensors.items():
+        _check(t.device == dev, f"{name} must be on {dev}")
+    _check(routing_logits.dim() == 2 and routing_logits.size(1) == E_GLOBAL,
+           f"routing_logits must be [T, {E_GLOBAL}]")
+    T = routing_logits.size(0)
+    _check(T <= MAX_TOKENS, f"at most {MAX_TOKENS} tokens per call")
+    _check(routing_logits.dtype == torch.float32, "routing_logits must be float32")
+    _check(routing_bias.numel() == E_GLOBAL, f"routing_bias must have {E_GLOBAL} elements")
+    _check(tuple(hidden_states.shape) == (T, H), f"hidden_states must be [T, {H}]")
+    _check(hidden_states.dtype == torch.float8_e4m3fn, "hidden_states must be float8_e4m3fn")
+    _check(tuple(hidden_states_scale.shape) == (HIDDEN_BLOCKS, T),
+           f"hidden_states_scale must be [{HIDDEN_BLOCKS}, T]")
+    _check(hidden_states_scale.dtype == torch.float32, "hidden_states_scale must be float32")
+    _check(tuple(gemm1_weights.shape) == (E_LOCAL, 2 * I, H), f"gemm1_weights must be [{E_LOCAL}, {2 * I}, {H}]")
+    _check(gemm1_weights.dtype == torch.float8_e4m3fn, "gemm1_weights must be float8_e4m3fn")
+    _check(tuple(gemm1_weights_scale.shape) == (E_LOCAL, GEMM1_OUT_BLOCKS, HIDDEN_BLOCKS),
+           f"gemm1_weights_scale must be [{E_LOCAL}, {GEMM1_OUT_BLOCKS}, {HIDDEN_BLOCKS}]")
+    _check(gemm1_weights_scale.dtype == torch.float32, "gemm1_weights_scale must be float32")
+    _check(tuple(gemm2_weights.shape) == (E_LOCAL, H, I), f"gemm2_weights must be [{E_LOCAL}, {H}, {I}]")
+    _check(gemm2_weights.dtype == torch.float8_e4m3fn, "gemm2_weights must be float8_e4m3fn")
+    _check(tuple(gemm2_weights_scale.shape) == (E_LOCAL, HIDDEN_BLOCKS, INTER_BLOCKS),
+           f"gemm2_weights_scale must be [{E_LOCAL}, {HIDDEN_BLOCKS}, {INTER_BLOCKS}]")
+    _check(gemm2_weights_scale.dtype == torch.float32, "gemm2_weights_scale must be float32")
+    for name in ("hidden_states", "gemm1_weights", "gemm2_weights"):
+        _check(tensors[name].is_contiguous(), f"{name} must be contiguous")
+    return T
+
+
+def _bias_arg(routing_bias: torch.Tensor) -> tuple[torch.Tensor, int]:
+    b = routing_bias.reshape(-1)
+    if b.dtype == torch.bfloat16:
+        return b.contiguous(), BIAS_BF16
+    return b.to(torch.float32).contiguous(), BIAS_FP32
+
+
+def run_dps(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+            gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+            routed_scaling_factor, output, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Destination-passing form: writes the bf16 [T, 7168] result into ``output``."""
+    T = _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    _check(isinstance(output, torch.Tensor) and output.device == routing_logits.device,
+           "output must be a CUDA tensor on the inputs' device")
+    _check(tuple(output.shape) == (T, H) and output.dtype == torch.bfloat16 and output.is_contiguous(),
+           f"output must be a contiguous bf16 [T, {H}] tensor")
+    if T == 0:
+        return output
+    lib = load_library()
+    dev = routing_logits.device
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias)
+        hs_scale = hidden_states_scale.contiguous()
+        s13 = gemm1_weights_scale.contiguous()
+        s2 = gemm2_weights_scale.contiguous()
+        ws = workspace if workspace is not None else get_workspace(T, dev)
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        code = lib.moe_b200_run(
+            logits.data_ptr(), bias.data_ptr(), bias_dtype, hidden_states.data_ptr(),
+            hs_scale.data_ptr(), gemm1_weights.data_ptr(), s13.data_ptr(), gemm2_weights.data_ptr(),
+            s2.data_ptr(), int(local_expert_offset), float(routed_scaling_factor), T,
+            output.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+    _raise_on(code, "moe_b200_run")
+    return output
+
+
+def run(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+        gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+        routed_scaling_factor) -> torch.Tensor:
+    """Value-returning form of the reference entry point (solution/cuda/main.py:31-54)."""
+    T = _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    out = torch.empty((T, H), dtype=torch.bfloat16, device=routing_logits.device)
+    return run_dps(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                   routed_scaling_factor, out)
+
+
+def route(routing_logits, routing_bias, routed_scaling_factor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Routing only: (topk_idx int32 [T, 8] best first, topk_w fp32 [T, 8])."""
+    _check(routing_logits.is_cuda and routing_logits.dtype == torch.float32
+           and routing_logits.dim() == 2 and routing_logits.size(1) == E_GLOBAL,
+           f"routing_logits must be a CUDA float32 [T, {E_GLOBAL}] tensor")
+    T = routing_logits.size(0)
+    dev = routing_logits.device
+    idx = torch.empty((T, TOP_K), dtype=torch.int32, device=dev)
+    w = torch.empty((T, TOP_K), dtype=torch.float32, device=dev)
+    if T == 0:
+        return idx, w
+    lib = load_library()
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias.to(dev))
+        code = lib.moe_b200_route(logits.data_ptr(), bias.data_ptr(), bias_dtype, T,
+                                  float(routed_scaling_factor), idx.data_ptr(), w.data_ptr(),
+                                  torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_route")
+    return idx, w
+
+
+def read_status(workspace: torch.Tensor) -> int:
+    """Device status word of the last call that used ``workspace`` (0 = clean)."""
+    lib = load_library()
+    st = ctypes.c_uint32(0)
+    with torch.cuda.device(workspace.device):
+        lib.moe_b200_read_status(workspace.data_ptr(), ctypes.byref(st),
+                                 torch.cuda.current_stream(workspace.device).cuda_stream)
+    return int(st.value)

@@ -1,0 +1,137 @@
+/*
+ * moe_b200.h -- C ABI of the B200 (sm_100a) fused FP8 block-scale MoE layer
+ * moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048.
+ *
+ * Plain pointers, sizes and a cudaStream_t passed as void*; no framework
+ * types. All device pointers must live on the current CUDA device.
+ *
+ * Shapes (fixed by the operator definition, reference solution/cuda/kernel.h:8-23):
+ *   H = 7168, I = 2048, E_global = 256, E_local = 32, top_k = 8,
+ *   n_group = 8, topk_group = 4, block = 128.
+ */
+#ifndef MOE_B200_H_
+#define MOE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define MOE_B200_API __attribute__((visibility("default")))
+#else
+#define MOE_B200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes ------------------------------------------------------ */
+#define MOE_B200_OK 0
+#define MOE_B200_ERR_INVALID_ARGUMENT 1   /* null pointer, negative size, bad dtype code */
+#define MOE_B200_ERR_MISALIGNED 2         /* a pointer breaks the alignment rule below */
+#define MOE_B200_ERR_WORKSPACE_TOO_SMALL 3
+#define MOE_B200_ERR_UNSUPPORTED_DEVICE 4 /* current device is not sm_100 */
+#define MOE_B200_ERR_DRIVER 5             /* tensor-map encode unavailable or failed */
+#define MOE_B200_ERR_CUDA 6               /* a CUDA runtime call failed */
+#define MOE_B200_ERR_DEVICE_TIMEOUT 7     /* a kernel gave up a bounded wait */
+
+#define MOE_B200_BIAS_BF16 0
+#define MOE_B200_BIAS_FP32 1
+
+/* Largest num_tokens accepted by the entry points below. */
+#define MOE_B200_MAX_TOKENS 262144
+
+/*
+ * Bytes of device workspace moe_b200_run needs for num_tokens tokens.
+ * The workspace is scratch owned by the caller; its contents need no
+ * initialisation and are rewritten by every call.
+ */
+MOE_B200_API size_t moe_b200_workspace_bytes(int64_t num_tokens);
+
+/*
+ * Full MoE layer, destination-passing style: writes output[T, 7168] (bf16).
+ *
+ * Replaces the reference entry run(...) of solution/cuda/main.py:31-54 /
+ * solution/cuda/main.cpp:13-142 (same arguments, same meaning), with the
+ * output supplied by the caller as in the DPS form of the contest API
+ * (reference README.md:227-257).
+ *
+ *   routing_logits        [T, 256]            fp32
+ *   routing_bias          [256]               bf16 (bias_dtype 0) or fp32 (1)
+ *   hidden_states         [T, 7168]           e4m3 (float8_e4m3fn bytes)
+ *   hidden_states_scale   [56, T]             fp32, block-major
+ *   gemm1_weights         [32, 4096, 7168]    e4m3; rows [0,2048) up, [2048,4096) gate
+ *   gemm1_weights_scale   [32, 32, 56]        fp32
+ *   gemm2_weights         [32, 7168, 2048]    e4m3
+ *   gemm2_weights_scale   [32, 56, 16]        fp32
+ *   local_expert_offset   first global expert id owned by this call
+ *   routed_scaling_factor multiplies the renormalised routing weights
+ *   output                [T, 7168]           bf16, written in full
+ *
+ * Alignment: hidden_states, gemm1_weights, gemm2_weights, routing_logits,
+ * routing_bias and output 16 bytes; workspace 256 bytes.
+ * The call is asynchronous on `stream` (a cudaStream_t) and performs no
+ * host synchronisation, so it may be captured in a CUDA graph.
+ */
+MOE_B200_API int moe_b200_run(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                 const void* hidden_states, const float* hidden_states_scale,
+                 const void* gemm1_weights, const float* gemm1_weights_scale,
+                 const void* gemm2_weights, const float* gemm2_weights_scale,
+                 int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
+                 void* output, void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Routing only: DeepSeek-V3 no-aux top-8 selection and weights.
+ * Replaces the reference launcher launch_noaux_routing_topk8
+ * (solution/cuda/kernel.h:37-44, kernel.cu:2527-2537). Experts are listed
+ * best first (biased score descending, ties to the lower expert id).
+ *   topk_idx [T, 8] int32 global expert ids, topk_w [T, 8] fp32.
+ */
+MOE_B200_API int moe_b200_route(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                   int64_t num_tokens, double routed_scaling_factor, int32_t* topk_idx,
+                   float* topk_w, void* stream);
+
+/*
+ * Reads the device status word of the last moe_b200_run that used this
+ * workspace (synchronises `stream`). *status receives the raw bits (0 when
+ * every bounded wait completed); returns MOE_B200_ERR_DEVICE_TIMEOUT when
+ * any bit is set. No reference counterpart (the reference's waits are
+ * unbounded, solution/cuda/kernel.cu:300-307).
+ */
+MOE_B200_API int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream);
+
+/* Human-readable text for a status code. */
+MOE_B200_API const char* moe_b200_status_string(int status);
+
+/*
+ * Byte offsets of the intermediate buffers inside the workspace, for
+ * inspection by tests. No reference counterpart (the reference allocates
+ * its intermediates per call, solution/cuda/main.cpp:50-108).
+ */
+typedef struct moe_b200_workspace_layout {
+  size_t total_bytes;
+  size_t counts;      /* int32[32] local-expert histogram */
+  size_t status;      /* uint32 status word */
+  size_t seg_off;     /* int32[33] expert segment starts */
+  size_t topk_idx;    /* int32[T, 8] */
+  size_t topk_w;      /* fp32[T, 8] */
+  size_t perm_tok;    /* int32[cap_rows] token of each permuted row */
+  size_t perm_w;      /* fp32[cap_rows] routing weight of each permuted row */
+  size_t c_hi;        /* e4m3[cap_rows, 2048] */
+  size_t c_lo;        /* e4m3[cap_rows, 2048] */
+  size_t c_scale;     /* fp32[16, cap_rows] */
+  size_t y_acc;       /* fp32[T, 7168] */
+  size_t g1_acc;      /* fp32[cap_rows, 4096], 0 when the plan for T does not split K */
+  int64_t cap_rows;   /* max(8T, 256) */
+} moe_b200_workspace_layout;
+
+MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);
+
+/* ABI version of this header (bumped on any signature change). */
+MOE_B200_API int moe_b200_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H_ */

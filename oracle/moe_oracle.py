@@ -1,0 +1,180 @@
+"""CPU oracle of the fused FP8 block-scale MoE layer -- TEST INFRASTRUCTURE.
+
+This module is the checker, never the product: only tests/, the smoke()
+check in __graft_entry__.py and bench.py's CPU-baseline / reference arm
+may import it. The product path (moe_host / libmoe_b200.so) never calls it
+and has no CPU fallback.
+
+It restates, in plain PyTorch-on-CPU fp32, the algorithm of the reference
+solution for moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048:
+
+* routing            solution/cuda/kernel.cu:2278-2375 (noaux_routing_topk8_kernel)
+* permutation        solution/cuda/kernel.cu:2465-2495 (count / fill kernels),
+                     with segments ordered by token id (the reference's order
+                     inside a segment depends on atomics)
+* dequant + GEMM1    solution/cuda/kernel.cu:690-833 (A scale index kt*T+tok,
+                     W13 scale index nblk*56+kt), shapes main.cpp:32-40
+* SwiGLU             solution/cuda/kernel.h:207 -- silu on the second half:
+                     C = silu(G1[:, I:]) * G1[:, :I]
+* GEMM2 + combine    W2 scale [e, h/128, i/128] (kernel.cu:1466 with
+                     S_cols = 16 from main.cpp:130), out[t] += w * O
+* final cast         main.cpp:141 (fp32 -> bf16)
+
+Tie-breaking is made explicit: every top-k orders by value descending and,
+on equal values, by the smaller index (the reference kernel's __ffs / strict
+'>' choices, kernel.cu:2303-2305, 2320, 2361).
+
+Pinning: the reference repository ships no golden vectors, tests or
+fixtures for this path. This restatement is pinned against the output of
+the DeepSeek-routing reference of the same operator in the installed
+flashinfer-python 0.6.11.post2 package
+(flashinfer/trace/templates/moe.py, _trtllm_fp8_block_scale_moe_ds_routing_reference),
+imported only by tests/golden/make_golden.py to write tests/golden/*.npz.
+"""
+from __future__ import annotations
+
+import torch
+
+H = 7168
+I = 2048
+E_GLOBAL = 256
+E_LOCAL = 32
+TOP_K = 8
+N_GROUP = 8
+TOPK_GROUP = 4
+BLOCK = 128
+
+
+def _sort_desc_stable(x: torch.Tensor, dim: int) -> torch.Tensor:
+    """Indices ordering x descending; equal values keep ascending index order."""
+    return torch.sort(x, dim=dim, descending=True, stable=True).indices
+
+
+@torch.no_grad()
+def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, routed_scaling_factor: float):
+    """DeepSeek-V3 no-aux routing (kernel.cu:2278-2375).
+
+    Returns (topk_idx int64 [T, 8] best first, topk_w fp32 [T, 8]).
+    """
+    logits = routing_logits.detach().to("cpu", torch.float32)
+    bias = routing_bias.detach().to("cpu").to(torch.float32).reshape(-1)
+    T = logits.shape[0]
+    s = 1.0 / (1.0 + torch.exp(-logits))
+    sb = s + bias
+    grouped = sb.view(T, N_GROUP, E_GLOBAL // N_GROUP)
+    top2 = torch.sort(grouped, dim=2, descending=True, stable=True).values[:, :, :2]
+    group_scores = top2[:, :, 0] + top2[:, :, 1]
+    kept_groups = _sort_desc_stable(group_scores, 1)[:, :TOPK_GROUP]
+    group_mask = torch.zeros(T, N_GROUP, dtype=torch.bool)
+    group_mask.scatter_(1, kept_groups, True)
+    expert_mask = group_mask.repeat_interleave(E_GLOBAL // N_GROUP, dim=1)
+    pruned = sb.masked_fill(~expert_mask, float("-inf"))
+    topk_idx = _sort_desc_stable(pruned, 1)[:, :TOP_K]
+    s_sel = s.gather(1, topk_idx)
+    total = torch.zeros(T, dtype=torch.float32)
+    for k in range(TOP_K):  # summed in selection order, like the kernel
+        total = total + s_sel[:, k]
+    total = torch.clamp_min(total, 1e-20)
+    topk_w = (s_sel / total.unsqueeze(1)) * float(routed_scaling_factor)
+    return topk_idx, topk_w.to(torch.float32)
+
+
+@torch.no_grad()
+def permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, local_expert_offset: int):
+    """Per-local-expert segments of (token, weight), tokens ascending.
+
+    Returns (seg_off int64 [33], perm_tok int64 [n], perm_w fp32 [n]).
+    """
+    idx = topk_idx.to("cpu", torch.int64)
+    w = topk_w.to("cpu", torch.float32)
+    le = idx - int(local_expert_offset)
+    seg = [0]
+    toks, ws = [], []
+    for e in range(E_LOCAL):
+        hit = le == e                       # [T, 8], at most one hit per row
+        rows = torch.nonzero(hit.any(dim=1), as_tuple=False).squeeze(1)
+        toks.append(rows)
+        ws.append((w * hit).sum(dim=1)[rows])
+        seg.append(seg[-1] + rows.numel())
+    return (torch.tensor(seg, dtype=torch.int64), torch.cat(toks), torch.cat(ws).to(torch.float32))
+
+
+def dequant_hidden(hidden_states: torch.Tensor, hidden_states_scale: torch.Tensor) -> torch.Tensor:
+    """fp8 [T, H] x scale [H/128, T] -> fp32 [T, H]."""
+    a = hidden_states.to("cpu").to(torch.float32)
+    sc = hidden_states_scale.to("cpu", torch.float32).t()           # [T, 56]
+    T = a.shape[0]
+    return (a.view(T, H // BLOCK, BLOCK) * sc.unsqueeze(2)).view(T, H)
+
+
+def dequant_block(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:
+    """fp8 [R, C] x scale [R/128, C/128] -> fp32 [R, C]."""
+    R, C = w.shape
+    wf = w.to("cpu").to(torch.float32).view(R // BLOCK, BLOCK, C // BLOCK, BLOCK)
+    return (wf * scale.to("cpu", torch.float32)[:, None, :, None]).view(R, C)
+
+
+@torch.no_grad()
+def expert_forward(a_rows: torch.Tensor, w13_e, s13_e, w2_e, s2_e, return_c: bool = False):
+    """One expert on fp32 activation rows: GEMM1 -> SwiGLU -> GEMM2."""
+    g1 = a_rows.matmul(dequant_block(w13_e, s13_e).t())
+    x1, x2 = g1[:, :I], g1[:, I:]
+    c = x2 / (1.0 + torch.exp(-x2)) * x1
+    o = c.matmul(dequant_block(w2_e, s2_e).t())
+    return (o, c) if return_c else o
+
+
+@torch.no_grad()
+def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                routed_scaling_factor, token_subset=None, experts=None, return_fp32=False):
+    """Full layer on the CPU. Returns bf16 [T, 7168] (or fp32 with return_fp32).
+
+    token_subset: optional 1-D index tensor; only those rows are computed
+    (each output row depends only on its own token), rows in subset order.
+    experts: optional iterable of local expert ids to include (the others
+    are skipped), used for bounded CPU-baseline samples.
+    """
+    topk_idx, topk_w = route(routing_logits, routing_bias, routed_scaling_factor)
+    hs, hs_scale = hidden_states, hidden_states_scale
+    if token_subset is not None:
+        sub = torch.as_tensor(token_subset, dtype=torch.int64)
+        topk_idx, topk_w = topk_idx[sub], topk_w[sub]
+        hs = hidden_states.to("cpu")[sub]
+        hs_scale = hidden_states_scale.to("cpu")[:, sub]
+    a = dequant_hidden(hs, hs_scale)
+    T = a.shape[0]
+    seg, perm_tok, perm_w = permute(topk_idx, topk_w, local_expert_offset)
+    out = torch.zeros(T, H, dtype=torch.float32)
+    wanted = set(range(E_LOCAL)) if experts is None else set(int(e) for e in experts)
+    for e in range(E_LOCAL):
+        lo, hi = int(seg[e]), int(seg[e + 1])
+        if hi == lo or e not in wanted:
+            continue
+        tok = perm_tok[lo:hi]
+        o = expert_forward(a.index_select(0, tok), gemm1_weights[e], gemm1_weights_scale[e],
+                           gemm2_weights[e], gemm2_weights_scale[e])
+        out.index_add_(0, tok, o * perm_w[lo:hi].unsqueeze(1))
+    return out if return_fp32 else out.to(torch.bfloat16)
+
+
+def active_local_experts(routing_logits, routing_bias, routed_scaling_factor, local_expert_offset):
+    """Sorted local expert ids selected by at least one token."""
+    idx, _ = route(routing_logits, routing_bias, routed_scaling_factor)
+    le = idx - int(local_expert_offset)
+    le = le[(le >= 0) & (le < E_LOCAL)]
+    return sorted(set(le.tolist()))
+
+
+def output_close(out: torch.Tensor, ref: torch.Tensor, rel: float = 1e-2, frac: float = 0.999):
+    """The layer's tolerance: |out - ref| <= rel * max|ref| on >= frac of elements.
+
+    Returns (ok, matched_fraction, max_abs_err, max_abs_ref).
+    """
+    o = out.detach().to("cpu", torch.float32)
+    r = ref.detach().to("cpu", torch.float32)
+    ref_max = float(r.abs().max()) if r.numel() else 0.0
+    err = (o - r).abs()
+    tol = rel * ref_max
+    matched = float((err <= tol).float().mean()) if r.numel() else 1.0
+    return matched >= frac, matched, float(err.max()) if r.numel() else 0.0, ref_max

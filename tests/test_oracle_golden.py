@@ -1,0 +1,38 @@
+"""Pins the CPU oracle against the golden fixtures (independent reference
+implementation of the operator, see tests/golden/make_golden.py)."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+from conftest import golden_files, golden_inputs, load_golden
+
+import moe_oracle
+import workloads
+
+
+@pytest.mark.parametrize("path", golden_files(), ids=lambda p: p.rsplit("/", 1)[-1][:-4])
+def test_oracle_matches_golden(path):
+    g = load_golden(path)
+    inp, active = golden_inputs(g)
+    out = moe_oracle.moe_forward(*workloads.as_args(inp))
+    ref = g["output"]
+    assert out.shape == ref.shape == (g["T"], workloads.H)
+    # Same fp32 math in a different operation order: the bf16 results agree
+    # to within one bf16 ulp of the larger value almost everywhere.
+    ok, matched, max_err, ref_max = moe_oracle.output_close(out, ref, rel=1e-3, frac=0.9999)
+    assert ok, f"matched {matched:.6f}, max err {max_err} vs max|ref| {ref_max}"
+    # and to the layer's own tolerance on every element
+    ok, matched, _, _ = moe_oracle.output_close(out, ref, rel=1e-2, frac=1.0)
+    assert ok
+    exact = float((out.view(torch.int16) == ref.view(torch.int16)).float().mean())
+    assert exact > 0.95, f"only {exact:.4f} of elements bit-identical"
+
+
+def test_golden_cases_cover_offsets_and_variants():
+    cases = [load_golden(p) for p in golden_files()]
+    assert len(cases) >= 5
+    assert {c["variant"] for c in cases} >= {"uniform", "hot", "zipf"}
+    assert {c["local_expert_offset"] for c in cases} >= {0, 32, 224}
+    assert any(c["T"] == 1 for c in cases)
+    assert any(c["T"] == 16 and c["seed"] == 0 for c in cases)
