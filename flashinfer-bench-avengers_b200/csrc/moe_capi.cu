@@ -194,6 +194,15 @@ int launch_route(const float* logits, const void* bias, int bias_dtype, int T, f
   return cudaGetLastError() == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }
 
+thread_local cudaEvent_t t_stage_events[MOE_B200_NUM_STAGE_EVENTS];
+thread_local bool t_stage_events_on = false;
+
+// External event records, so the marks also fire when the call is replayed
+// from a captured CUDA graph.
+void mark_stage(int i, cudaStream_t s) {
+  if (t_stage_events_on) cudaEventRecordWithFlags(t_stage_events[i], s, cudaEventRecordExternal);
+}
+
 }  // namespace
 }  // namespace moe
 
@@ -202,6 +211,20 @@ using namespace moe;
 extern "C" {
 
 int moe_b200_abi_version(void) { return 1; }
+
+int moe_b200_set_stage_events(void* const* events, int num_events) {
+  if (events == nullptr) {
+    t_stage_events_on = false;
+    return MOE_B200_OK;
+  }
+  if (num_events != MOE_B200_NUM_STAGE_EVENTS) return MOE_B200_ERR_INVALID_ARGUMENT;
+  for (int i = 0; i < MOE_B200_NUM_STAGE_EVENTS; ++i) {
+    if (events[i] == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+    t_stage_events[i] = static_cast<cudaEvent_t>(events[i]);
+  }
+  t_stage_events_on = true;
+  return MOE_B200_OK;
+}
 
 size_t moe_b200_workspace_bytes(int64_t num_tokens) {
   if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return 0;
@@ -321,12 +344,15 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
     return MOE_B200_ERR_DRIVER;
 
   // ---- launches ------------------------------------------------------------
+  mark_stage(0, s);
   if (cudaMemsetAsync(ws + l.counts, 0, l.seg_off - l.counts, s) != cudaSuccess) return MOE_B200_ERR_CUDA;
   if (cudaMemsetAsync(y_acc, 0, static_cast<size_t>(T) * kHidden * sizeof(float), s) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
+  mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
                     static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, counts, s);
   if (st != MOE_B200_OK) return st;
+  mark_stage(2, s);
 
   PermuteParams pp;
   pp.topk_idx = topk_idx;
@@ -339,6 +365,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.perm_w = perm_w;
   permute_kernel<<<1, 1024, 0, s>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  mark_stage(3, s);
 
   GemmParams g1;
   std::memset(&g1, 0, sizeof(g1));
@@ -368,6 +395,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
       return MOE_B200_ERR_CUDA;
   }
 
+  mark_stage(4, s);
   GemmParams g2 = g1;
   g2.act_scale = c_scale;
   g2.w_scale = gemm2_weights_scale;
@@ -376,12 +404,14 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   const int grid2 = grid_for(num_tokens, plan.g2_bn, kHiddenBlocks, plan.g2_splits, di.sm_count);
   if (launch_moe_gemm(kGemm2, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, s) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
+  mark_stage(5, s);
 
   const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
   int fgrid = static_cast<int>(div_up(n4, 256));
   if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
   finalize_kernel<<<fgrid, 256, 0, s>>>(y_acc, static_cast<uint16_t*>(output), n4);
   if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  mark_stage(6, s);
   return MOE_B200_OK;
 }
 

@@ -83,6 +83,8 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_status_string.restype = ctypes.c_char_p
         lib.moe_b200_get_workspace_layout.argtypes = [_I64, ctypes.POINTER(WorkspaceLayout)]
         lib.moe_b200_get_workspace_layout.restype = ctypes.c_int
+        lib.moe_b200_set_stage_events.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int]
+        lib.moe_b200_set_stage_events.restype = ctypes.c_int
         lib.moe_b200_abi_version.argtypes = []
         lib.moe_b200_abi_version.restype = ctypes.c_int
         _lib = lib
@@ -255,3 +257,20 @@ def read_status(workspace: torch.Tensor) -> int:
         lib.moe_b200_read_status(workspace.data_ptr(), ctypes.byref(st),
                                  torch.cuda.current_stream(workspace.device).cuda_stream)
     return int(st.value)
+
+
+NUM_STAGE_EVENTS = 7
+STAGE_NAMES = ("clear", "route", "permute", "gemm1", "gemm2", "finalize")
+
+
+def set_stage_events(events) -> None:
+    """Profiling hook: record these 7 torch.cuda.Event objects at the stage
+    boundaries of every later run on this thread (None switches it off).
+    Each event must already have been recorded once (torch creates the
+    underlying CUDA event lazily)."""
+    lib = load_library()
+    if events is None:
+        _raise_on(lib.moe_b200_set_stage_events(None, 0), "moe_b200_set_stage_events")
+        return
+    arr = (ctypes.c_void_p * NUM_STAGE_EVENTS)(*[ctypes.c_void_p(e.cuda_event) for e in events])
+    _raise_on(lib.moe_b200_set_stage_events(arr, NUM_STAGE_EVENTS), "moe_b200_set_stage_events")

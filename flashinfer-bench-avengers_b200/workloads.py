@@ -104,9 +104,12 @@ def make_expert_weights(seed: int, le: int, device="cpu"):
 
 def make_inputs(T: int, seed: int = 0, device="cpu", variant: str = "uniform",
                 local_expert_offset: int = 0, routed_scaling_factor: float = 2.5,
-                experts=None) -> dict:
+                experts=None, weight_seed: int | None = None) -> dict:
     """All ten arguments of run(...). ``experts`` lists the local experts whose
-    weights are materialised (default: all 32); the others are zero."""
+    weights are materialised (default: all 32); the others are zero.
+    ``weight_seed`` (default ``seed``) seeds the expert weights separately,
+    so expert-parallel ranks can share tokens but own different experts."""
+    wseed = seed if weight_seed is None else weight_seed
     device = torch.device(device)
     out = make_routing_inputs(T, seed, device, variant, local_expert_offset)
     hs, hs_scale = make_hidden(T, seed, device)
@@ -115,7 +118,7 @@ def make_inputs(T: int, seed: int = 0, device="cpu", variant: str = "uniform",
     w2 = torch.zeros(E_LOCAL, H, I, dtype=torch.float8_e4m3fn, device=device)
     s2 = torch.ones(E_LOCAL, H // BLOCK, I // BLOCK, dtype=torch.float32, device=device)
     for le in (range(E_LOCAL) if experts is None else experts):
-        q13, sc13, q2, sc2 = make_expert_weights(seed, le, device)
+        q13, sc13, q2, sc2 = make_expert_weights(wseed, le, device)
         w13[le].copy_(q13)
         s13[le].copy_(sc13)
         w2[le].copy_(q2)

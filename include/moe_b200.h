@@ -127,6 +127,20 @@ typedef struct moe_b200_workspace_layout {
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);
 
+/*
+ * Profiling hook. When `events` is non-null, later moe_b200_run calls made
+ * by the calling thread record events[i] (cudaEvent_t values created on the
+ * current device) on their stream at the stage boundaries:
+ *   0 start, 1 after the scratch clears, 2 after routing, 3 after the
+ *   permutation, 4 after GEMM1 (+SwiGLU), 5 after GEMM2, 6 after the final
+ *   bf16 conversion.
+ * num_events must be 7. Pass NULL to switch the hook off. No reference
+ * counterpart (the reference marks stages with NVTX ranges only,
+ * solution/cuda/kernel.cu:477,1249,...).
+ */
+#define MOE_B200_NUM_STAGE_EVENTS 7
+MOE_B200_API int moe_b200_set_stage_events(void* const* events, int num_events);
+
 /* ABI version of this header (bumped on any signature change). */
 MOE_B200_API int moe_b200_abi_version(void);
 

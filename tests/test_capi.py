@@ -1,0 +1,109 @@
+"""The C-ABI library: builds, loads without a GPU, exports every symbol the
+header declares, and rejects bad arguments before touching the device."""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import PKG, ROOT
+
+HEADER = os.path.join(ROOT, "include", "moe_b200.h")
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build as moe_build
+
+    moe_build.build()
+    import moe_host
+
+    return moe_host.load_library()
+
+
+def declared_functions() -> list[str]:
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"MOE_B200_API\s+[\w\s\*]+?\b(moe_b200_\w+)\s*\(", text)))
+
+
+def test_header_declares_the_entry_points():
+    names = declared_functions()
+    for n in ("moe_b200_run", "moe_b200_route", "moe_b200_workspace_bytes", "moe_b200_read_status",
+              "moe_b200_status_string", "moe_b200_get_workspace_layout", "moe_b200_set_stage_events",
+              "moe_b200_abi_version"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in moe_b200.h but not exported"
+
+
+def test_library_is_sm100a_only():
+    import build as moe_build
+
+    assert moe_build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
+    assert os.path.exists(os.path.join(PKG, "libmoe_b200.so"))
+
+
+def test_workspace_size_and_layout(lib):
+    import moe_host
+
+    assert moe_host.workspace_bytes(-1) == 0
+    assert moe_host.workspace_bytes(moe_host.MAX_TOKENS + 1) == 0
+    prev = 0
+    for T in (0, 1, 16, 64, 65, 4096, 16384):
+        n = moe_host.workspace_bytes(T)
+        assert n > 0 and n % 256 == 0
+        lay = moe_host.workspace_layout(T)
+        assert lay.total_bytes == n
+        assert lay.cap_rows == max(8 * T, 256)
+        offs = [lay.counts, lay.seg_off, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w, lay.c_hi,
+                lay.c_lo, lay.c_scale, lay.y_acc]
+        assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
+        assert lay.c_lo - lay.c_hi >= lay.cap_rows * 2048
+        assert (lay.g1_acc != 0) == (T <= 64)
+        if T > 65:  # plans without the decode scratch grow with T
+            assert n >= prev
+        prev = n
+
+
+def test_status_strings(lib):
+    import moe_host
+
+    assert moe_host.status_string(0) == "ok"
+    for code in range(1, 8):
+        assert moe_host.status_string(code) not in ("ok", "unknown status")
+    assert moe_host.status_string(99) == "unknown status"
+
+
+def test_run_rejects_bad_arguments_without_a_device(lib):
+    P = ctypes.c_void_p
+    good = ctypes.create_string_buffer(4096 + 256)
+    base = (ctypes.addressof(good) + 255) // 256 * 256
+    p = P(base)
+    args_null = [None, None, 0, None, None, None, None, None, None, 0, 2.5, 4, None, None, 0, None]
+    assert lib.moe_b200_run(*args_null) == 1                       # null pointers
+    full = [p, p, 0, p, p, p, p, p, p, 0, 2.5, 4, p, p, 1 << 40, None]
+    full[11] = -1
+    assert lib.moe_b200_run(*full) == 1                            # negative T
+    full[11] = 4
+    full[2] = 7
+    assert lib.moe_b200_run(*full) == 1                            # bad bias dtype code
+    full[2] = 0
+    full[3] = P(base + 1)
+    assert lib.moe_b200_run(*full) == 2                            # misaligned hidden_states
+    full[3] = p
+    full[13] = P(base + 16)
+    assert lib.moe_b200_run(*full) == 2                            # misaligned workspace
+    full[13] = p
+    full[14] = 16
+    assert lib.moe_b200_run(*full) == 3                            # workspace too small
+    full[11] = 0
+    assert lib.moe_b200_run(*full) == 0                            # T = 0 is a no-op
+    assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
+    assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
+    assert lib.moe_b200_set_stage_events(None, 0) == 0
+    assert lib.moe_b200_abi_version() == 1
