@@ -46,8 +46,13 @@ import workloads  # noqa: E402
 
 METRIC = "fused-MoE µs/call and TFLOPS vs FP8/HBM roofline, T=1..16384, 1/2/4/8 B200"
 UNIT = "us/call"
-HEADLINE_T = 64
 SEED = 1234
+# name -> (T, routing variant, description); "decode" is the default headline.
+WORKLOADS = {
+    "decode": (64, "uniform", "config1 decode: one MoE layer call, T=64"),
+    "prefill": (4096, "hot", "config2 prefill: one MoE layer call, T=4096, 4 hot local experts"),
+    "stress": (16384, "zipf", "config4 stress: one MoE layer call, T=16384, Zipf(1.2) expert popularity"),
+}
 
 # Algorithmic sizes (bytes, FLOPs) of the operator.
 W13_BYTES = 2 * 2048 * 7168 + 32 * 56 * 4          # per active expert, weights + scales
@@ -357,6 +362,8 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-extras", action="store_true", help="skip the sweep/prefill/stress points")
+    ap.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
+                    help="headline configuration (default: config 1 decode, T=64)")
     args = ap.parse_args()
     warmup = max(args.warmup, 3)
 
@@ -382,8 +389,9 @@ def main() -> None:
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
 
+    HEADLINE_T, variant, desc = WORKLOADS[args.workload]
     offset = (32 * rank) % 256
-    inp = workloads.make_inputs(HEADLINE_T, SEED, device, "uniform", offset, 2.5, weight_seed=SEED + 1 + rank)
+    inp = workloads.make_inputs(HEADLINE_T, SEED, device, variant, offset, 2.5, weight_seed=SEED + 1 + rank)
     st = routing_stats(inp)
 
     with ClockSampler(device) as clocks:
@@ -402,14 +410,20 @@ def main() -> None:
     stage = r["stage_ms"]
     kb, kf = kernel_bytes(st), kernel_flops(st)
     dominant = "gemm1" if stage["gemm1"] >= stage["gemm2"] else "gemm2"
-    rl = roofline_entry(stage[dominant], kb[dominant], kf[dominant], peaks, "hbm")
-    rl.update({"bound": "hbm", "kernel": dominant,
+    # a kernel is tensor-bound when its FLOPs at the dense e4m3 peak take
+    # longer than its bytes at the HBM peak
+    bound = ("tensor" if kf[dominant] / (2.0 * peaks["bf16_tflops"] * 1e12) > kb[dominant] / (peaks["hbm_gbs"] * 1e9)
+             else "hbm")
+    rl = roofline_entry(stage[dominant], kb[dominant], kf[dominant], peaks, bound)
+    rl.update({"bound": bound, "kernel": dominant,
                "traffic": NCU_TRAFFIC_BYTES.get((dominant, HEADLINE_T)),
                "algorithmic_bytes": kb[dominant], "kernel_us": round(stage[dominant] * 1e3, 2),
-               "peak_source": f"{peaks['source']} (MEASURED_PEAKS.json hbm_gbs)" if peaks["source"] == "measured"
-               else "fallback 6.65 TB/s"})
+               "algorithmic_flops": kf[dominant],
+               "peak_source": (("measured HBM copy, MEASURED_PEAKS.json hbm_gbs" if bound == "hbm" else
+                                "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops): dense e4m3")
+                               if peaks["source"] == "measured" else "fallback 6.65 TB/s / 1.59 PFLOP/s")})
 
-    launches_per_call = 6 if HEADLINE_T <= 64 else 5
+    launches_per_call = 6 if HEADLINE_T <= 64 else 5  # route, permute, gemm1, [swiglu], gemm2, finalize
     line = {
         "metric": METRIC,
         "value": round(mean_ms * 1e3, 2),
@@ -424,7 +438,7 @@ def main() -> None:
         "dtype": "fp8_e4m3 (fp32 accumulate)",
         "data": "synthetic, seeded (contest dataset unavailable); N(0,1) logits, N(0,0.1) bf16 bias, "
                 "e4m3 1x128 / 128x128 block-scaled N(0,1) activations and N(0,0.02) weights",
-        "config": {"workload": f"config1 decode: one MoE layer call, T={HEADLINE_T}, 32 local experts per GPU",
+        "config": {"workload": f"{desc}, 32 local experts per GPU",
                    "T": HEADLINE_T, "local_expert_offset": offset, "E_act": st["E_act"],
                    "sum_Tk": st["sum_Tk"], "parallelism": f"ep{world}" + (" + NCCL all-reduce" if world > 1 else ""),
                    "l2": "flushed (256 MB write) before every timed call"},
@@ -436,7 +450,7 @@ def main() -> None:
         "clocks": clocks.summary(),
     }
 
-    if world == 1 and not args.no_extras:
+    if world == 1 and not args.no_extras and args.workload == "decode":
         n_extra = max(5, args.steps // 2)
         line["sweep"] = [point(T, "uniform", n_extra, warmup, flush, peaks, device) for T in (1, 4, 16, 64)]
         line["prefill"] = point(4096, "hot", n_extra, warmup, flush, peaks, device)
@@ -460,7 +474,8 @@ def run_reference(args, world: int, rank: int, warmup: int) -> None:
 
     torch.set_num_threads(os.cpu_count() or 1)
     device = "cuda" if torch.cuda.is_available() else "cpu"
-    inp = workloads.make_inputs(HEADLINE_T, SEED, device, "uniform", 0, 2.5, weight_seed=SEED + 1)
+    HEADLINE_T, variant, desc = WORKLOADS[args.workload]
+    inp = workloads.make_inputs(HEADLINE_T, SEED, device, variant, 0, 2.5, weight_seed=SEED + 1)
     times = []
     base = None
     for i in range(warmup + args.steps):
@@ -474,8 +489,7 @@ def run_reference(args, world: int, rank: int, warmup: int) -> None:
         "metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(v / 1e3, 3), "higher_is_better": False, "scaling": "weak",
         "vs_baseline": None, "dtype": "fp32 (dequantised e4m3)", "data": "synthetic, seeded",
-        "config": {"workload": f"config1 decode: one MoE layer call, T={HEADLINE_T}, 32 local experts",
-                   "T": HEADLINE_T},
+        "config": {"workload": f"{desc}, 32 local experts", "T": HEADLINE_T},
         "impl": "reference",
         "cpu_baseline": base,
         "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},

@@ -12,11 +12,14 @@
 // the promotion of block k.
 //
 // Roles (one CTA per SM, persistent over a static tile list):
-//   warp 0        TMA producer: weight tiles (2-D TMA), token rows (TMA
-//                 gather4 for GEMM1, 2-D TMA for GEMM2), scales (cp.async)
+//   warp 0        TMA producer: weight tiles and permuted token rows (2-D
+//                 TMA), block scales (one bulk copy + cp.async per K block)
 //   warp 1        TMEM owner and single-thread MMA issuer
 //   warp 2        scale combiner: weight scale x activation scale per column
-//   warps 3..6    epilogue: TMEM -> registers, promotion, final epilogue
+//   warp 3        spare (keeps the epilogue warpgroup-aligned)
+//   warps 4..     epilogue: TMEM -> registers, promotion, final epilogue;
+//                 4 or 8 warps, each owning one TMEM lane quarter and a
+//                 group of token columns
 //
 // GEMM1 computes, for 128 intermediate rows i of block `blk`, both
 //   up[i]   = W13[e, blk*128 + i, :]        . A[tok, :]
@@ -39,7 +42,7 @@
 
 namespace moe {
 
-template <int kKind, int BN, int kStages>
+template <int kKind, int BN, int kStages, int kEpiWarps_>
 struct GemmTraits {
   static constexpr bool kIsG1 = kKind != kGemm2;
   static constexpr int kNumA = kIsG1 ? 2 : 1;     // weight tiles per stage (up+gate / W2)
@@ -57,10 +60,25 @@ struct GemmTraits {
   static constexpr int kScaleSlots = 8;
   // scale slot: raw[BN] | wscale[4] | combined[kNumA][BN]
   static constexpr int kSlotFloats = BN + 4 + kNumA * BN;
-  static constexpr int kEpiWarps = 4;
-  static constexpr int kThreads = (3 + kEpiWarps) * 32;
+  // Warps 0..3 are the role warpgroup (producer, MMA, scale combiner, one
+  // spare); warps 4.. are the epilogue. Epilogue warp w reads TMEM lane
+  // quarter w % 4 and the column group (w - 4) / 4.
+  static constexpr int kRoleWarps = 4;
+  static constexpr int kEpiWarps = kEpiWarps_;
+  static constexpr int kWarpsPerQuarter = kEpiWarps / 4;
+  static constexpr int kCPT = BN / kWarpsPerQuarter;   // token columns per epilogue thread
+  static constexpr int kThreads = (kRoleWarps + kEpiWarps) * 32;
   static constexpr int kColsPerLane = BN >= 32 ? BN / 32 : 1;
   static constexpr uint32_t kIdesc = idesc_e4m3_f32<128, BN>();
+  // Register split for the widest epilogue (GEMM1, BN = 128, 8 epilogue warps):
+  // the block launches with kLaunchRegs per thread; the role warpgroup gives
+  // registers back and the epilogue warpgroups take them.
+  static constexpr bool kSplitRegs = kIsG1 && kEpiWarps == 8 && BN == 128;
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kRoleRegs = 56;
+  static constexpr int kEpiRegs = 224;
+  static_assert(!kSplitRegs || kRoleRegs * 128 + kEpiRegs * 32 * kEpiWarps <= kLaunchRegs * kThreads,
+                "register split exceeds the block's launch registers");
 
   // shared memory layout (offsets from the 1024-aligned base)
   static constexpr int kOffStages = 0;
@@ -68,15 +86,17 @@ struct GemmTraits {
   static constexpr int kOffBars = kOffRing + kScaleSlots * kSlotFloats * 4;
   static constexpr int kNumBars = 2 * kStages + 4 + 3 * kScaleSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;
-  // misc: tmem base (4) | abort (4) | unit_pre[33] | seg[33] | epilogue scratch
+  // misc: tmem base (4) | abort (4) | unit_pre[33] | seg[33] | cnt[32] | epilogue scratch
   static constexpr int kOffUnitPre = kOffMisc + 16;
   static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
-  static constexpr int kOffEpi = kOffSeg + 34 * 4;
+  static constexpr int kOffCnt = kOffSeg + 34 * 4;
+  static constexpr int kOffEpi = kOffCnt + 32 * 4;
   // epilogue scratch: red[4][BN] | inv[BN] | tok[BN] | w[BN]
   static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
   static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;  // + alignment slack
 
   static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "BN");
+  static_assert(kEpiWarps % 4 == 0 && kCPT >= 16 && kCPT % 16 == 0, "epilogue column split");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -86,11 +106,11 @@ struct Tile {
 
 template <int BN, int kKBlocks>
 __device__ __forceinline__ void decode_tile(int u, const int* s_unit_pre, const int* s_seg,
-                                            int splits, Tile& t) {
+                                            const int* s_cnt, int splits, Tile& t) {
   int e = 0;
 #pragma unroll 1
   while (s_unit_pre[e + 1] <= u) ++e;
-  const int cnt = s_seg[e + 1] - s_seg[e];
+  const int cnt = s_cnt[e];
   const int nt = (cnt + BN - 1) / BN;
   int local = u - s_unit_pre[e];
   t.e = e;
@@ -149,12 +169,12 @@ __device__ __forceinline__ float silu_mul(float gate, float up) {
   return gate / (1.0f + expf(-gate)) * up;
 }
 
-template <int kKind, int BN, int kStages>
-__global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
+template <int kKind, int BN, int kStages, int kEpiWarps>
+__global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_b0,
                     const __grid_constant__ CUtensorMap tm_b1, const GemmParams p) {
-  using Tr = GemmTraits<kKind, BN, kStages>;
+  using Tr = GemmTraits<kKind, BN, kStages, kEpiWarps>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -171,6 +191,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + Tr::kOffMisc + 4);
   int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
   int* s_seg = reinterpret_cast<int*>(smem + Tr::kOffSeg);
+  int* s_cnt = reinterpret_cast<int*>(smem + Tr::kOffCnt);
   float* s_red = reinterpret_cast<float*>(smem + Tr::kOffEpi);   // [4][BN]
   float* s_inv = s_red + 4 * BN;                                 // [BN]
   int* s_ctok = reinterpret_cast<int*>(s_inv + BN);              // [BN]
@@ -194,7 +215,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
       mbar_init(smem_u32(&acce_bar[b]), Tr::kEpiWarps);
     }
     for (int s = 0; s < Tr::kScaleSlots; ++s) {
-      mbar_init(smem_u32(&sraw_bar[s]), 32);
+      mbar_init(smem_u32(&sraw_bar[s]), 2);
       mbar_init(smem_u32(&sfull_bar[s]), 1);
       mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
     }
@@ -209,8 +230,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
   if (warp == 2) {
     // per-expert tile counts -> prefix over experts of the work units
     const int lo = p.seg_off[lane];
-    const int hi = p.seg_off[lane + 1];
-    const int cnt = hi - lo;
+    const int cnt = p.counts[lane];
     const int units = ((cnt + BN - 1) / BN) * Tr::kRowBlocks * splits;
     int incl = units;
 #pragma unroll
@@ -220,7 +240,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
     }
     s_unit_pre[lane + 1] = incl;
     s_seg[lane] = lo;
-    if (lane == 31) s_seg[32] = hi;
+    s_cnt[lane] = cnt;
     if (lane == 0) s_unit_pre[0] = 0;
   }
   tc_fence_before();
@@ -231,6 +251,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
 
   if (warp == 0) {
     // ======================================================== TMA producer
+    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     int stage = 0;
     uint32_t ph = 0;
     int slot = 0;
@@ -238,20 +259,9 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
-      int gid[4] = {0, 0, 0, 0};
-      int ctok[Tr::kColsPerLane];
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       int arow0, arow1 = 0, wrow0, wrow1 = 0;
       if constexpr (Tr::kIsG1) {
-        if (lane < BN / 4) {
-#pragma unroll
-          for (int r = 0; r < 4; ++r) gid[r] = p.perm_tok[t.row0 + min(4 * lane + r, t.nvalid - 1)];
-        }
-#pragma unroll
-        for (int i = 0; i < Tr::kColsPerLane; ++i) {
-          const int c = lane + 32 * i;
-          ctok[i] = (c < BN) ? p.perm_tok[t.row0 + min(c, t.nvalid - 1)] : 0;
-        }
         arow0 = t.e * kGemm1Out + t.blk * kBlk;
         arow1 = arow0 + kInter;
         wrow0 = (t.e * kGemm1OutBlocks + t.blk) * kHiddenBlocks;
@@ -266,51 +276,38 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
           ok = false;
           break;
         }
-        uint8_t* st = smem + Tr::kOffStages + stage * Tr::kStageBytes;
-        const uint32_t fb = smem_u32(&full_bar[stage]);
-        const int kx = kb * kBlk;
         if (lane == 0) {
+          uint8_t* st = smem + Tr::kOffStages + stage * Tr::kStageBytes;
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          const int kx = kb * kBlk;
           mbar_arrive_expect_tx(fb, Tr::kStageBytes);
           tma_load_2d(smem_u32(st), &tm_w, fb, kx, arow0);
           if constexpr (Tr::kIsG1) {
             tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
+            tma_load_2d(smem_u32(st + 2 * Tr::kATileBytes), &tm_b0, fb, kx, t.row0);
           } else {
             tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_b0, fb, kx, t.row0);
             tma_load_2d(smem_u32(st + Tr::kATileBytes + Tr::kBTileBytes), &tm_b1, fb, kx, t.row0);
           }
-        }
-        if constexpr (Tr::kIsG1) {
-          if (lane < BN / 4) {
-            tma_gather4(smem_u32(st + 2 * Tr::kATileBytes + lane * 512), &tm_b0, fb, kx, gid[0],
-                        gid[1], gid[2], gid[3]);
-          }
-        }
-        // scales for this K block
-        float* sp = ring + slot * Tr::kSlotFloats;
-#pragma unroll
-        for (int i = 0; i < Tr::kColsPerLane; ++i) {
-          const int c = lane + 32 * i;
-          if (c < BN) {
-            const float* src;
-            if constexpr (Tr::kIsG1) {
-              src = p.act_scale + static_cast<int64_t>(kb) * p.num_tokens + ctok[i];
-            } else {
-              src = p.act_scale + static_cast<int64_t>(kb) * p.cap + min(t.row0 + c, p.cap - 1);
-            }
-            cp_async_4(smem_u32(sp + c), src);
-          }
-        }
-        if (lane == 0) {
+          // Scales of this K block: the BN activation scales are contiguous in
+          // the permuted row order (segment starts are 16-row aligned), the
+          // weight scale(s) are single floats.
+          float* sp = ring + slot * Tr::kSlotFloats;
+          const uint32_t sb = smem_u32(&sraw_bar[slot]);
+          mbar_arrive_expect_tx(sb, BN * 4);
+          bulk_load(smem_u32(sp), p.act_scale + static_cast<int64_t>(kb) * p.cap + t.row0, BN * 4, sb);
           cp_async_4(smem_u32(sp + BN), p.w_scale + wrow0 + kb);
           if constexpr (Tr::kIsG1) cp_async_4(smem_u32(sp + BN + 1), p.w_scale + wrow1 + kb);
+          cp_async_arrive_noinc(sb);
         }
-        cp_async_arrive_noinc(smem_u32(&sraw_bar[slot]));
+        __syncwarp();
         if (++stage == kStages) { stage = 0; ph ^= 1; }
         if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
       }
     }
   } else if (warp == 1) {
     // ========================================================== MMA issuer
+    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     int stage = 0;
     uint32_t ph = 0;
     int abuf = 0;
@@ -318,7 +315,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
             !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
@@ -353,12 +350,13 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
     }
   } else if (warp == 2) {
     // ======================================================= scale combiner
+    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     int slot = 0;
     uint32_t sph = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&sraw_bar[slot]), sph, s_abort, p.status, kStatusTimeoutScale)) {
           ok = false;
@@ -381,22 +379,30 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
         if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
       }
     }
+  } else if (warp < Tr::kRoleWarps) {
+    // spare warp of the role warpgroup
+    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
   } else {
     // ============================================================ epilogue
+    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Tr::kEpiRegs));
+    constexpr int CPT = Tr::kCPT;
+    const int ew = warp - Tr::kRoleWarps;
     const int q = warp & 3;                   // TMEM lane quarter of this warp
+    const int col0 = (ew >> 2) * CPT;         // first token column of this warp
     const int row_in_tile = q * 32 + lane;    // weight row inside the 128-row block
-    const int et = (warp - 3) * 32 + lane;    // 0..127 inside the epilogue group
+    const int et = ew * 32 + lane;            // 0.. inside the epilogue group
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    constexpr uint32_t kEpiThreads = 32 * Tr::kEpiWarps;
     int slot = 0;
     uint32_t sph = 0;
     int abuf = 0;
     uint32_t aph = 0;
     bool ok = true;
-    float acc0[BN];
-    float acc1[Tr::kIsG1 ? BN : 1];
+    float acc0[CPT];
+    float acc1[Tr::kIsG1 ? CPT : 1];
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       // per-column data for the final epilogue, loaded early
       int my_tok = 0;
       float my_w = 0.f;
@@ -407,10 +413,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
         }
       }
 #pragma unroll
-      for (int c = 0; c < BN; ++c) acc0[c] = 0.f;
+      for (int c = 0; c < CPT; ++c) acc0[c] = 0.f;
       if constexpr (Tr::kIsG1) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) acc1[c] = 0.f;
+        for (int c = 0; c < CPT; ++c) acc1[c] = 0.f;
       }
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue) ||
@@ -419,42 +425,26 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
           break;
         }
         tc_fence_after();
-        const float* comb0 = ring + slot * Tr::kSlotFloats + BN + 4;
-        const uint32_t taddr = lane_base + abuf * Tr::kAccCols;
-        if constexpr (BN == 16) {
-          uint32_t v[16];
-          tmem_ld16(taddr, v);
-          uint32_t g[16];
-          if constexpr (Tr::kIsG1) tmem_ld16(taddr + BN, g);
-          tmem_wait_ld();
+        const float* comb0 = ring + slot * Tr::kSlotFloats + BN + 4 + col0;
+        const uint32_t taddr = lane_base + abuf * Tr::kAccCols + col0;
 #pragma unroll
-          for (int c = 0; c < 16; ++c) acc0[c] = fmaf(__uint_as_float(v[c]), comb0[c], acc0[c]);
+        for (int ch = 0; ch < CPT / 16; ++ch) {
+          uint32_t v[16];
+          tmem_ld16(taddr + ch * 16, v);
           if constexpr (Tr::kIsG1) {
+            uint32_t g[16];
+            tmem_ld16(taddr + BN + ch * 16, g);
+            tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+              acc0[ch * 16 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 16 + c], acc0[ch * 16 + c]);
+              acc1[ch * 16 + c] = fmaf(__uint_as_float(g[c]), comb0[BN + ch * 16 + c], acc1[ch * 16 + c]);
+            }
+          } else {
+            tmem_wait_ld();
 #pragma unroll
             for (int c = 0; c < 16; ++c)
-              acc1[c] = fmaf(__uint_as_float(g[c]), comb0[BN + c], acc1[c]);
-          }
-        } else {
-#pragma unroll
-          for (int ch = 0; ch < BN / 32; ++ch) {
-            uint32_t v[32];
-            tmem_ld32(taddr + ch * 32, v);
-            if constexpr (Tr::kIsG1) {
-              uint32_t g[32];
-              tmem_ld32(taddr + BN + ch * 32, g);
-              tmem_wait_ld();
-#pragma unroll
-              for (int c = 0; c < 32; ++c) {
-                acc0[ch * 32 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 32 + c], acc0[ch * 32 + c]);
-                acc1[ch * 32 + c] =
-                    fmaf(__uint_as_float(g[c]), comb0[BN + ch * 32 + c], acc1[ch * 32 + c]);
-              }
-            } else {
-              tmem_wait_ld();
-#pragma unroll
-              for (int c = 0; c < 32; ++c)
-                acc0[ch * 32 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 32 + c], acc0[ch * 32 + c]);
-            }
+              acc0[ch * 16 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 16 + c], acc0[ch * 16 + c]);
           }
         }
         tc_fence_before();
@@ -472,32 +462,32 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
       if constexpr (kKind == kGemm1Fused) {
         // h = silu(gate) * up, kept in acc0
 #pragma unroll
-        for (int c = 0; c < BN; ++c) acc0[c] = silu_mul(acc1[c], acc0[c]);
-        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        for (int c = 0; c < CPT; ++c) acc0[c] = silu_mul(acc1[c], acc0[c]);
+        named_bar_sync(1, kEpiThreads);
 #pragma unroll
-        for (int g = 0; g < (BN + 31) / 32; ++g) {
+        for (int g = 0; g < (CPT + 31) / 32; ++g) {
           float v[32];
 #pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = (g * 32 + c < BN) ? fabsf(acc0[min(g * 32 + c, BN - 1)]) : 0.f;
+          for (int c = 0; c < 32; ++c) v[c] = (g * 32 + c < CPT) ? fabsf(acc0[min(g * 32 + c, CPT - 1)]) : 0.f;
           const float m = warp_colmax32(v, lane);
-          if (g * 32 + lane < BN) s_red[q * BN + g * 32 + lane] = m;
+          if (g * 32 + lane < CPT) s_red[q * BN + col0 + g * 32 + lane] = m;
         }
-        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        named_bar_sync(1, kEpiThreads);
         if (et < BN) {
           const float amax = fmaxf(fmaxf(s_red[et], s_red[BN + et]), fmaxf(s_red[2 * BN + et], s_red[3 * BN + et]));
           s_inv[et] = amax > 0.f ? 448.0f / amax : 0.f;
           if (et < t.nvalid) p.c_scale[static_cast<int64_t>(t.blk) * p.cap + t.row0 + et] = amax * (1.0f / 448.0f);
         }
-        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        named_bar_sync(1, kEpiThreads);
         const int col = t.blk * kBlk + row_in_tile;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          if (c < t.nvalid) {
-            const float x = acc0[c] * s_inv[c];
+        for (int c = 0; c < CPT; ++c) {
+          if (col0 + c < t.nvalid) {
+            const float x = acc0[c] * s_inv[col0 + c];
             const __nv_fp8_e4m3 qh(x);
             const float r = x - static_cast<float>(qh);
             const __nv_fp8_e4m3 ql(r);
-            const int64_t off = static_cast<int64_t>(t.row0 + c) * kInter + col;
+            const int64_t off = static_cast<int64_t>(t.row0 + col0 + c) * kInter + col;
             p.c_hi[off] = qh.__x;
             p.c_lo[off] = ql.__x;
           }
@@ -505,25 +495,26 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
       } else if constexpr (kKind == kGemm1Split) {
         const int col = t.blk * kBlk + row_in_tile;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          if (c < t.nvalid) {
-            float* dst = p.g1_acc + static_cast<int64_t>(t.row0 + c) * kGemm1Out + col;
+        for (int c = 0; c < CPT; ++c) {
+          if (col0 + c < t.nvalid) {
+            float* dst = p.g1_acc + static_cast<int64_t>(t.row0 + col0 + c) * kGemm1Out + col;
             red_add_f32(dst, acc0[c]);
             red_add_f32(dst + kInter, acc1[c]);
           }
         }
       } else {
-        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        named_bar_sync(1, kEpiThreads);
         if (et < BN) {
           s_ctok[et] = my_tok;
           s_cw[et] = my_w;
         }
-        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        named_bar_sync(1, kEpiThreads);
         const int col = t.blk * kBlk + row_in_tile;
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          if (c < t.nvalid) {
-            red_add_f32(p.y_acc + static_cast<int64_t>(s_ctok[c]) * kHidden + col, acc0[c] * s_cw[c]);
+        for (int c = 0; c < CPT; ++c) {
+          if (col0 + c < t.nvalid) {
+            red_add_f32(p.y_acc + static_cast<int64_t>(s_ctok[col0 + c]) * kHidden + col,
+                        acc0[c] * s_cw[col0 + c]);
           }
         }
       }
@@ -546,47 +537,56 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------- launchers
-template <int kKind, int BN, int kStages>
+template <int kKind, int BN, int kStages, int kEpiWarps>
 static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const CUtensorMap& b1,
                               const GemmParams& p, int grid, cudaStream_t stream) {
-  using Tr = GemmTraits<kKind, BN, kStages>;
-  auto kern = moe_gemm_kernel<kKind, BN, kStages>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+  using Tr = GemmTraits<kKind, BN, kStages, kEpiWarps>;
+  auto kern = moe_gemm_kernel<kKind, BN, kStages, kEpiWarps>;
+  static int checked_device = -1;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
   if (err != cudaSuccess) return err;
+  if (checked_device != dev) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    if constexpr (Tr::kSplitRegs) {
+      // The warpgroup register split is only safe if the block launches with
+      // exactly the registers it was sized for.
+      cudaFuncAttributes attr;
+      err = cudaFuncGetAttributes(&attr, kern);
+      if (err != cudaSuccess) return err;
+      if (attr.numRegs != Tr::kLaunchRegs) return cudaErrorInvalidConfiguration;
+    }
+    checked_device = dev;
+  }
   kern<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(w, b0, b1, p);
   return cudaGetLastError();
 }
 
+#define MOE_GEMM_CONFIGS(X)            \
+  X(kGemm1Fused, 128, 4, 8)            \
+  X(kGemm1Fused, 64, 5, 4)             \
+  X(kGemm1Split, 16, 6, 4)             \
+  X(kGemm2, 128, 4, 8)                 \
+  X(kGemm2, 64, 6, 4)                  \
+  X(kGemm2, 16, 10, 4)
+
 cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtensorMap& b0,
                             const CUtensorMap& b1, const GemmParams& p, int grid,
                             cudaStream_t stream) {
-  switch (kind) {
-    case kGemm1Fused:
-      if (bn == 64) return launch_one<kGemm1Fused, 64, 5>(w, b0, b1, p, grid, stream);
-      if (bn == 32) return launch_one<kGemm1Fused, 32, 6>(w, b0, b1, p, grid, stream);
-      break;
-    case kGemm1Split:
-      if (bn == 16) return launch_one<kGemm1Split, 16, 6>(w, b0, b1, p, grid, stream);
-      if (bn == 32) return launch_one<kGemm1Split, 32, 6>(w, b0, b1, p, grid, stream);
-      break;
-    case kGemm2:
-      if (bn == 128) return launch_one<kGemm2, 128, 4>(w, b0, b1, p, grid, stream);
-      if (bn == 64) return launch_one<kGemm2, 64, 6>(w, b0, b1, p, grid, stream);
-      if (bn == 16) return launch_one<kGemm2, 16, 10>(w, b0, b1, p, grid, stream);
-      break;
-    default:
-      break;
-  }
+#define MOE_GEMM_DISPATCH(K, BN_, S, E) \
+  if (kind == K && bn == BN_) return launch_one<K, BN_, S, E>(w, b0, b1, p, grid, stream);
+  MOE_GEMM_CONFIGS(MOE_GEMM_DISPATCH)
+#undef MOE_GEMM_DISPATCH
   return cudaErrorInvalidValue;
 }
 
 bool gemm_config_supported(int kind, int bn) {
-  switch (kind) {
-    case kGemm1Fused: return bn == 64 || bn == 32;
-    case kGemm1Split: return bn == 16 || bn == 32;
-    case kGemm2: return bn == 128 || bn == 64 || bn == 16;
-    default: return false;
-  }
+#define MOE_GEMM_SUPPORTED(K, BN_, S, E) \
+  if (kind == K && bn == BN_) return true;
+  MOE_GEMM_CONFIGS(MOE_GEMM_SUPPORTED)
+#undef MOE_GEMM_SUPPORTED
+  return false;
 }
 
 }  // namespace moe

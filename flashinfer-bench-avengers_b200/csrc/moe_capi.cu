@@ -49,7 +49,7 @@ Plan choose_plan(int64_t T) {
     p.g2_splits = T <= 16 ? 2 : 1;
   } else {
     p.split_g1 = false;
-    p.g1_bn = 64;
+    p.g1_bn = T >= 1024 ? 128 : 64;
     p.g1_splits = 1;
     p.g2_bn = T >= 1024 ? 128 : 64;
     p.g2_splits = 1;
@@ -65,9 +65,11 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   moe_b200_workspace_layout l;
   std::memset(&l, 0, sizeof(l));
   const Plan plan = choose_plan(T);
-  // Permuted-row capacity: every (token, local expert) pair, at least 256
-  // rows so a TMA box never exceeds the tensor extent.
-  const size_t cap = std::max<size_t>(static_cast<size_t>(T) * kTopK, 256);
+  // Permuted-row capacity: every (token, local expert) pair, the padding of
+  // 32 segments to kSegAlign rows, and one 128-row tile of slack so tile
+  // reads that run past the last segment stay inside the buffers.
+  const size_t cap = (static_cast<size_t>(T) * kTopK + kSegAlign - 1) / kSegAlign * kSegAlign +
+                     kExpertsLocal * kSegAlign + 128;
   size_t off = 0;
   l.counts = off;
   l.status = off + kExpertsLocal * sizeof(int);
@@ -82,6 +84,10 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   off = align_up(off + cap * sizeof(int32_t));
   l.perm_w = off;
   off = align_up(off + cap * sizeof(float));
+  l.a_perm = off;
+  off = align_up(off + cap * kHidden);
+  l.sa_perm = off;
+  off = align_up(off + cap * kHiddenBlocks * sizeof(float));
   l.c_hi = off;
   off = align_up(off + cap * kInter);
   l.c_lo = off;
@@ -197,10 +203,16 @@ int launch_route(const float* logits, const void* bias, int bias_dtype, int T, f
 thread_local cudaEvent_t t_stage_events[MOE_B200_NUM_STAGE_EVENTS];
 thread_local bool t_stage_events_on = false;
 
-// External event records, so the marks also fire when the call is replayed
-// from a captured CUDA graph.
+// While the stream is being captured the marks are external event records,
+// so they also fire when the captured CUDA graph is replayed.
 void mark_stage(int i, cudaStream_t s) {
-  if (t_stage_events_on) cudaEventRecordWithFlags(t_stage_events[i], s, cudaEventRecordExternal);
+  if (!t_stage_events_on) return;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return;
+  if (cs == cudaStreamCaptureStatusActive)
+    cudaEventRecordWithFlags(t_stage_events[i], s, cudaEventRecordExternal);
+  else
+    cudaEventRecord(t_stage_events[i], s);
 }
 
 }  // namespace
@@ -210,7 +222,7 @@ using namespace moe;
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 1; }
+int moe_b200_abi_version(void) { return 2; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
@@ -326,6 +338,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   float* topk_w = reinterpret_cast<float*>(ws + l.topk_w);
   int32_t* perm_tok = reinterpret_cast<int32_t*>(ws + l.perm_tok);
   float* perm_w = reinterpret_cast<float*>(ws + l.perm_w);
+  uint8_t* a_perm = ws + l.a_perm;
+  float* sa_perm = reinterpret_cast<float*>(ws + l.sa_perm);
   uint8_t* c_hi = ws + l.c_hi;
   uint8_t* c_lo = ws + l.c_lo;
   float* c_scale = reinterpret_cast<float*>(ws + l.c_scale);
@@ -333,8 +347,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   float* g1_acc = plan.split_g1 ? reinterpret_cast<float*>(ws + l.g1_acc) : nullptr;
 
   // ---- tensor maps ---------------------------------------------------------
-  CUtensorMap tm_hidden, tm_w13, tm_w2, tm_chi, tm_clo;
-  if (!encode_u8_2d(&tm_hidden, hidden_states, kHidden, num_tokens, 128, 1) ||
+  CUtensorMap tm_aperm, tm_w13, tm_w2, tm_chi, tm_clo;
+  if (!encode_u8_2d(&tm_aperm, a_perm, kHidden, cap, 128, plan.g1_bn) ||
       !encode_u8_2d(&tm_w13, gemm1_weights, kHidden, static_cast<uint64_t>(kExpertsLocal) * kGemm1Out,
                     128, 128) ||
       !encode_u8_2d(&tm_w2, gemm2_weights, kInter, static_cast<uint64_t>(kExpertsLocal) * kHidden, 128,
@@ -365,14 +379,28 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.perm_w = perm_w;
   permute_kernel<<<1, 1024, 0, s>>>(pp);
   if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  GatherParams gp;
+  gp.seg_off = seg_off;
+  gp.perm_tok = perm_tok;
+  gp.hidden = static_cast<const uint8_t*>(hidden_states);
+  gp.hidden_scale = hidden_states_scale;
+  gp.num_tokens = T;
+  gp.cap = cap;
+  gp.a_perm = a_perm;
+  gp.sa_perm = sa_perm;
+  int ggrid = static_cast<int>(div_up(cap, 8));
+  if (ggrid > di.sm_count * 4) ggrid = di.sm_count * 4;
+  gather_rows_kernel<<<ggrid, 256, 0, s>>>(gp);
+  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
   mark_stage(3, s);
 
   GemmParams g1;
   std::memset(&g1, 0, sizeof(g1));
   g1.seg_off = seg_off;
+  g1.counts = counts;
   g1.perm_tok = perm_tok;
   g1.perm_w = perm_w;
-  g1.act_scale = hidden_states_scale;
+  g1.act_scale = sa_perm;
   g1.w_scale = gemm1_weights_scale;
   g1.num_tokens = T;
   g1.cap = cap;
@@ -386,12 +414,12 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   if (plan.split_g1) {
     if (cudaMemsetAsync(g1_acc, 0, static_cast<size_t>(cap) * kGemm1Out * sizeof(float), s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
-    if (launch_moe_gemm(kGemm1Split, plan.g1_bn, tm_w13, tm_hidden, tm_hidden, g1, grid1, s) != cudaSuccess)
+    if (launch_moe_gemm(kGemm1Split, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
     swiglu_quant_kernel<<<di.sm_count * 2, 256, 0, s>>>(seg_off, g1_acc, c_hi, c_lo, c_scale, cap);
     if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
-    if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_hidden, tm_hidden, g1, grid1, s) != cudaSuccess)
+    if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
   }
 

@@ -21,12 +21,23 @@ struct RouteParams {
 struct PermuteParams {
   const int32_t* topk_idx;  // [T, 8]
   const float* topk_w;      // [T, 8]
-  const int* counts;        // [32]
+  const int* counts;        // [32] assignments per local expert
   int num_tokens;
   int local_expert_offset;
-  int* seg_off;             // [33] segment starts in the permuted row order
-  int32_t* perm_tok;        // [8T] token of each permuted row
-  float* perm_w;            // [8T] routing weight of each permuted row
+  int* seg_off;             // [33] segment starts (multiples of kSegAlign)
+  int32_t* perm_tok;        // [cap] token of each permuted row, -1 for padding
+  float* perm_w;            // [cap] routing weight of each permuted row
+};
+
+struct GatherParams {
+  const int* seg_off;       // [33]
+  const int32_t* perm_tok;  // [cap]
+  const uint8_t* hidden;    // [T, 7168] e4m3
+  const float* hidden_scale;  // [56, T]
+  int num_tokens;
+  int cap;
+  uint8_t* a_perm;          // [cap, 7168] e4m3
+  float* sa_perm;           // [56, cap]
 };
 
 // The three grouped-GEMM flavours built from one kernel template.
@@ -37,10 +48,11 @@ enum GemmKind : int {
 };
 
 struct GemmParams {
-  const int* seg_off;       // [33]
+  const int* seg_off;       // [33] padded segment starts
+  const int* counts;        // [32] valid rows per segment
   const int32_t* perm_tok;  // [cap]
   const float* perm_w;      // [cap]
-  const float* act_scale;   // GEMM1: hidden_states_scale [56, T]; GEMM2: c_scale [16, cap]
+  const float* act_scale;   // GEMM1: sa_perm [56, cap]; GEMM2: c_scale [16, cap]
   const float* w_scale;     // GEMM1: [32, 32, 56]; GEMM2: [32, 56, 16]
   int num_tokens;           // T
   int cap;                  // row capacity of the permuted buffers (8T)
@@ -55,6 +67,7 @@ struct GemmParams {
 
 __global__ void route_kernel(RouteParams p);
 __global__ void permute_kernel(PermuteParams p);
+__global__ void gather_rows_kernel(GatherParams p);
 __global__ void swiglu_quant_kernel(const int* seg_off, const float* g1_acc, uint8_t* c_hi,
                                     uint8_t* c_lo, float* c_scale, int cap);
 __global__ void finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4);

@@ -18,5 +18,8 @@ constexpr int kTopK = 8;
 constexpr int kGroups = 8;
 constexpr int kGroupSize = 32;
 constexpr int kTopKGroups = 4;
+// Expert segments of the permuted row space start on multiples of this many
+// rows, so every GEMM tile starts 16-byte aligned in the fp32 scale arrays.
+constexpr int kSegAlign = 16;
 
 }  // namespace moe

@@ -147,9 +147,9 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
 // One CTA of 1024 threads. Tokens are processed in chunks of 1024 (one per
 // thread); inside a chunk a warp ranks its 32 tokens per expert with ballots,
 // warps are ranked with a shuffle scan, so each expert segment lists its
-// tokens in increasing token order.
+// tokens in increasing token order. Segments start on multiples of
+// kSegAlign rows; the padding rows carry token -1 and weight 0.
 __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
-  __shared__ int s_off[kExpertsLocal + 1];
   __shared__ int s_run[kExpertsLocal];
   __shared__ int s_wcnt[32][kExpertsLocal];  // [warp][expert]
   __shared__ int s_wpre[32][kExpertsLocal];
@@ -160,19 +160,29 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
 
   if (warp == 0) {
     const int c = p.counts[lane];
-    int incl = c;
+    const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+    int incl = padded;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, off);
       if (lane >= off) incl += o;
     }
-    s_off[lane + 1] = incl;
-    s_run[lane] = incl - c;
-    if (lane == 0) s_off[0] = 0;
+    s_run[lane] = incl - padded;
     p.seg_off[lane + 1] = incl;
     if (lane == 0) p.seg_off[0] = 0;
   }
   __syncthreads();
+  // padding rows: expert e = tid / kSegAlign, slot j = tid % kSegAlign
+  if (tid < kExpertsLocal * kSegAlign) {
+    const int e = tid / kSegAlign;
+    const int j = tid % kSegAlign;
+    const int c = p.counts[e];
+    const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+    if (c + j < padded) {
+      p.perm_tok[s_run[e] + c + j] = -1;
+      p.perm_w[s_run[e] + c + j] = 0.f;
+    }
+  }
 
   const uint32_t lt_mask = (1u << lane) - 1u;
   for (int base = 0; base < p.num_tokens; base += 1024) {
@@ -248,6 +258,32 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
       p.perm_w[pos] = w;
     }
     __syncthreads();
+  }
+}
+
+// Copies every permuted row's activations and block scales into contiguous
+// buffers (one warp per row): a_perm[r, :] = hidden[tok(r), :] and
+// sa_perm[kb, r] = hidden_scale[kb, tok(r)]; padding rows become zeros.
+// This replaces per-row TMA gathers inside GEMM1 with plain 2-D tiles.
+__global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
+  const int rows = p.seg_off[kExpertsLocal];
+  const int lane = threadIdx.x & 31;
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps_total) {
+    const int tok = p.perm_tok[r];
+    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(r) * kHidden);
+    if (tok >= 0) {
+      const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(tok) * kHidden);
+#pragma unroll
+      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = src[lane + 32 * i];
+      for (int kb = lane; kb < kHiddenBlocks; kb += 32)
+        p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = p.hidden_scale[static_cast<int64_t>(kb) * p.num_tokens + tok];
+    } else {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = z;
+      for (int kb = lane; kb < kHiddenBlocks; kb += 32) p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = 0.f;
+    }
   }
 }
 

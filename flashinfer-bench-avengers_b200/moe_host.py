@@ -50,6 +50,8 @@ class WorkspaceLayout(ctypes.Structure):
         ("topk_w", ctypes.c_size_t),
         ("perm_tok", ctypes.c_size_t),
         ("perm_w", ctypes.c_size_t),
+        ("a_perm", ctypes.c_size_t),
+        ("sa_perm", ctypes.c_size_t),
         ("c_hi", ctypes.c_size_t),
         ("c_lo", ctypes.c_size_t),
         ("c_scale", ctypes.c_size_t),

@@ -112,17 +112,19 @@ typedef struct moe_b200_workspace_layout {
   size_t total_bytes;
   size_t counts;      /* int32[32] local-expert histogram */
   size_t status;      /* uint32 status word */
-  size_t seg_off;     /* int32[33] expert segment starts */
+  size_t seg_off;     /* int32[33] expert segment starts (multiples of 16 rows) */
   size_t topk_idx;    /* int32[T, 8] */
   size_t topk_w;      /* fp32[T, 8] */
-  size_t perm_tok;    /* int32[cap_rows] token of each permuted row */
+  size_t perm_tok;    /* int32[cap_rows] token of each permuted row, -1 for padding */
   size_t perm_w;      /* fp32[cap_rows] routing weight of each permuted row */
+  size_t a_perm;      /* e4m3[cap_rows, 7168] token rows in permuted order */
+  size_t sa_perm;     /* fp32[56, cap_rows] their block scales */
   size_t c_hi;        /* e4m3[cap_rows, 2048] */
   size_t c_lo;        /* e4m3[cap_rows, 2048] */
   size_t c_scale;     /* fp32[16, cap_rows] */
   size_t y_acc;       /* fp32[T, 7168] */
   size_t g1_acc;      /* fp32[cap_rows, 4096], 0 when the plan for T does not split K */
-  int64_t cap_rows;   /* max(8T, 256) */
+  int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
 } moe_b200_workspace_layout;
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);
