@@ -30,7 +30,9 @@
 // bits, so GEMM2 sees C at close to bf16 precision while staying on the
 // e4m3 tensor-core path.
 // GEMM2 computes O[h] = W2[e, h, :] . C[row, :] (hi and lo accumulate into
-// one TMEM accumulator) and red.adds w * O into the fp32 output rows.
+// one TMEM accumulator) and red.adds w * O into the fp32 output rows; its
+// wide form covers two 128-row W2 blocks per tile (M = 256), which cuts the
+// token-tile traffic per FLOP by a third.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cstdint>
@@ -44,14 +46,16 @@ namespace moe {
 
 template <int kKind, int BN, int kStages, int kEpiWarps_>
 struct GemmTraits {
-  static constexpr bool kIsG1 = kKind != kGemm2;
-  static constexpr int kNumA = kIsG1 ? 2 : 1;     // weight tiles per stage (up+gate / W2)
-  static constexpr int kNumB = kIsG1 ? 1 : 2;     // token tiles per stage (A rows / hi+lo)
+  static constexpr bool kIsG1 = kKind == kGemm1Fused || kKind == kGemm1Split;
+  // weight tiles per stage: GEMM1 up + gate, GEMM2 one or two W2 row blocks
+  static constexpr int kNumA = (kKind == kGemm2) ? 1 : 2;
+  // token tiles per stage: GEMM1 activation rows, GEMM2 the hi and lo parts of C
+  static constexpr int kNumB = kIsG1 ? 1 : 2;
   static constexpr int kATileBytes = 128 * 128;
   static constexpr int kBTileBytes = BN * 128;
   static constexpr int kStageBytes = kNumA * kATileBytes + kNumB * kBTileBytes;
   static constexpr int kKBlocks = kIsG1 ? kHiddenBlocks : kInterBlocks;
-  static constexpr int kRowBlocks = kIsG1 ? kInterBlocks : kHiddenBlocks;
+  static constexpr int kRowBlocks = kIsG1 ? kInterBlocks : kHiddenBlocks / kNumA;
   static constexpr int kAccCols = kNumA * BN;     // fp32 TMEM columns per accumulator buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32
                                    : (2 * kAccCols <= 64) ? 64
@@ -73,7 +77,7 @@ struct GemmTraits {
   // Register split for the widest epilogue (GEMM1, BN = 128, 8 epilogue warps):
   // the block launches with kLaunchRegs per thread; the role warpgroup gives
   // registers back and the epilogue warpgroups take them.
-  static constexpr bool kSplitRegs = kIsG1 && kEpiWarps == 8 && BN == 128;
+  static constexpr bool kSplitRegs = kNumA == 2 && kEpiWarps == 8 && BN == 128;
   static constexpr int kLaunchRegs = 168;
   static constexpr int kRoleRegs = 56;
   static constexpr int kEpiRegs = 224;
@@ -267,8 +271,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         wrow0 = (t.e * kGemm1OutBlocks + t.blk) * kHiddenBlocks;
         wrow1 = (t.e * kGemm1OutBlocks + kInterBlocks + t.blk) * kHiddenBlocks;
       } else {
-        arow0 = t.e * kHidden + t.blk * kBlk;
-        wrow0 = (t.e * kHiddenBlocks + t.blk) * kInterBlocks;
+        arow0 = t.e * kHidden + t.blk * Tr::kNumA * kBlk;
+        arow1 = arow0 + kBlk;
+        wrow0 = (t.e * kHiddenBlocks + t.blk * Tr::kNumA) * kInterBlocks;
+        wrow1 = wrow0 + kInterBlocks;
       }
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer) ||
@@ -282,13 +288,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
           const int kx = kb * kBlk;
           mbar_arrive_expect_tx(fb, Tr::kStageBytes);
           tma_load_2d(smem_u32(st), &tm_w, fb, kx, arow0);
-          if constexpr (Tr::kIsG1) {
-            tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
-            tma_load_2d(smem_u32(st + 2 * Tr::kATileBytes), &tm_b0, fb, kx, t.row0);
-          } else {
-            tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_b0, fb, kx, t.row0);
-            tma_load_2d(smem_u32(st + Tr::kATileBytes + Tr::kBTileBytes), &tm_b1, fb, kx, t.row0);
-          }
+          if constexpr (Tr::kNumA == 2) tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
+          uint8_t* bt = st + Tr::kNumA * Tr::kATileBytes;
+          tma_load_2d(smem_u32(bt), &tm_b0, fb, kx, t.row0);
+          if constexpr (Tr::kNumB == 2) tma_load_2d(smem_u32(bt + Tr::kBTileBytes), &tm_b1, fb, kx, t.row0);
           // Scales of this K block: the BN activation scales are contiguous in
           // the permuted row order (segment starts are 16-row aligned), the
           // weight scale(s) are single floats.
@@ -297,7 +300,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
           mbar_arrive_expect_tx(sb, BN * 4);
           bulk_load(smem_u32(sp), p.act_scale + static_cast<int64_t>(kb) * p.cap + t.row0, BN * 4, sb);
           cp_async_4(smem_u32(sp + BN), p.w_scale + wrow0 + kb);
-          if constexpr (Tr::kIsG1) cp_async_4(smem_u32(sp + BN + 1), p.w_scale + wrow1 + kb);
+          if constexpr (Tr::kNumA == 2) cp_async_4(smem_u32(sp + BN + 1), p.w_scale + wrow1 + kb);
           cp_async_arrive_noinc(sb);
         }
         __syncwarp();
@@ -326,18 +329,19 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         if (lane == 0) {
           const uint32_t st = smem_u32(smem + Tr::kOffStages + stage * Tr::kStageBytes);
           const uint32_t d = tmem_base + abuf * Tr::kAccCols;
+          // accumulator a (columns a*BN..) = sum over the token tiles b of
+          // A_a . B_b (GEMM2: hi + lo), fresh at k = 0 of every K block
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            if constexpr (Tr::kIsG1) {
-              const uint64_t bdesc = sw128_kmajor_desc(st + 2 * Tr::kATileBytes + 32 * k);
-              umma_f8(d, sw128_kmajor_desc(st + 32 * k), bdesc, Tr::kIdesc, k > 0);
-              umma_f8(d + BN, sw128_kmajor_desc(st + Tr::kATileBytes + 32 * k), bdesc, Tr::kIdesc,
-                      k > 0);
-            } else {
-              const uint64_t adesc = sw128_kmajor_desc(st + 32 * k);
-              umma_f8(d, adesc, sw128_kmajor_desc(st + Tr::kATileBytes + 32 * k), Tr::kIdesc, k > 0);
-              umma_f8(d, adesc, sw128_kmajor_desc(st + Tr::kATileBytes + Tr::kBTileBytes + 32 * k),
-                      Tr::kIdesc, 1);
+#pragma unroll
+            for (int a = 0; a < Tr::kNumA; ++a) {
+              const uint64_t adesc = sw128_kmajor_desc(st + a * Tr::kATileBytes + 32 * k);
+#pragma unroll
+              for (int b = 0; b < Tr::kNumB; ++b) {
+                const uint64_t bdesc =
+                    sw128_kmajor_desc(st + Tr::kNumA * Tr::kATileBytes + b * Tr::kBTileBytes + 32 * k);
+                umma_f8(d + a * BN, adesc, bdesc, Tr::kIdesc, (k > 0 || b > 0) ? 1u : 0u);
+              }
             }
           }
           umma_commit(smem_u32(&empty_bar[stage]));
@@ -364,14 +368,14 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         }
         float* sp = ring + slot * Tr::kSlotFloats;
         const float w0 = sp[BN];
-        const float w1 = Tr::kIsG1 ? sp[BN + 1] : 0.f;
+        const float w1 = Tr::kNumA == 2 ? sp[BN + 1] : 0.f;
 #pragma unroll
         for (int i = 0; i < Tr::kColsPerLane; ++i) {
           const int c = lane + 32 * i;
           if (c < BN) {
             const float a = sp[c];
             sp[BN + 4 + c] = a * w0;
-            if constexpr (Tr::kIsG1) sp[BN + 4 + BN + c] = a * w1;
+            if constexpr (Tr::kNumA == 2) sp[BN + 4 + BN + c] = a * w1;
           }
         }
         __syncwarp();
@@ -399,14 +403,14 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     uint32_t aph = 0;
     bool ok = true;
     float acc0[CPT];
-    float acc1[Tr::kIsG1 ? CPT : 1];
+    float acc1[CPT];  // second accumulator (gate / second W2 block); unused when kNumA == 1
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       // per-column data for the final epilogue, loaded early
       int my_tok = 0;
       float my_w = 0.f;
-      if constexpr (kKind == kGemm2) {
+      if constexpr (!Tr::kIsG1) {
         if (et < BN && et < t.nvalid) {
           my_tok = p.perm_tok[t.row0 + et];
           my_w = p.perm_w[t.row0 + et];
@@ -414,7 +418,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       }
 #pragma unroll
       for (int c = 0; c < CPT; ++c) acc0[c] = 0.f;
-      if constexpr (Tr::kIsG1) {
+      if constexpr (Tr::kNumA == 2) {
 #pragma unroll
         for (int c = 0; c < CPT; ++c) acc1[c] = 0.f;
       }
@@ -427,24 +431,30 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         tc_fence_after();
         const float* comb0 = ring + slot * Tr::kSlotFloats + BN + 4 + col0;
         const uint32_t taddr = lane_base + abuf * Tr::kAccCols + col0;
+        // One phase per accumulator (up, gate): every TMEM load of the phase is
+        // issued before a single wait, then the promotion FMAs run.
 #pragma unroll
-        for (int ch = 0; ch < CPT / 16; ++ch) {
-          uint32_t v[16];
-          tmem_ld16(taddr + ch * 16, v);
-          if constexpr (Tr::kIsG1) {
-            uint32_t g[16];
-            tmem_ld16(taddr + BN + ch * 16, g);
-            tmem_wait_ld();
+        for (int ph_i = 0; ph_i < Tr::kNumA; ++ph_i) {
+          float* acc = (ph_i == 0) ? acc0 : acc1;
+          const float4* sc4 = reinterpret_cast<const float4*>(comb0 + ph_i * BN);
+          uint32_t v[CPT];
+          if constexpr (CPT % 32 == 0) {
 #pragma unroll
-            for (int c = 0; c < 16; ++c) {
-              acc0[ch * 16 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 16 + c], acc0[ch * 16 + c]);
-              acc1[ch * 16 + c] = fmaf(__uint_as_float(g[c]), comb0[BN + ch * 16 + c], acc1[ch * 16 + c]);
-            }
+            for (int ch = 0; ch < CPT / 32; ++ch)
+              tmem_ld32(taddr + ph_i * BN + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[ch * 32]));
           } else {
-            tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; ++c)
-              acc0[ch * 16 + c] = fmaf(__uint_as_float(v[c]), comb0[ch * 16 + c], acc0[ch * 16 + c]);
+            for (int ch = 0; ch < CPT / 16; ++ch)
+              tmem_ld16(taddr + ph_i * BN + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[ch * 16]));
+          }
+          tmem_wait_ld();
+#pragma unroll
+          for (int c4 = 0; c4 < CPT / 4; ++c4) {
+            const float4 sc = sc4[c4];
+            acc[4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]), sc.x, acc[4 * c4 + 0]);
+            acc[4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]), sc.y, acc[4 * c4 + 1]);
+            acc[4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]), sc.z, acc[4 * c4 + 2]);
+            acc[4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]), sc.w, acc[4 * c4 + 3]);
           }
         }
         tc_fence_before();
@@ -509,12 +519,14 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
           s_cw[et] = my_w;
         }
         named_bar_sync(1, kEpiThreads);
-        const int col = t.blk * kBlk + row_in_tile;
+        const int col = t.blk * Tr::kNumA * kBlk + row_in_tile;
 #pragma unroll
         for (int c = 0; c < CPT; ++c) {
           if (col0 + c < t.nvalid) {
-            red_add_f32(p.y_acc + static_cast<int64_t>(s_ctok[col0 + c]) * kHidden + col,
-                        acc0[c] * s_cw[col0 + c]);
+            float* dst = p.y_acc + static_cast<int64_t>(s_ctok[col0 + c]) * kHidden + col;
+            const float w = s_cw[col0 + c];
+            red_add_f32(dst, acc0[c] * w);
+            if constexpr (Tr::kNumA == 2) red_add_f32(dst + kBlk, acc1[c] * w);
           }
         }
       }
@@ -568,6 +580,7 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
   X(kGemm1Fused, 64, 5, 4)             \
   X(kGemm1Split, 16, 6, 4)             \
   X(kGemm2, 128, 4, 8)                 \
+  X(kGemm2Wide, 128, 3, 8)             \
   X(kGemm2, 64, 6, 4)                  \
   X(kGemm2, 16, 10, 4)
 

@@ -17,4 +17,12 @@ cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtens
 
 bool gemm_config_supported(int kind, int bn);
 
+// Token-major grouped GEMM (gemm_tm_sm100.cu) for prefill-size batches:
+// 128 token rows x 256 weight rows per tile. GEMM1 (gemm1 = true) reads the
+// permuted activations through `a0`; GEMM2 reads the hi / lo parts of C
+// through `a0` / `a1`. Both token maps must use 128-row boxes.
+cudaError_t launch_moe_gemm_tm(bool gemm1, const CUtensorMap& w, const CUtensorMap& a0,
+                               const CUtensorMap& a1, const GemmParams& p, int grid,
+                               cudaStream_t stream);
+
 }  // namespace moe

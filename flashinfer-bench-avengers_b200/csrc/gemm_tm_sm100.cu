@@ -1,0 +1,430 @@
+// Token-major grouped FP8 GEMMs for prefill-size batches (sm_100a).
+//
+// The MMA's M side is 128 permuted token rows (one TMEM lane each) and its N
+// side is 256 weight rows of one expert, K-major e4m3 operands with the
+// 128-byte swizzle, one tcgen05.mma M=128 N=256 K=32 per 32 K-elements.
+// After each 128-wide K block the epilogue folds the fresh accumulator into
+// fp32 registers with that block's scale. In this orientation the scale of a
+// TMEM lane's whole 128-column weight block is a single number, token scale
+// times weight scale, so the promotion is one FFMA per element with a
+// register operand -- no per-column scale loads. (The swap-AB kernels in
+// gemm_sm100.cu keep weights on M; they serve decode-size batches, where a
+// token tile of 16 keeps the MMA small.)
+//
+// GEMM1 tile: 128 tokens x (128 up rows + 128 gate rows of intermediate
+// block `blk`); epilogue C = silu(gate) * up (solution/cuda/kernel.h:207),
+// written as the hi/lo e4m3 pair with one scale per (row, 128-block).
+// GEMM2 tile: 128 tokens x 256 W2 rows (two 128-row blocks); the hi and lo
+// parts of C accumulate into one accumulator; epilogue red.adds w * O into
+// the fp32 combine rows with 16-byte vector reductions.
+//
+// Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-3
+// spare, warps 4-11 epilogue (TMEM lane quarter w % 4, column half
+// (w - 4) / 4). The role warpgroup drops to 56 registers and the epilogue
+// warpgroups rise to 224.
+#include <cuda.h>
+#include <cuda_fp8.h>
+#include <cstdint>
+
+#include "gemm_sm100.h"
+#include "moe_kernels.cuh"
+#include "moe_ptx.cuh"
+#include "moe_shapes.cuh"
+
+namespace moe {
+
+template <bool kG1, int kStages>
+struct TmTraits {
+  static constexpr int BM = 128;                   // token rows per tile
+  static constexpr int BW = 256;                   // weight rows per tile
+  static constexpr int kATileBytes = BM * 128;     // one token operand per K block
+  static constexpr int kNumA = kG1 ? 1 : 2;        // activations / C hi + lo
+  static constexpr int kBTileBytes = BW * 128;
+  static constexpr int kStageBytes = kNumA * kATileBytes + kBTileBytes;
+  static constexpr int kKBlocks = kG1 ? kHiddenBlocks : kInterBlocks;
+  static constexpr int kRowBlocks = kG1 ? kInterBlocks : kHiddenBlocks / 2;
+  static constexpr int kAccCols = 256;
+  static constexpr int kTmemCols = 512;            // two accumulator buffers
+  static constexpr int kScaleSlots = 8;
+  static constexpr int kSlotFloats = BM + 4;       // token scales | weight scales x2 | pad
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = (4 + kEpiWarps) * 32;
+  static constexpr uint32_t kIdesc = idesc_e4m3_f32<128, 256>();
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kRoleRegs = 56;
+  static constexpr int kEpiRegs = 224;
+  static_assert(kRoleRegs * 128 + kEpiRegs * 32 * kEpiWarps <= kLaunchRegs * kThreads,
+                "register split exceeds the block's launch registers");
+
+  static constexpr int kOffRing = kStages * kStageBytes;
+  static constexpr int kOffBars = kOffRing + kScaleSlots * kSlotFloats * 4;
+  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kScaleSlots;
+  static constexpr int kOffMisc = kOffBars + kNumBars * 8;
+  static constexpr int kOffUnitPre = kOffMisc + 16;
+  static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
+  static constexpr int kOffCnt = kOffSeg + 34 * 4;
+  static constexpr int kOffRed = kOffCnt + 32 * 4;   // [2][BM] row maxima (GEMM1)
+  static constexpr int kSmemBytes = kOffRed + 2 * BM * 4 + 1024;
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+namespace {
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
+               "f"(d)
+               : "memory");
+}
+
+__device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
+  const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+__device__ __forceinline__ float e4m3_round(float x) {
+  const __nv_fp8_e4m3 q(x);
+  return static_cast<float>(q);
+}
+
+// Units of work: per expert ceil(count / 128) token tiles x kRowBlocks weight
+// blocks, token tiles fastest so CTAs running at the same time share the
+// weight block through L2.
+struct TmTile {
+  int e, blk, row0, nvalid;
+};
+
+__device__ __forceinline__ void tm_decode(int u, const int* s_unit_pre, const int* s_seg, const int* s_cnt,
+                                          TmTile& t) {
+  int e = 0;
+#pragma unroll 1
+  while (s_unit_pre[e + 1] <= u) ++e;
+  const int cnt = s_cnt[e];
+  const int nt = (cnt + 127) / 128;
+  const int local = u - s_unit_pre[e];
+  const int tt = local % nt;
+  t.e = e;
+  t.blk = local / nt;
+  t.row0 = s_seg[e] + tt * 128;
+  t.nvalid = min(128, cnt - tt * 128);
+}
+
+}  // namespace
+
+template <bool kG1, int kStages>
+__global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
+    moe_gemm_tm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_a0,
+                       const __grid_constant__ CUtensorMap tm_a1, const GemmParams p) {
+  using Tr = TmTraits<kG1, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  float* ring = reinterpret_cast<float*>(smem + Tr::kOffRing);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Tr::kOffBars);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + kStages;
+  uint64_t* accf_bar = bars + 2 * kStages;
+  uint64_t* acce_bar = accf_bar + 2;
+  uint64_t* sfull_bar = acce_bar + 2;
+  uint64_t* sempty_bar = sfull_bar + Tr::kScaleSlots;
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + Tr::kOffMisc);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + Tr::kOffMisc + 4);
+  int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
+  int* s_seg = reinterpret_cast<int*>(smem + Tr::kOffSeg);
+  int* s_cnt = reinterpret_cast<int*>(smem + Tr::kOffCnt);
+  float* s_red = reinterpret_cast<float*>(smem + Tr::kOffRed);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  // ---------------------------------------------------------------- setup
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_a0);
+    if (!kG1) prefetch_tmap(&tm_a1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full_bar[s]), 1);
+      mbar_init(smem_u32(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&accf_bar[b]), 1);
+      mbar_init(smem_u32(&acce_bar[b]), Tr::kEpiWarps);
+    }
+    for (int s = 0; s < Tr::kScaleSlots; ++s) {
+      mbar_init(smem_u32(&sfull_bar[s]), 2);
+      mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(s_tmem), Tr::kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 2) {
+    const int lo = p.seg_off[lane];
+    const int cnt = p.counts[lane];
+    const int units = ((cnt + 127) / 128) * Tr::kRowBlocks;
+    int incl = units;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    s_unit_pre[lane + 1] = incl;
+    s_seg[lane] = lo;
+    s_cnt[lane] = cnt;
+    if (lane == 0) s_unit_pre[0] = 0;
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *s_tmem;
+  const int total_units = s_unit_pre[kExpertsLocal];
+
+  if (warp == 0) {
+    // ======================================================== TMA producer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    int stage = 0, slot = 0;
+    uint32_t ph = 0, sph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      TmTile t;
+      tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
+      int brow0, brow1, wrow0, wrow1;
+      if constexpr (kG1) {
+        brow0 = t.e * kGemm1Out + t.blk * kBlk;
+        brow1 = brow0 + kInter;
+        wrow0 = (t.e * kGemm1OutBlocks + t.blk) * kHiddenBlocks;
+        wrow1 = (t.e * kGemm1OutBlocks + kInterBlocks + t.blk) * kHiddenBlocks;
+      } else {
+        brow0 = t.e * kHidden + t.blk * 2 * kBlk;
+        brow1 = brow0 + kBlk;
+        wrow0 = (t.e * kHiddenBlocks + 2 * t.blk) * kInterBlocks;
+        wrow1 = wrow0 + kInterBlocks;
+      }
+      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+        if (!mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer) ||
+            !mbar_wait(smem_u32(&sempty_bar[slot]), sph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0) {
+          uint8_t* st = smem + stage * Tr::kStageBytes;
+          const uint32_t fb = smem_u32(&full_bar[stage]);
+          const int kx = kb * kBlk;
+          mbar_arrive_expect_tx(fb, Tr::kStageBytes);
+          tma_load_2d(smem_u32(st), &tm_a0, fb, kx, t.row0);
+          if constexpr (!kG1) tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_a1, fb, kx, t.row0);
+          uint8_t* bt = st + Tr::kNumA * Tr::kATileBytes;
+          tma_load_2d(smem_u32(bt), &tm_w, fb, kx, brow0);
+          tma_load_2d(smem_u32(bt + 128 * 128), &tm_w, fb, kx, brow1);
+          float* sp = ring + slot * Tr::kSlotFloats;
+          const uint32_t sb = smem_u32(&sfull_bar[slot]);
+          mbar_arrive_expect_tx(sb, Tr::BM * 4);
+          bulk_load(smem_u32(sp), p.act_scale + static_cast<int64_t>(kb) * p.cap + t.row0, Tr::BM * 4, sb);
+          cp_async_4(smem_u32(sp + Tr::BM), p.w_scale + wrow0 + kb);
+          cp_async_4(smem_u32(sp + Tr::BM + 1), p.w_scale + wrow1 + kb);
+          cp_async_arrive_noinc(sb);
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; ph ^= 1; }
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+      }
+    }
+  } else if (warp == 1) {
+    // ========================================================== MMA issuer
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    int stage = 0, abuf = 0;
+    uint32_t ph = 0, aph = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+        if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
+            !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        if (lane == 0) {
+          const uint32_t st = smem_u32(smem + stage * Tr::kStageBytes);
+          const uint32_t bt = st + Tr::kNumA * Tr::kATileBytes;
+          const uint32_t d = tmem_base + abuf * Tr::kAccCols;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t bdesc = sw128_kmajor_desc(bt + 32 * k);
+            umma_f8(d, sw128_kmajor_desc(st + 32 * k), bdesc, Tr::kIdesc, k > 0 ? 1u : 0u);
+            if constexpr (!kG1) umma_f8(d, sw128_kmajor_desc(st + Tr::kATileBytes + 32 * k), bdesc, Tr::kIdesc, 1u);
+          }
+          umma_commit(smem_u32(&empty_bar[stage]));
+          umma_commit(smem_u32(&accf_bar[abuf]));
+        }
+        __syncwarp();
+        if (++stage == kStages) { stage = 0; ph ^= 1; }
+        if (++abuf == 2) { abuf = 0; aph ^= 1; }
+      }
+    }
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+  } else {
+    // ============================================================ epilogue
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Tr::kEpiRegs));
+    const int q = warp & 3;              // TMEM lane quarter: token rows q*32 .. q*32+31
+    const int hf = (warp - 4) >> 2;      // column half
+    const int r = q * 32 + lane;         // token row inside the tile
+    const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+    int slot = 0, abuf = 0;
+    uint32_t sph = 0, aph = 0;
+    bool ok = true;
+    // GEMM1: acc0 = up, acc1 = gate for intermediate columns hf*64 .. +64.
+    // GEMM2: acc0 / acc1 = W2 rows (2*blk + hf)*128 + [0, 64) / [64, 128).
+    float acc0[64], acc1[64];
+    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+      TmTile t;
+      tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
+      const bool valid = r < t.nvalid;
+      int my_tok = 0;
+      float my_w = 0.f;
+      if constexpr (!kG1) {
+        if (valid) {
+          my_tok = p.perm_tok[t.row0 + r];
+          my_w = p.perm_w[t.row0 + r];
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 64; ++c) { acc0[c] = 0.f; acc1[c] = 0.f; }
+      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        const float* sp = ring + slot * Tr::kSlotFloats;
+        const float ts = sp[r];
+        // GEMM1: up / gate scales; GEMM2: this half's W2 block scale for both phases
+        const float s0 = ts * (kG1 ? sp[Tr::BM] : sp[Tr::BM + hf]);
+        const float s1 = kG1 ? ts * sp[Tr::BM + 1] : s0;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sempty_bar[slot]));
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+        if (!mbar_wait(smem_u32(&accf_bar[abuf]), aph, s_abort, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tb = lane_base + abuf * Tr::kAccCols;
+        const uint32_t col_a = kG1 ? hf * 64 : hf * 128;
+        const uint32_t col_b = kG1 ? 128 + hf * 64 : hf * 128 + 64;
+        uint32_t v[64];
+        tmem_ld32(tb + col_a, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tb + col_a + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc0[c] = fmaf(__uint_as_float(v[c]), s0, acc0[c]);
+        tmem_ld32(tb + col_b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
+        tmem_ld32(tb + col_b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&acce_bar[abuf]));
+        if (++abuf == 2) { abuf = 0; aph ^= 1; }
+#pragma unroll
+        for (int c = 0; c < 64; ++c) acc1[c] = fmaf(__uint_as_float(v[c]), s1, acc1[c]);
+      }
+      if (!ok) break;
+
+      // ------------------------------------------------- final epilogue
+      const int64_t row = t.row0 + r;
+      if constexpr (kG1) {
+        float m = 0.f;
+#pragma unroll
+        for (int c = 0; c < 64; ++c) {
+          const float g = acc1[c];
+          acc0[c] = g / (1.0f + expf(-g)) * acc0[c];
+          m = fmaxf(m, fabsf(acc0[c]));
+        }
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        s_red[hf * Tr::BM + r] = m;
+        named_bar_sync(1, 32 * Tr::kEpiWarps);
+        const float amax = fmaxf(s_red[r], s_red[Tr::BM + r]);
+        const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+        if (valid) {
+          if (hf == 0) p.c_scale[static_cast<int64_t>(t.blk) * p.cap + row] = amax * (1.0f / 448.0f);
+          uint4* hi_dst = reinterpret_cast<uint4*>(p.c_hi + row * kInter + t.blk * kBlk + hf * 64);
+          uint4* lo_dst = reinterpret_cast<uint4*>(p.c_lo + row * kInter + t.blk * kBlk + hf * 64);
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint32_t wh[4], wl[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              float x[4], res[4];
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                x[i] = acc0[16 * g + 4 * j + i] * inv;
+                res[i] = x[i] - e4m3_round(x[i]);
+              }
+              wh[j] = pack_e4m3x4(x[0], x[1], x[2], x[3]);
+              wl[j] = pack_e4m3x4(res[0], res[1], res[2], res[3]);
+            }
+            hi_dst[g] = make_uint4(wh[0], wh[1], wh[2], wh[3]);
+            lo_dst[g] = make_uint4(wl[0], wl[1], wl[2], wl[3]);
+          }
+        }
+      } else {
+        if (valid) {
+          float* dst = p.y_acc + static_cast<int64_t>(my_tok) * kHidden + (2 * t.blk + hf) * kBlk;
+#pragma unroll
+          for (int c = 0; c < 64; c += 4)
+            red_add_v4(dst + c, acc0[c] * my_w, acc0[c + 1] * my_w, acc0[c + 2] * my_w, acc0[c + 3] * my_w);
+#pragma unroll
+          for (int c = 0; c < 64; c += 4)
+            red_add_v4(dst + 64 + c, acc1[c] * my_w, acc1[c + 1] * my_w, acc1[c + 2] * my_w, acc1[c + 3] * my_w);
+        }
+      }
+    }
+  }
+
+  // --------------------------------------------------------------- teardown
+  if (*s_abort) {
+    const uint64_t t0 = globaltimer_ns();
+    while (globaltimer_ns() - t0 < 2000000ull) {
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Tr::kTmemCols);
+  }
+}
+
+template <bool kG1, int kStages>
+static cudaError_t launch_tm(const CUtensorMap& w, const CUtensorMap& a0, const CUtensorMap& a1,
+                             const GemmParams& p, int grid, cudaStream_t stream) {
+  using Tr = TmTraits<kG1, kStages>;
+  auto kern = moe_gemm_tm_kernel<kG1, kStages>;
+  static int checked_device = -1;
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) return err;
+  if (checked_device != dev) {
+    err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
+    if (err != cudaSuccess) return err;
+    // The warpgroup register split is only safe if the block launches with
+    // exactly the registers it was sized for.
+    cudaFuncAttributes attr;
+    err = cudaFuncGetAttributes(&attr, kern);
+    if (err != cudaSuccess) return err;
+    if (attr.numRegs != Tr::kLaunchRegs) return cudaErrorInvalidConfiguration;
+    checked_device = dev;
+  }
+  kern<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(w, a0, a1, p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_moe_gemm_tm(bool gemm1, const CUtensorMap& w, const CUtensorMap& a0, const CUtensorMap& a1,
+                               const GemmParams& p, int grid, cudaStream_t stream) {
+  return gemm1 ? launch_tm<true, 4>(w, a0, a1, p, grid, stream) : launch_tm<false, 3>(w, a0, a1, p, grid, stream);
+}
+
+}  // namespace moe

@@ -37,7 +37,12 @@ struct Plan {
   int g1_splits;
   int g2_bn;
   int g2_splits;
+  bool g2_wide;    // two W2 row blocks per GEMM2 tile
+  bool token_major;  // prefill: token-major GEMMs (gemm_tm_sm100.cu)
 };
+
+// From this many tokens per call the prefill (token-major) GEMMs are used.
+constexpr int64_t kTokenMajorMinTokens = 512;
 
 Plan choose_plan(int64_t T) {
   Plan p{};
@@ -53,6 +58,8 @@ Plan choose_plan(int64_t T) {
     p.g1_splits = 1;
     p.g2_bn = T >= 1024 ? 128 : 64;
     p.g2_splits = 1;
+    p.g2_wide = T >= 1024;
+    p.token_major = T >= kTokenMajorMinTokens;
   }
   return p;
 }
@@ -348,13 +355,15 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
 
   // ---- tensor maps ---------------------------------------------------------
   CUtensorMap tm_aperm, tm_w13, tm_w2, tm_chi, tm_clo;
-  if (!encode_u8_2d(&tm_aperm, a_perm, kHidden, cap, 128, plan.g1_bn) ||
+  const uint32_t a_box = plan.token_major ? 128 : plan.g1_bn;
+  const uint32_t c_box = plan.token_major ? 128 : plan.g2_bn;
+  if (!encode_u8_2d(&tm_aperm, a_perm, kHidden, cap, 128, a_box) ||
       !encode_u8_2d(&tm_w13, gemm1_weights, kHidden, static_cast<uint64_t>(kExpertsLocal) * kGemm1Out,
                     128, 128) ||
       !encode_u8_2d(&tm_w2, gemm2_weights, kInter, static_cast<uint64_t>(kExpertsLocal) * kHidden, 128,
                     128) ||
-      !encode_u8_2d(&tm_chi, c_hi, kInter, cap, 128, plan.g2_bn) ||
-      !encode_u8_2d(&tm_clo, c_lo, kInter, cap, 128, plan.g2_bn))
+      !encode_u8_2d(&tm_chi, c_hi, kInter, cap, 128, c_box) ||
+      !encode_u8_2d(&tm_clo, c_lo, kInter, cap, 128, c_box))
     return MOE_B200_ERR_DRIVER;
 
   // ---- launches ------------------------------------------------------------
@@ -418,6 +427,10 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
       return MOE_B200_ERR_CUDA;
     swiglu_quant_kernel<<<di.sm_count * 2, 256, 0, s>>>(seg_off, g1_acc, c_hi, c_lo, c_scale, cap);
     if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  } else if (plan.token_major) {
+    const int grid_tm = grid_for(num_tokens, 128, kInterBlocks, 1, di.sm_count);
+    if (launch_moe_gemm_tm(true, tm_w13, tm_aperm, tm_aperm, g1, grid_tm, s) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
   } else {
     if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
@@ -429,9 +442,16 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g2.w_scale = gemm2_weights_scale;
   g2.splits = plan.g2_splits;
   g2.y_acc = y_acc;
-  const int grid2 = grid_for(num_tokens, plan.g2_bn, kHiddenBlocks, plan.g2_splits, di.sm_count);
-  if (launch_moe_gemm(kGemm2, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, s) != cudaSuccess)
+  const int g2_kind = plan.g2_wide ? kGemm2Wide : kGemm2;
+  const int grid2 = grid_for(num_tokens, plan.g2_bn, plan.g2_wide ? kHiddenBlocks / 2 : kHiddenBlocks,
+                             plan.g2_splits, di.sm_count);
+  if (plan.token_major) {
+    const int grid_tm = grid_for(num_tokens, 128, kHiddenBlocks / 2, 1, di.sm_count);
+    if (launch_moe_gemm_tm(false, tm_w2, tm_chi, tm_clo, g2, grid_tm, s) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
+  } else if (launch_moe_gemm(g2_kind, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, s) != cudaSuccess) {
     return MOE_B200_ERR_CUDA;
+  }
   mark_stage(5, s);
 
   const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;

@@ -45,6 +45,7 @@ enum GemmKind : int {
   kGemm1Fused = 0,  // GEMM1 over the full K, SwiGLU + hi/lo e4m3 split in the epilogue
   kGemm1Split = 1,  // GEMM1 over a K slice, fp32 red.add into g1_acc
   kGemm2 = 2,       // GEMM2 (hi + lo operands), weighted fp32 red.add into y_acc
+  kGemm2Wide = 3,   // GEMM2 over two 128-row W2 blocks per tile (M = 256)
 };
 
 struct GemmParams {
