@@ -68,9 +68,13 @@ FLOP_PER_ASSIGNMENT_G2 = 2 * 2048 * 7168
 PUBLISHED_US = {1: 551.0, 7: 1034.0, 14: 1609.0, 15: 850.0, 16: 1727.0, 32: 2803.0, 80: 3620.0,
                 901: 4545.0, 11948: 11731.0, 14107: 15650.0}
 
-# DRAM traffic per launch from ncu captures (profiles/), keyed by (kernel, T).
-# None until a capture of that launch exists.
-NCU_TRAFFIC_BYTES = {}
+# DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
+# the ncu captures summarised in profiles/, keyed by (kernel, T) of the bench
+# workloads; None when no capture of that launch exists.
+NCU_TRAFFIC_BYTES = {
+    ("gemm1", 64): 472_598_016 + 4_210_944,        # profiles/decode_gemms_T64.md
+    ("gemm1", 4096): 947_077_376 + 75_514_368,     # profiles/gemm1_token_major_prefill_T4096_hot.md
+}
 
 
 def load_peaks() -> dict:
