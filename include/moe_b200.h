@@ -143,6 +143,39 @@ MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_work
 #define MOE_B200_NUM_STAGE_EVENTS 7
 MOE_B200_API int moe_b200_set_stage_events(void* const* events, int num_events);
 
+/*
+ * Allocation-free variant of moe_b200_run for small batches. No counterpart
+ * in the reference (its host code allocates per call, main.cpp:50-108).
+ *
+ * For callers that may not allocate device memory when they call the layer:
+ * runtimes that reserve every buffer up front and forbid cudaMalloc later,
+ * host code without a CUDA allocator to provide a workspace, or latency-
+ * critical loops that cannot afford an allocation. The caller passes the
+ * inputs and the output (same meaning and alignment as moe_b200_run); the
+ * scratch is a fixed MOE_B200_NOALLOC_SCRATCH_BYTES array inside the library,
+ * which every GPU that loads the library holds until the process exits.
+ *
+ * Limits and behaviour:
+ *   - num_tokens <= MOE_B200_NOALLOC_MAX_TOKENS, otherwise the call returns
+ *     MOE_B200_ERR_WORKSPACE_TOO_SMALL without doing anything;
+ *   - the first call on a device looks up that device's array address (with
+ *     the device current); make that first call before any stream capture;
+ *   - all calls on a device share the one array: calls that may overlap on
+ *     the GPU (different streams without ordering, or several threads) race
+ *     and corrupt each other's results. Each call clears what must start at
+ *     zero, so leftovers from the previous call do no harm;
+ *   - no cudaMalloc, cudaFree or other allocating routine is called.
+ */
+#define MOE_B200_NOALLOC_MAX_TOKENS 16
+#define MOE_B200_NOALLOC_SCRATCH_BYTES (24u << 20)
+MOE_B200_API int moe_b200_run_noalloc(const float* routing_logits, const void* routing_bias,
+                                      int routing_bias_dtype, const void* hidden_states,
+                                      const float* hidden_states_scale, const void* gemm1_weights,
+                                      const float* gemm1_weights_scale, const void* gemm2_weights,
+                                      const float* gemm2_weights_scale, int64_t local_expert_offset,
+                                      double routed_scaling_factor, int64_t num_tokens,
+                                      void* output, void* stream);
+
 /* ABI version of this header (bumped on any signature change). */
 MOE_B200_API int moe_b200_abi_version(void);
 
