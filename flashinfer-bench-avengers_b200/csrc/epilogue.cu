@@ -11,6 +11,7 @@
 #include <cstdint>
 
 #include "moe_kernels.cuh"
+#include "moe_ptx.cuh"
 #include "moe_shapes.cuh"
 
 namespace moe {
@@ -19,6 +20,8 @@ namespace moe {
 __global__ void __launch_bounds__(256) swiglu_quant_kernel(const int* seg_off, const float* g1_acc,
                                                            uint8_t* c_hi, uint8_t* c_lo,
                                                            float* c_scale, int cap) {
+  pdl_launch_next();
+  pdl_wait();
   const int rows = seg_off[kExpertsLocal];
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
@@ -60,6 +63,8 @@ __global__ void __launch_bounds__(256) swiglu_quant_kernel(const int* seg_off, c
 
 // n4 = number of float4 groups (T * 7168 / 4).
 __global__ void __launch_bounds__(256) finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4) {
+  pdl_launch_next();
+  pdl_wait();
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
     const float4 v = reinterpret_cast<const float4*>(y_acc)[i];

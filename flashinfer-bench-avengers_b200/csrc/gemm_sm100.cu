@@ -61,7 +61,9 @@ struct GemmTraits {
                                    : (2 * kAccCols <= 64) ? 64
                                    : (2 * kAccCols <= 128) ? 128
                                    : (2 * kAccCols <= 256) ? 256 : 512;
-  static constexpr int kScaleSlots = 8;
+  // The scale ring must not be shallower than the stage ring, or it caps the
+  // bytes in flight (the decode kernels are latency x bytes-in-flight bound).
+  static constexpr int kScaleSlots = kStages + 4 > 8 ? kStages + 4 : 8;
   // scale slot: raw[BN] | wscale[4] | combined[kNumA][BN]
   static constexpr int kSlotFloats = BN + 4 + kNumA * BN;
   // Warps 0..3 are the role warpgroup (producer, MMA, scale combiner, one
@@ -88,13 +90,19 @@ struct GemmTraits {
   static constexpr int kOffStages = 0;
   static constexpr int kOffRing = kStages * kStageBytes;
   static constexpr int kOffBars = kOffRing + kScaleSlots * kSlotFloats * 4;
-  static constexpr int kNumBars = 2 * kStages + 4 + 3 * kScaleSlots;
+  // Work units are handed out dynamically: the producer takes the next unit
+  // from a per-call counter and passes it to the other roles through a small
+  // ring (s_units + full/empty barriers).
+  static constexpr int kUnitSlots = 4;
+  static constexpr int kUnitConsumers = 2 + kEpiWarps;  // MMA, scale combiner, epilogue warps
+  static constexpr int kNumBars = 2 * kStages + 4 + 3 * kScaleSlots + 2 * kUnitSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;
   // misc: tmem base (4) | abort (4) | unit_pre[33] | seg[33] | cnt[32] | epilogue scratch
   static constexpr int kOffUnitPre = kOffMisc + 16;
   static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
   static constexpr int kOffCnt = kOffSeg + 34 * 4;
-  static constexpr int kOffEpi = kOffCnt + 32 * 4;
+  static constexpr int kOffUnits = kOffCnt + 32 * 4;
+  static constexpr int kOffEpi = kOffUnits + kUnitSlots * 4;
   // epilogue scratch: red[4][BN] | inv[BN] | tok[BN] | w[BN]
   static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
   static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;  // + alignment slack
@@ -191,6 +199,9 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   uint64_t* sraw_bar = acce_bar + 2;
   uint64_t* sfull_bar = sraw_bar + Tr::kScaleSlots;
   uint64_t* sempty_bar = sfull_bar + Tr::kScaleSlots;
+  uint64_t* ufull_bar = sempty_bar + Tr::kScaleSlots;
+  uint64_t* uempty_bar = ufull_bar + Tr::kUnitSlots;
+  volatile int* s_units = reinterpret_cast<volatile int*>(smem + Tr::kOffUnits);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + Tr::kOffMisc);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + Tr::kOffMisc + 4);
   int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
@@ -223,6 +234,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       mbar_init(smem_u32(&sfull_bar[s]), 1);
       mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
     }
+    for (int s = 0; s < Tr::kUnitSlots; ++s) {
+      mbar_init(smem_u32(&ufull_bar[s]), 1);
+      mbar_init(smem_u32(&uempty_bar[s]), Tr::kUnitConsumers);
+    }
     *s_abort = 0;
     fence_mbar_init();
     fence_proxy_async_smem();
@@ -231,6 +246,12 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     tmem_alloc(smem_u32(s_tmem), Tr::kTmemCols);
     tmem_relinquish();
   }
+  // Everything up to pdl_wait() overlaps the previous kernel's tail
+  // (programmatic dependent launch). The segment table comes from the
+  // permutation, which has completed before this grid is launched (the
+  // kernels between release their dependents only after their own wait), so
+  // it can be read here; the producer also issues the first stages' weight
+  // tiles, which no earlier kernel writes, before waiting.
   if (warp == 2) {
     // per-expert tile counts -> prefix over experts of the work units
     const int lo = p.seg_off[lane];
@@ -256,12 +277,59 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   if (warp == 0) {
     // ======================================================== TMA producer
     if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    // The first unit and the weight tiles of its first stages are taken
+    // before waiting for the previous kernel (the stages are fresh, so no
+    // empty-slot wait; the unit counter was cleared by the permutation).
+    int u = -1;
+    if (lane == 0) u = atomicAdd(p.sched, 1);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= total_units) u = -1;
+    int pre_issued = 0;
+    if (u >= 0) {
+      Tile t;
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      const int nkb = t.kb1 - t.kb0;
+      const int rot = (t.blk * 5 + t.e * 3) % nkb;
+      pre_issued = nkb < kStages ? nkb : kStages;
+      if (lane == 0) {
+        int arow0, arow1;
+        if constexpr (Tr::kIsG1) {
+          arow0 = t.e * kGemm1Out + t.blk * kBlk;
+          arow1 = arow0 + kInter;
+        } else {
+          arow0 = t.e * kHidden + t.blk * Tr::kNumA * kBlk;
+          arow1 = arow0 + kBlk;
+        }
+        for (int i = 0; i < pre_issued; ++i) {
+          const int kb = t.kb0 + (i + rot) % nkb;
+          uint8_t* st = smem + Tr::kOffStages + i * Tr::kStageBytes;
+          const uint32_t fb = smem_u32(&full_bar[i]);
+          mbar_arrive_expect_tx(fb, Tr::kStageBytes);
+          tma_load_2d(smem_u32(st), &tm_w, fb, kb * kBlk, arow0);
+          if constexpr (Tr::kNumA == 2) tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kb * kBlk, arow1);
+        }
+      }
+    }
+    pdl_wait();
+    pdl_launch_next();
     int stage = 0;
     uint32_t ph = 0;
     int slot = 0;
     uint32_t sph = 0;
+    int uslot = 0;
+    uint32_t uph = 0;
+    int iter = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    while (ok) {
+      // publish the unit (or the end marker -1) to the other roles
+      if (!mbar_wait(smem_u32(&uempty_bar[uslot]), uph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) break;
+      if (lane == 0) {
+        s_units[uslot] = u;
+        mbar_arrive(smem_u32(&ufull_bar[uslot]));
+      }
+      __syncwarp();
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       int arow0, arow1 = 0, wrow0, wrow1 = 0;
@@ -276,8 +344,18 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         wrow0 = (t.e * kHiddenBlocks + t.blk * Tr::kNumA) * kInterBlocks;
         wrow1 = wrow0 + kInterBlocks;
       }
-      for (int kb = t.kb0; kb < t.kb1; ++kb) {
-        if (!mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer) ||
+      // K blocks are visited in a tile-dependent rotation: weight rows are
+      // 2 KB (W2) or 7 KB (W13) apart, and CTAs that all start at K block 0
+      // would aim their 128-byte row slices at the same address residues.
+      // Each weight tile here belongs to one CTA, so no L2 sharing is lost.
+      const int nkb = t.kb1 - t.kb0;
+      const int rot = (t.blk * 5 + t.e * 3) % nkb;
+      for (int i = 0; i < nkb; ++i) {
+        const int kb = t.kb0 + (i + rot) % nkb;
+        const bool weights_issued = iter < pre_issued;
+        ++iter;
+        if ((!weights_issued &&
+             !mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) ||
             !mbar_wait(smem_u32(&sempty_bar[slot]), sph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) {
           ok = false;
           break;
@@ -286,9 +364,11 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
           uint8_t* st = smem + Tr::kOffStages + stage * Tr::kStageBytes;
           const uint32_t fb = smem_u32(&full_bar[stage]);
           const int kx = kb * kBlk;
-          mbar_arrive_expect_tx(fb, Tr::kStageBytes);
-          tma_load_2d(smem_u32(st), &tm_w, fb, kx, arow0);
-          if constexpr (Tr::kNumA == 2) tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
+          if (!weights_issued) {
+            mbar_arrive_expect_tx(fb, Tr::kStageBytes);
+            tma_load_2d(smem_u32(st), &tm_w, fb, kx, arow0);
+            if constexpr (Tr::kNumA == 2) tma_load_2d(smem_u32(st + Tr::kATileBytes), &tm_w, fb, kx, arow1);
+          }
           uint8_t* bt = st + Tr::kNumA * Tr::kATileBytes;
           tma_load_2d(smem_u32(bt), &tm_b0, fb, kx, t.row0);
           if constexpr (Tr::kNumB == 2) tma_load_2d(smem_u32(bt + Tr::kBTileBytes), &tm_b1, fb, kx, t.row0);
@@ -307,16 +387,29 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         if (++stage == kStages) { stage = 0; ph ^= 1; }
         if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
       }
+      if (lane == 0) u = atomicAdd(p.sched, 1);
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u >= total_units) u = -1;
     }
   } else if (warp == 1) {
     // ========================================================== MMA issuer
     if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    pdl_wait();
+    pdl_launch_next();
     int stage = 0;
     uint32_t ph = 0;
     int abuf = 0;
     uint32_t aph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    int uslot = 0;
+    uint32_t uph = 0;
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
@@ -355,10 +448,20 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   } else if (warp == 2) {
     // ======================================================= scale combiner
     if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    pdl_wait();
+    pdl_launch_next();
     int slot = 0;
     uint32_t sph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    int uslot = 0;
+    uint32_t uph = 0;
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
@@ -386,9 +489,13 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   } else if (warp < Tr::kRoleWarps) {
     // spare warp of the role warpgroup
     if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    pdl_wait();
+    pdl_launch_next();
   } else {
     // ============================================================ epilogue
     if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Tr::kEpiRegs));
+    pdl_wait();
+    pdl_launch_next();
     constexpr int CPT = Tr::kCPT;
     const int ew = warp - Tr::kRoleWarps;
     const int q = warp & 3;                   // TMEM lane quarter of this warp
@@ -404,7 +511,15 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     bool ok = true;
     float acc0[CPT];
     float acc1[CPT];  // second accumulator (gate / second W2 block); unused when kNumA == 1
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    int uslot = 0;
+    uint32_t uph = 0;
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       // per-column data for the final epilogue, loaded early
@@ -571,8 +686,7 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
     }
     checked_device = dev;
   }
-  kern<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(w, b0, b1, p);
-  return cudaGetLastError();
+  return launch_kernel(kern, grid, Tr::kThreads, Tr::kSmemBytes, stream, true, w, b0, b1, p);
 }
 
 #define MOE_GEMM_CONFIGS(X)            \

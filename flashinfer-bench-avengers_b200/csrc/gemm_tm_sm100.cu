@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     tmem_alloc(smem_u32(s_tmem), Tr::kTmemCols);
     tmem_relinquish();
   }
+  // Everything above overlaps the previous kernel's tail (programmatic
+  // dependent launch); the routing and permutation results are read below.
+  pdl_wait();
+  pdl_launch_next();
   if (warp == 2) {
     const int lo = p.seg_off[lane];
     const int cnt = p.counts[lane];
@@ -418,8 +422,7 @@ static cudaError_t launch_tm(const CUtensorMap& w, const CUtensorMap& a0, const 
     if (attr.numRegs != Tr::kLaunchRegs) return cudaErrorInvalidConfiguration;
     checked_device = dev;
   }
-  kern<<<grid, Tr::kThreads, Tr::kSmemBytes, stream>>>(w, a0, a1, p);
-  return cudaGetLastError();
+  return launch_kernel(kern, grid, Tr::kThreads, Tr::kSmemBytes, stream, true, w, a0, a1, p);
 }
 
 cudaError_t launch_moe_gemm_tm(bool gemm1, const CUtensorMap& w, const CUtensorMap& a0, const CUtensorMap& a1,

@@ -49,9 +49,9 @@ Plan choose_plan(int64_t T) {
   if (T <= 64) {
     p.split_g1 = true;
     p.g1_bn = 16;
-    p.g1_splits = T <= 16 ? 8 : 4;
+    p.g1_splits = 8;
     p.g2_bn = 16;
-    p.g2_splits = T <= 16 ? 2 : 1;
+    p.g2_splits = 2;
   } else {
     p.split_g1 = false;
     p.g1_bn = T >= 1024 ? 128 : 64;
@@ -80,9 +80,12 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   size_t off = 0;
   l.counts = off;
   l.status = off + kExpertsLocal * sizeof(int);
-  off = align_up(off + kExpertsLocal * sizeof(int) + sizeof(uint32_t));
+  l.sched = l.status + 16;
+  off = align_up(l.sched + 4 * sizeof(int));
   l.seg_off = off;
   off = align_up(off + (kExpertsLocal + 1) * sizeof(int));
+  l.chunk_counts = off;
+  off = align_up(off + static_cast<size_t>((T + 1023) / 1024) * kExpertsLocal * sizeof(int));
   l.topk_idx = off;
   off = align_up(off + cap * sizeof(int32_t));
   l.topk_w = off;
@@ -192,7 +195,7 @@ int grid_for(int64_t T, int bn, int row_blocks, int splits, int sm_count) {
 }
 
 int launch_route(const float* logits, const void* bias, int bias_dtype, int T, float rsf,
-                 int local_off, int32_t* topk_idx, float* topk_w, int* counts, cudaStream_t s) {
+                 int local_off, int32_t* topk_idx, float* topk_w, cudaStream_t s) {
   RouteParams rp;
   rp.logits = logits;
   rp.bias = bias;
@@ -202,7 +205,8 @@ int launch_route(const float* logits, const void* bias, int bias_dtype, int T, f
   rp.local_expert_offset = local_off;
   rp.topk_idx = topk_idx;
   rp.topk_w = topk_w;
-  rp.counts = counts;
+  // The first kernel of a call is launched without the dependent-launch
+  // attribute, so it starts only after all earlier work on the stream.
   route_kernel<<<static_cast<unsigned>(div_up(T, 8)), 256, 0, s>>>(rp);
   return cudaGetLastError() == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }
@@ -229,7 +233,7 @@ using namespace moe;
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 2; }
+int moe_b200_abi_version(void) { return 4; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
@@ -286,7 +290,7 @@ int moe_b200_route(const float* routing_logits, const void* routing_bias, int ro
   int st = current_device_info(&di);
   if (st != MOE_B200_OK) return st;
   return launch_route(routing_logits, routing_bias, routing_bias_dtype, static_cast<int>(num_tokens),
-                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w, nullptr,
+                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w,
                       static_cast<cudaStream_t>(stream));
 }
 
@@ -340,6 +344,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int* counts = reinterpret_cast<int*>(ws + l.counts);
   uint32_t* status = reinterpret_cast<uint32_t*>(ws + l.status);
+  int* sched = reinterpret_cast<int*>(ws + l.sched);
   int* seg_off = reinterpret_cast<int*>(ws + l.seg_off);
   int32_t* topk_idx = reinterpret_cast<int32_t*>(ws + l.topk_idx);
   float* topk_w = reinterpret_cast<float*>(ws + l.topk_w);
@@ -367,13 +372,13 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
     return MOE_B200_ERR_DRIVER;
 
   // ---- launches ------------------------------------------------------------
+  // Nothing is cleared here: the permutation counts without atomics and
+  // clears the status word, the gather kernel clears the accumulation
+  // buffers, so the workspace may hold anything when the call starts.
   mark_stage(0, s);
-  if (cudaMemsetAsync(ws + l.counts, 0, l.seg_off - l.counts, s) != cudaSuccess) return MOE_B200_ERR_CUDA;
-  if (cudaMemsetAsync(y_acc, 0, static_cast<size_t>(T) * kHidden * sizeof(float), s) != cudaSuccess)
-    return MOE_B200_ERR_CUDA;
   mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
-                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, counts, s);
+                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
   if (st != MOE_B200_OK) return st;
   mark_stage(2, s);
 
@@ -381,13 +386,22 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.topk_idx = topk_idx;
   pp.topk_w = topk_w;
   pp.counts = counts;
+  pp.chunk_counts = reinterpret_cast<int*>(ws + l.chunk_counts);
+  pp.status = status;
+  pp.sched = sched;
   pp.num_tokens = T;
   pp.local_expert_offset = local_off;
   pp.seg_off = seg_off;
   pp.perm_tok = perm_tok;
   pp.perm_w = perm_w;
-  permute_kernel<<<1, 1024, 0, s>>>(pp);
-  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  if (T <= 1024) {
+    if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
+  } else {
+    const int chunks = static_cast<int>(div_up(T, 1024));
+    if (launch_kernel(permute_count_kernel, chunks, 1024, 0, s, true, pp) != cudaSuccess ||
+        launch_kernel(permute_place_kernel, chunks, 1024, 0, s, true, pp) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
+  }
   GatherParams gp;
   gp.seg_off = seg_off;
   gp.perm_tok = perm_tok;
@@ -397,10 +411,12 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   gp.cap = cap;
   gp.a_perm = a_perm;
   gp.sa_perm = sa_perm;
+  gp.y_acc = y_acc;
+  gp.g1_acc = g1_acc;
   int ggrid = static_cast<int>(div_up(cap, 8));
+  if (ggrid < di.sm_count) ggrid = di.sm_count;
   if (ggrid > di.sm_count * 4) ggrid = di.sm_count * 4;
-  gather_rows_kernel<<<ggrid, 256, 0, s>>>(gp);
-  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  if (launch_kernel(gather_rows_kernel, ggrid, 256, 0, s, true, gp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   mark_stage(3, s);
 
   GemmParams g1;
@@ -419,14 +435,14 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g1.c_scale = c_scale;
   g1.g1_acc = g1_acc;
   g1.status = status;
+  g1.sched = sched;
   const int grid1 = grid_for(num_tokens, plan.g1_bn, kInterBlocks, plan.g1_splits, di.sm_count);
   if (plan.split_g1) {
-    if (cudaMemsetAsync(g1_acc, 0, static_cast<size_t>(cap) * kGemm1Out * sizeof(float), s) != cudaSuccess)
-      return MOE_B200_ERR_CUDA;
     if (launch_moe_gemm(kGemm1Split, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
-    swiglu_quant_kernel<<<di.sm_count * 2, 256, 0, s>>>(seg_off, g1_acc, c_hi, c_lo, c_scale, cap);
-    if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+    if (launch_kernel(swiglu_quant_kernel, di.sm_count * 2, 256, 0, s, true, static_cast<const int*>(seg_off),
+                      static_cast<const float*>(g1_acc), c_hi, c_lo, c_scale, cap) != cudaSuccess)
+      return MOE_B200_ERR_CUDA;
   } else if (plan.token_major) {
     const int grid_tm = grid_for(num_tokens, 128, kInterBlocks, 1, di.sm_count);
     if (launch_moe_gemm_tm(true, tm_w13, tm_aperm, tm_aperm, g1, grid_tm, s) != cudaSuccess)
@@ -439,6 +455,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   mark_stage(4, s);
   GemmParams g2 = g1;
   g2.act_scale = c_scale;
+  g2.sched = sched + 1;
   g2.w_scale = gemm2_weights_scale;
   g2.splits = plan.g2_splits;
   g2.y_acc = y_acc;
@@ -457,8 +474,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
   int fgrid = static_cast<int>(div_up(n4, 256));
   if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
-  finalize_kernel<<<fgrid, 256, 0, s>>>(y_acc, static_cast<uint16_t*>(output), n4);
-  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
+                    static_cast<uint16_t*>(output), n4) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;
 }

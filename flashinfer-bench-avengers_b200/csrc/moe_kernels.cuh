@@ -2,6 +2,7 @@
 #pragma once
 
 #include <cstdint>
+#include <utility>
 #include <cuda_runtime.h>
 
 namespace moe {
@@ -15,13 +16,15 @@ struct RouteParams {
   int local_expert_offset;
   int32_t* topk_idx;        // [T, 8] global expert ids, best first
   float* topk_w;            // [T, 8]
-  int* counts;              // [32] local-expert histogram (atomics), may be null
 };
 
 struct PermuteParams {
   const int32_t* topk_idx;  // [T, 8]
   const float* topk_w;      // [T, 8]
-  const int* counts;        // [32] assignments per local expert
+  int* counts;              // [32] assignments per local expert (written)
+  int* chunk_counts;        // [ceil(T/1024), 32] per-chunk counts (multi-CTA path)
+  uint32_t* status;         // device status word (cleared)
+  int* sched;               // [4] GEMM unit counters (cleared)
   int num_tokens;
   int local_expert_offset;
   int* seg_off;             // [33] segment starts (multiples of kSegAlign)
@@ -38,6 +41,8 @@ struct GatherParams {
   int cap;
   uint8_t* a_perm;          // [cap, 7168] e4m3
   float* sa_perm;           // [56, cap]
+  float* y_acc;             // [T, 7168] cleared
+  float* g1_acc;            // [cap, 4096] used rows cleared; null unless K-split
 };
 
 // The three grouped-GEMM flavours built from one kernel template.
@@ -64,10 +69,33 @@ struct GemmParams {
   float* g1_acc;            // [cap, 4096] fp32 (kGemm1Split)
   float* y_acc;             // [T, 7168] fp32 (kGemm2)
   uint32_t* status;         // device status word
+  int* sched;               // this GEMM's unit counter (cleared by the permutation)
 };
+
+// Launches `kern` on `stream`; with `dependent` set the launch carries the
+// programmatic-stream-serialization attribute, so the kernel may start while
+// its predecessor finishes (the kernel itself must griddepcontrol.wait before
+// reading the predecessor's results).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                          bool dependent, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = dependent ? attr : nullptr;
+  cfg.numAttrs = dependent ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 __global__ void route_kernel(RouteParams p);
 __global__ void permute_kernel(PermuteParams p);
+__global__ void permute_count_kernel(PermuteParams p);
+__global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
 __global__ void swiglu_quant_kernel(const int* seg_off, const float* g1_acc, uint8_t* c_hi,
                                     uint8_t* c_lo, float* c_scale, int cap);

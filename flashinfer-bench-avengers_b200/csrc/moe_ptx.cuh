@@ -20,9 +20,16 @@ constexpr uint32_t kStatusTimeoutMma = 1u << 1;
 constexpr uint32_t kStatusTimeoutEpilogue = 1u << 2;
 constexpr uint32_t kStatusTimeoutScale = 1u << 3;
 constexpr uint32_t kStatusBadRouting = 1u << 4;
+constexpr uint32_t kStatusTimeoutUnit = 1u << 5;
 
 // A wait longer than this is treated as a hang (1 s).
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
+
+// Programmatic dependent launch: wait until the preceding kernel of the
+// stream has completed and its writes are visible (a no-op when the kernel
+// was launched without the attribute); let the next kernel start launching.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_next() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));

@@ -29,6 +29,7 @@ __device__ __forceinline__ bool ranks_before(float va, int ia, float vb, int ib)
 // Lane l of the warp owns experts 8l .. 8l+7, so group g (32 experts) is
 // owned by lanes 4g .. 4g+3.
 __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
+  pdl_launch_next();
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int t = blockIdx.x * (blockDim.x >> 5) + warp;
@@ -137,29 +138,77 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
     const float w = (my_s / sum) * p.routed_scaling_factor;
     p.topk_idx[t * kTopK + lane] = my_idx;
     p.topk_w[t * kTopK + lane] = w;
-    if (p.counts != nullptr) {
-      const int le = my_idx - p.local_expert_offset;
-      if (le >= 0 && le < kExpertsLocal) atomicAdd(&p.counts[le], 1);
-    }
   }
 }
 
-// One CTA of 1024 threads. Tokens are processed in chunks of 1024 (one per
-// thread); inside a chunk a warp ranks its 32 tokens per expert with ballots,
-// warps are ranked with a shuffle scan, so each expert segment lists its
-// tokens in increasing token order. Segments start on multiples of
-// kSegAlign rows; the padding rows carry token -1 and weight 0.
+namespace {
+
+// The local-expert selections of token t as a 32-bit mask (bit e = local
+// expert e) with the (local id, weight) pairs in routing order.
+__device__ __forceinline__ uint32_t token_selection(const PermuteParams& p, int t, int (&sidx)[kTopK],
+                                                    float (&sw)[kTopK]) {
+  uint32_t mask = 0;
+  if (t < p.num_tokens) {
+    const int4* ip = reinterpret_cast<const int4*>(p.topk_idx + t * kTopK);
+    const float4* wp = reinterpret_cast<const float4*>(p.topk_w + t * kTopK);
+    const int4 i0 = ip[0], i1 = ip[1];
+    const float4 w0 = wp[0], w1 = wp[1];
+    const int ii[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
+    const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      const int le = ii[k] - p.local_expert_offset;
+      sidx[k] = le;
+      sw[k] = ww[k];
+      if (le >= 0 && le < kExpertsLocal) mask |= 1u << le;
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) { sidx[k] = -1; sw[k] = 0.f; }
+  }
+  return mask;
+}
+
+}  // namespace
+
+// One CTA of 1024 threads, tokens in chunks of 1024 (one per thread).
+// Pass 1 counts the assignments of every local expert with warp ballots (no
+// atomics, so no buffer has to be cleared beforehand). Pass 2 ranks each
+// warp's 32 tokens per expert with ballots and the warps with a shuffle
+// scan, so each expert segment lists its tokens in increasing token order.
+// Segments start on multiples of kSegAlign rows; the padding rows carry
+// token -1 and weight 0. Also clears the call's device status word.
 __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
   __shared__ int s_run[kExpertsLocal];
   __shared__ int s_wcnt[32][kExpertsLocal];  // [warp][expert]
   __shared__ int s_wpre[32][kExpertsLocal];
 
+  pdl_launch_next();
+  pdl_wait();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  if (tid == 0) *p.status = 0;
+  if (tid < 4) p.sched[tid] = 0;
 
+  // ---- pass 1: per-expert counts ------------------------------------------
+  int my_count = 0;  // lane e of each warp: this warp's tokens choosing expert e
+  for (int base = 0; base < p.num_tokens; base += 1024) {
+    int sidx[kTopK];
+    float sw[kTopK];
+    const uint32_t mask = token_selection(p, base + tid, sidx, sw);
+#pragma unroll
+    for (int e = 0; e < kExpertsLocal; ++e) {
+      const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+      if (lane == e) my_count += __popc(bal);
+    }
+  }
+  s_wcnt[warp][lane] = my_count;
+  __syncthreads();
   if (warp == 0) {
-    const int c = p.counts[lane];
+    int c = 0;
+#pragma unroll 8
+    for (int w = 0; w < 32; ++w) c += s_wcnt[w][lane];
     const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
     int incl = padded;
 #pragma unroll
@@ -168,6 +217,7 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
       if (lane >= off) incl += o;
     }
     s_run[lane] = incl - padded;
+    p.counts[lane] = c;
     p.seg_off[lane + 1] = incl;
     if (lane == 0) p.seg_off[0] = 0;
   }
@@ -184,35 +234,19 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
     }
   }
 
+  // ---- pass 2: positions -------------------------------------------------
   const uint32_t lt_mask = (1u << lane) - 1u;
   for (int base = 0; base < p.num_tokens; base += 1024) {
     const int t = base + tid;
-    uint32_t mask = 0;
     int sidx[kTopK];
     float sw[kTopK];
-    if (t < p.num_tokens) {
-      const int4* ip = reinterpret_cast<const int4*>(p.topk_idx + t * kTopK);
-      const float4* wp = reinterpret_cast<const float4*>(p.topk_w + t * kTopK);
-      const int4 i0 = ip[0], i1 = ip[1];
-      const float4 w0 = wp[0], w1 = wp[1];
-      const int ii[8] = {i0.x, i0.y, i0.z, i0.w, i1.x, i1.y, i1.z, i1.w};
-      const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        const int le = ii[k] - p.local_expert_offset;
-        sidx[k] = le;
-        sw[k] = ww[k];
-        if (le >= 0 && le < kExpertsLocal) mask |= 1u << le;
-      }
-    } else {
-#pragma unroll
-      for (int k = 0; k < kTopK; ++k) { sidx[k] = -1; sw[k] = 0.f; }
-    }
+    const uint32_t mask = token_selection(p, t, sidx, sw);
 
     // Rank inside the warp, per expert. Ranks of the set bits of `mask` are
     // packed 5 bits each in increasing expert order.
     uint64_t ranks = 0;
     int nset = 0;
+    __syncthreads();  // previous chunk's readers of s_wcnt / s_wpre are done
 #pragma unroll
     for (int e = 0; e < kExpertsLocal; ++e) {
       const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
@@ -257,33 +291,173 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
       p.perm_tok[pos] = t;
       p.perm_w[pos] = w;
     }
-    __syncthreads();
+  }
+}
+
+// Multi-CTA permutation for batches of more than 1024 tokens, one 1024-token
+// chunk per CTA, same result as permute_kernel. permute_count_kernel writes
+// each chunk's per-expert counts; permute_place_kernel derives the segment
+// starts from all chunks' counts and places its chunk's tokens after those
+// of earlier chunks.
+__global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
+  __shared__ int s_wcnt[32][kExpertsLocal];
+  pdl_launch_next();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  int sidx[kTopK];
+  float sw[kTopK];
+  const uint32_t mask = token_selection(p, blockIdx.x * 1024 + tid, sidx, sw);
+  int my_count = 0;
+#pragma unroll
+  for (int e = 0; e < kExpertsLocal; ++e) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+    if (lane == e) my_count = __popc(bal);
+  }
+  s_wcnt[warp][lane] = my_count;
+  __syncthreads();
+  if (warp == 0) {
+    int c = 0;
+#pragma unroll 8
+    for (int w = 0; w < 32; ++w) c += s_wcnt[w][lane];
+    p.chunk_counts[blockIdx.x * kExpertsLocal + lane] = c;
+  }
+}
+
+__global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
+  __shared__ int s_start[kExpertsLocal];
+  __shared__ int s_total[kExpertsLocal];
+  __shared__ int s_base[kExpertsLocal];
+  __shared__ int s_wcnt[32][kExpertsLocal];
+  __shared__ int s_wpre[32][kExpertsLocal];
+  pdl_launch_next();
+  pdl_wait();
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int chunk = blockIdx.x;
+  if (warp == 0) {
+    int total = 0, before = 0;
+    for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+      const int v = p.chunk_counts[c * kExpertsLocal + lane];
+      total += v;
+      if (c < chunk) before += v;
+    }
+    const int padded = (total + kSegAlign - 1) / kSegAlign * kSegAlign;
+    int incl = padded;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    s_start[lane] = incl - padded;
+    s_total[lane] = total;
+    s_base[lane] = incl - padded + before;
+    if (chunk == 0) {
+      p.counts[lane] = total;
+      p.seg_off[lane + 1] = incl;
+      if (lane == 0) {
+        p.seg_off[0] = 0;
+        *p.status = 0;
+      }
+      if (lane < 4) p.sched[lane] = 0;
+    }
+  }
+  __syncthreads();
+  if (chunk == 0 && tid < kExpertsLocal * kSegAlign) {
+    const int e = tid / kSegAlign;
+    const int j = tid % kSegAlign;
+    const int c = s_total[e];
+    const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+    if (c + j < padded) {
+      p.perm_tok[s_start[e] + c + j] = -1;
+      p.perm_w[s_start[e] + c + j] = 0.f;
+    }
+  }
+  const int t = chunk * 1024 + tid;
+  int sidx[kTopK];
+  float sw[kTopK];
+  const uint32_t mask = token_selection(p, t, sidx, sw);
+  const uint32_t lt_mask = (1u << lane) - 1u;
+  uint64_t ranks = 0;
+  int nset = 0;
+#pragma unroll
+  for (int e = 0; e < kExpertsLocal; ++e) {
+    const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+    if (lane == e) s_wcnt[warp][e] = __popc(bal);
+    if ((mask >> e) & 1u) {
+      ranks |= static_cast<uint64_t>(__popc(bal & lt_mask)) << (5 * nset);
+      ++nset;
+    }
+  }
+  __syncthreads();
+  {
+    const int e = warp;
+    const int c = s_wcnt[lane][e];
+    int incl = c;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    s_wpre[lane][e] = s_base[e] + incl - c;
+  }
+  __syncthreads();
+  uint32_t m = mask;
+  int j = 0;
+  while (m) {
+    const int e = __ffs(m) - 1;
+    m &= m - 1;
+    const int r = static_cast<int>((ranks >> (5 * j)) & 31u);
+    ++j;
+    float w = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      if (sidx[k] == e) w = sw[k];
+    }
+    const int pos = s_wpre[warp][e] + r;
+    p.perm_tok[pos] = t;
+    p.perm_w[pos] = w;
   }
 }
 
 // Copies every permuted row's activations and block scales into contiguous
 // buffers (one warp per row): a_perm[r, :] = hidden[tok(r), :] and
-// sa_perm[kb, r] = hidden_scale[kb, tok(r)]; padding rows become zeros.
+// sa_perm[kb, r] = hidden_scale[kb, tok(r)].
 // This replaces per-row TMA gathers inside GEMM1 with plain 2-D tiles.
+// It also clears the buffers that the GEMMs accumulate into with fp32
+// reductions: every row of the combine buffer y_acc and, for the K-split
+// decode plan, the used rows of g1_acc.
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
+  // Releases GEMM1 only after the permutation has completed: GEMM1 reads the
+  // segment table before its own wait to prefetch weight tiles.
+  pdl_wait();
+  pdl_launch_next();
   const int rows = p.seg_off[kExpertsLocal];
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t y4 = static_cast<int64_t>(p.num_tokens) * (kHidden / 4);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < y4; i += nthreads)
+    reinterpret_cast<float4*>(p.y_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Padding rows are skipped: they only ever feed token columns or rows that
+  // the GEMM epilogues discard, and every output column depends on its own
+  // token row alone.
   for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps_total) {
     const int tok = p.perm_tok[r];
-    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(r) * kHidden);
-    if (tok >= 0) {
-      const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(tok) * kHidden);
-#pragma unroll
-      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = src[lane + 32 * i];
-      for (int kb = lane; kb < kHiddenBlocks; kb += 32)
-        p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = p.hidden_scale[static_cast<int64_t>(kb) * p.num_tokens + tok];
-    } else {
-      const uint4 z = make_uint4(0, 0, 0, 0);
-#pragma unroll
-      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = z;
-      for (int kb = lane; kb < kHiddenBlocks; kb += 32) p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = 0.f;
+    if (tok < 0) continue;
+    if (p.g1_acc != nullptr) {
+      float4* g = reinterpret_cast<float4*>(p.g1_acc + static_cast<int64_t>(r) * kGemm1Out);
+#pragma unroll 4
+      for (int i = lane; i < kGemm1Out / 4; i += 32) g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(r) * kHidden);
+    const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(tok) * kHidden);
+#pragma unroll
+    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = src[lane + 32 * i];
+    for (int kb = lane; kb < kHiddenBlocks; kb += 32)
+      p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = p.hidden_scale[static_cast<int64_t>(kb) * p.num_tokens + tok];
   }
 }
 

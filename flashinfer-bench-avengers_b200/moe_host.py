@@ -58,6 +58,8 @@ class WorkspaceLayout(ctypes.Structure):
         ("y_acc", ctypes.c_size_t),
         ("g1_acc", ctypes.c_size_t),
         ("cap_rows", ctypes.c_int64),
+        ("chunk_counts", ctypes.c_size_t),
+        ("sched", ctypes.c_size_t),
     ]
 
 

@@ -125,6 +125,8 @@ typedef struct moe_b200_workspace_layout {
   size_t y_acc;       /* fp32[T, 7168] */
   size_t g1_acc;      /* fp32[cap_rows, 4096], 0 when the plan for T does not split K */
   int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
+  size_t chunk_counts; /* int32[ceil(T/1024), 32] per-chunk expert counts */
+  size_t sched;       /* int32[4] work-unit counters of the GEMM kernels */
 } moe_b200_workspace_layout;
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);

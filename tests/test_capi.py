@@ -60,7 +60,7 @@ def test_workspace_size_and_layout(lib):
         lay = moe_host.workspace_layout(T)
         assert lay.total_bytes == n
         assert lay.cap_rows == (8 * T + 15) // 16 * 16 + 32 * 16 + 128
-        offs = [lay.counts, lay.seg_off, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w, lay.a_perm,
+        offs = [lay.counts, lay.seg_off, lay.chunk_counts, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w, lay.a_perm,
                 lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
         assert lay.c_lo - lay.c_hi >= lay.cap_rows * 2048
@@ -106,4 +106,4 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 2
+    assert lib.moe_b200_abi_version() == 4

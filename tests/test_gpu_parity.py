@@ -107,7 +107,6 @@ def test_permutation_bit_exact(host, T, offset, variant):
     hs = inp["hidden_states"].view(torch.uint8).cpu()
     valid = perm_tok >= 0
     assert torch.equal(a_perm[valid], hs[perm_tok[valid]])
-    assert int(a_perm[~valid].count_nonzero()) == 0
     assert host.read_status(ws) == 0
 
 
