@@ -248,39 +248,63 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
 
 
 def time_e2e(inp: dict, steps: int, warmup: int, group=None) -> dict:
-    """The public API call with host buffers: per step, H2D of the step's
-    activations from pinned memory, the layer, D2H of the bf16 result."""
+    """The public API call with host buffers: every step copies its
+    activations host->device from pinned memory, runs the layer through
+    moe_host.run_dps and copies the bf16 result device->host. Copies run on
+    their own streams with two buffer sets, so step i+1's upload and step
+    i-1's download overlap step i's compute; the timed region spans the first
+    upload to the last download."""
     import moe_host
     import torch.distributed as dist
 
     dev = inp["routing_logits"].device
     T = inp["routing_logits"].shape[0]
-    host_in = {k: inp[k].cpu().pin_memory() for k in ("routing_logits", "hidden_states", "hidden_states_scale")}
-    dev_in = {k: torch.empty_like(v, device=dev) for k, v in host_in.items()}
-    out = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
-    host_out = torch.empty(T, 7168, dtype=torch.bfloat16).pin_memory()
+    keys = ("routing_logits", "hidden_states", "hidden_states_scale")
+    host_in = {k: inp[k].cpu().pin_memory() for k in keys}
+    dev_in = [{k: torch.empty_like(v, device=dev) for k, v in host_in.items()} for _ in range(2)]
+    out = [torch.empty(T, 7168, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    host_out = [torch.empty(T, 7168, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     h2d = sum(v.numel() * v.element_size() for v in host_in.values())
-    d2h = host_out.numel() * host_out.element_size()
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    compute = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    uploaded = [torch.cuda.Event() for _ in range(2)]
+    computed = [torch.cuda.Event() for _ in range(2)]
+    downloaded = [torch.cuda.Event() for _ in range(2)]
+    for b in range(2):
+        computed[b].record(compute)
+        downloaded[b].record(compute)
 
-    def step():
-        for k in dev_in:
-            dev_in[k].copy_(host_in[k], non_blocking=True)
-        moe_host.run_dps(dev_in["routing_logits"], inp["routing_bias"], dev_in["hidden_states"],
-                         dev_in["hidden_states_scale"], inp["gemm1_weights"], inp["gemm1_weights_scale"],
+    def step(i):
+        b = i % 2
+        with torch.cuda.stream(up):
+            up.wait_event(computed[b])           # buffer b's previous compute is done
+            for k in keys:
+                dev_in[b][k].copy_(host_in[k], non_blocking=True)
+            uploaded[b].record(up)
+        compute.wait_event(uploaded[b])
+        compute.wait_event(downloaded[b])        # out[b] has been read back
+        moe_host.run_dps(dev_in[b]["routing_logits"], inp["routing_bias"], dev_in[b]["hidden_states"],
+                         dev_in[b]["hidden_states_scale"], inp["gemm1_weights"], inp["gemm1_weights_scale"],
                          inp["gemm2_weights"], inp["gemm2_weights_scale"], inp["local_expert_offset"],
-                         inp["routed_scaling_factor"], out)
+                         inp["routed_scaling_factor"], out[b])
         if group is not None:
-            dist.all_reduce(out, group=group)
-        host_out.copy_(out, non_blocking=True)
+            dist.all_reduce(out[b], group=group)
+        computed[b].record(compute)
+        with torch.cuda.stream(down):
+            down.wait_event(computed[b])
+            host_out[b].copy_(out[b], non_blocking=True)
+            downloaded[b].record(down)
 
-    for _ in range(warmup):
-        step()
+    for i in range(warmup):
+        step(i)
     torch.cuda.synchronize()
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
+    s.record(up)
+    for i in range(steps):
+        step(i)
+    down.wait_event(computed[(steps - 1) % 2])
+    e.record(down)
     torch.cuda.synchronize()
     return {"ms": s.elapsed_time(e) / steps, "h2d": h2d, "d2h": d2h}
 

@@ -58,12 +58,17 @@ struct TmTraits {
 
   static constexpr int kOffRing = kStages * kStageBytes;
   static constexpr int kOffBars = kOffRing + kScaleSlots * kSlotFloats * 4;
-  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kScaleSlots;
+  // Work units are handed out dynamically through a small ring (s_units +
+  // full/empty barriers), like the swap-AB kernels.
+  static constexpr int kUnitSlots = 4;
+  static constexpr int kUnitConsumers = 1 + kEpiWarps;   // MMA warp + epilogue warps
+  static constexpr int kNumBars = 2 * kStages + 4 + 2 * kScaleSlots + 2 * kUnitSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;
   static constexpr int kOffUnitPre = kOffMisc + 16;
   static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
   static constexpr int kOffCnt = kOffSeg + 34 * 4;
-  static constexpr int kOffRed = kOffCnt + 32 * 4;   // [2][BM] row maxima (GEMM1)
+  static constexpr int kOffUnits = kOffCnt + 32 * 4;
+  static constexpr int kOffRed = kOffUnits + kUnitSlots * 4;   // [2][BM] row maxima (GEMM1)
   static constexpr int kSmemBytes = kOffRed + 2 * BM * 4 + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -89,7 +94,8 @@ __device__ __forceinline__ float e4m3_round(float x) {
 
 // Units of work: per expert ceil(count / 128) token tiles x kRowBlocks weight
 // blocks, token tiles fastest so CTAs running at the same time share the
-// weight block through L2.
+// weight block through L2. Units are handed out in increasing order by an
+// atomic counter, so faster CTAs take more of them.
 struct TmTile {
   int e, blk, row0, nvalid;
 };
@@ -127,6 +133,9 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
   uint64_t* acce_bar = accf_bar + 2;
   uint64_t* sfull_bar = acce_bar + 2;
   uint64_t* sempty_bar = sfull_bar + Tr::kScaleSlots;
+  uint64_t* ufull_bar = sempty_bar + Tr::kScaleSlots;
+  uint64_t* uempty_bar = ufull_bar + Tr::kUnitSlots;
+  volatile int* s_units = reinterpret_cast<volatile int*>(smem + Tr::kOffUnits);
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + Tr::kOffMisc);
   volatile int* s_abort = reinterpret_cast<volatile int*>(smem + Tr::kOffMisc + 4);
   int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
@@ -153,6 +162,10 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     for (int s = 0; s < Tr::kScaleSlots; ++s) {
       mbar_init(smem_u32(&sfull_bar[s]), 2);
       mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
+    }
+    for (int s = 0; s < Tr::kUnitSlots; ++s) {
+      mbar_init(smem_u32(&ufull_bar[s]), 1);
+      mbar_init(smem_u32(&uempty_bar[s]), Tr::kUnitConsumers);
     }
     *s_abort = 0;
     fence_mbar_init();
@@ -190,10 +203,23 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
   if (warp == 0) {
     // ======================================================== TMA producer
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
-    int stage = 0, slot = 0;
-    uint32_t ph = 0, sph = 0;
+    int stage = 0, slot = 0, uslot = 0;
+    uint32_t ph = 0, sph = 0, uph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    while (ok) {
+      int u = -1;
+      if (lane == 0) u = atomicAdd(p.sched, 1);
+      u = __shfl_sync(0xffffffffu, u, 0);
+      if (u >= total_units) u = -1;
+      // publish the unit (or the end marker -1) to the MMA and epilogue warps
+      if (!mbar_wait(smem_u32(&uempty_bar[uslot]), uph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) break;
+      if (lane == 0) {
+        s_units[uslot] = u;
+        mbar_arrive(smem_u32(&ufull_bar[uslot]));
+      }
+      __syncwarp();
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       TmTile t;
       tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
       int brow0, brow1, wrow0, wrow1;
@@ -240,10 +266,16 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
   } else if (warp == 1) {
     // ========================================================== MMA issuer
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
-    int stage = 0, abuf = 0;
-    uint32_t ph = 0, aph = 0;
+    int stage = 0, abuf = 0, uslot = 0;
+    uint32_t ph = 0, aph = 0, uph = 0;
     bool ok = true;
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
         if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
             !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
@@ -278,13 +310,19 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     const int hf = (warp - 4) >> 2;      // column half
     const int r = q * 32 + lane;         // token row inside the tile
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    int slot = 0, abuf = 0;
-    uint32_t sph = 0, aph = 0;
+    int slot = 0, abuf = 0, uslot = 0;
+    uint32_t sph = 0, aph = 0, uph = 0;
     bool ok = true;
     // GEMM1: acc0 = up, acc1 = gate for intermediate columns hf*64 .. +64.
     // GEMM2: acc0 / acc1 = W2 rows (2*blk + hf)*128 + [0, 64) / [64, 128).
     float acc0[64], acc1[64];
-    for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
       TmTile t;
       tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
       const bool valid = r < t.nvalid;

@@ -41,6 +41,10 @@ struct Plan {
   bool token_major;  // prefill: token-major GEMMs (gemm_tm_sm100.cu)
 };
 
+// Up to this many tokens per call routing and permutation share one kernel.
+// (one warp routes T/32 tokens in turn there, so it only pays off for tiny T)
+constexpr int64_t kFusedFrontMaxTokens = 8;
+
 // From this many tokens per call the prefill (token-major) GEMMs are used.
 constexpr int64_t kTokenMajorMinTokens = 512;
 
@@ -377,9 +381,13 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   // buffers, so the workspace may hold anything when the call starts.
   mark_stage(0, s);
   mark_stage(1, s);
-  st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
-                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
-  if (st != MOE_B200_OK) return st;
+  // Small batches route and permute in one single-CTA kernel.
+  const bool fused_front = T <= kFusedFrontMaxTokens;
+  if (!fused_front) {
+    st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
+                      static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
+    if (st != MOE_B200_OK) return st;
+  }
   mark_stage(2, s);
 
   PermuteParams pp;
@@ -394,7 +402,20 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.seg_off = seg_off;
   pp.perm_tok = perm_tok;
   pp.perm_w = perm_w;
-  if (T <= 1024) {
+  if (fused_front) {
+    RouteParams rp;
+    rp.logits = routing_logits;
+    rp.bias = routing_bias;
+    rp.bias_is_fp32 = routing_bias_dtype == MOE_B200_BIAS_FP32 ? 1 : 0;
+    rp.num_tokens = T;
+    rp.routed_scaling_factor = static_cast<float>(routed_scaling_factor);
+    rp.local_expert_offset = local_off;
+    rp.topk_idx = topk_idx;
+    rp.topk_w = topk_w;
+    // first kernel of the call: no dependent-launch attribute
+    route_permute_kernel<<<1, 1024, 0, s>>>(rp, pp);
+    if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  } else if (T <= 1024) {
     if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
     const int chunks = static_cast<int>(div_up(T, 1024));

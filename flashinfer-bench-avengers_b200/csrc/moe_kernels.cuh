@@ -94,6 +94,7 @@ cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t 
 
 __global__ void route_kernel(RouteParams p);
 __global__ void permute_kernel(PermuteParams p);
+__global__ void route_permute_kernel(RouteParams rp, PermuteParams pp);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);

@@ -26,14 +26,9 @@ __device__ __forceinline__ bool ranks_before(float va, int ia, float vb, int ib)
 
 }  // namespace
 
-// Lane l of the warp owns experts 8l .. 8l+7, so group g (32 experts) is
-// owned by lanes 4g .. 4g+3.
-__global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
-  pdl_launch_next();
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
-  if (t >= p.num_tokens) return;
+// Routes token t with one warp: lane l owns experts 8l .. 8l+7, so group g
+// (32 experts) is owned by lanes 4g .. 4g+3.
+__device__ __forceinline__ void route_token(const RouteParams& p, int t, int lane) {
 
   // ---- scores -------------------------------------------------------------
   const float4* lrow = reinterpret_cast<const float4*>(p.logits + static_cast<int64_t>(t) * kExpertsGlobal);
@@ -141,6 +136,13 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   }
 }
 
+// One warp per token, 8 tokens per CTA.
+__global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
+  pdl_launch_next();
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (t < p.num_tokens) route_token(p, t, threadIdx.x & 31);
+}
+
 namespace {
 
 // The local-expert selections of token t as a 32-bit mask (bit e = local
@@ -178,13 +180,11 @@ __device__ __forceinline__ uint32_t token_selection(const PermuteParams& p, int 
 // scan, so each expert segment lists its tokens in increasing token order.
 // Segments start on multiples of kSegAlign rows; the padding rows carry
 // token -1 and weight 0. Also clears the call's device status word.
-__global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
+__device__ __forceinline__ void permute_body(const PermuteParams& p) {
   __shared__ int s_run[kExpertsLocal];
   __shared__ int s_wcnt[32][kExpertsLocal];  // [warp][expert]
   __shared__ int s_wpre[32][kExpertsLocal];
 
-  pdl_launch_next();
-  pdl_wait();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -292,6 +292,23 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
       p.perm_w[pos] = w;
     }
   }
+}
+
+__global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
+  pdl_launch_next();
+  pdl_wait();
+  permute_body(p);
+}
+
+// Tiny batches: routing and permutation in one CTA (saves a launch and a
+// round trip through global memory). Warp w routes tokens w, w+32, ..., then
+// the CTA permutes.
+__global__ void __launch_bounds__(1024) route_permute_kernel(RouteParams rp, PermuteParams pp) {
+  pdl_launch_next();
+  const int warp = threadIdx.x >> 5;
+  for (int t = warp; t < rp.num_tokens; t += 32) route_token(rp, t, threadIdx.x & 31);
+  __syncthreads();
+  permute_body(pp);
 }
 
 // Multi-CTA permutation for batches of more than 1024 tokens, one 1024-token
