@@ -695,6 +695,7 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
   X(kGemm1Split, 16, 6, 4)             \
   X(kGemm2, 128, 4, 8)                 \
   X(kGemm2Wide, 128, 3, 8)             \
+  X(kGemm2Wide, 16, 6, 4)              \
   X(kGemm2, 64, 6, 4)                  \
   X(kGemm2, 16, 10, 4)
 

@@ -56,6 +56,9 @@ Plan choose_plan(int64_t T) {
     p.g1_splits = 8;
     p.g2_bn = 16;
     p.g2_splits = 2;
+    // Two W2 blocks per tile: the weight bytes in flight per SM (six 32 KB
+    // stages) match GEMM1's, which is what sets the streaming rate here.
+    p.g2_wide = true;
   } else {
     p.split_g1 = false;
     p.g1_bn = T >= 1024 ? 128 : 64;
