@@ -1,6 +1,6 @@
 // Element-wise kernels around the grouped GEMMs.
 //
-// swiglu_quant_kernel   decode path only: after a K-split GEMM1 has summed
+// swiglu_quant_kernel   decode path only: after the K-split GEMM1 has summed
 //                       its slices into fp32, apply C = silu(gate) * up
 //                       (solution/cuda/kernel.h:207 semantics) and write the
 //                       hi/lo e4m3 pair with one scale per (row, 128-block).

@@ -181,11 +181,55 @@ __device__ __forceinline__ float silu_mul(float gate, float up) {
   return gate / (1.0f + expf(-gate)) * up;
 }
 
+// GEMM1 final epilogue: h = silu(gate) * up for the 128 intermediate columns
+// of block t.blk (one per epilogue thread row) and the token columns
+// col0 .. col0+CPT of this thread, written as the e4m3 pair C = s * (hi + lo)
+// with s = amax / 448 per (token row, 128-block). acc0 = up, acc1 = gate;
+// acc0 is overwritten. Every epilogue thread must call it (named barrier 1).
+template <int BN, int CPT>
+__device__ __forceinline__ void swiglu_quant_store(float (&acc0)[CPT], const float (&acc1)[CPT],
+                                                   const Tile& t, int q, int col0, int lane, int et,
+                                                   int row_in_tile, float* s_red, float* s_inv,
+                                                   const GemmParams& p, uint32_t epi_threads) {
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) acc0[c] = silu_mul(acc1[c], acc0[c]);
+  named_bar_sync(1, epi_threads);   // the previous tile's readers of s_red / s_inv are done
+#pragma unroll
+  for (int g = 0; g < (CPT + 31) / 32; ++g) {
+    float v[32];
+#pragma unroll
+    for (int c = 0; c < 32; ++c) v[c] = (g * 32 + c < CPT) ? fabsf(acc0[min(g * 32 + c, CPT - 1)]) : 0.f;
+    const float m = warp_colmax32(v, lane);
+    if (g * 32 + lane < CPT) s_red[q * BN + col0 + g * 32 + lane] = m;
+  }
+  named_bar_sync(1, epi_threads);
+  if (et < BN) {
+    const float amax = fmaxf(fmaxf(s_red[et], s_red[BN + et]), fmaxf(s_red[2 * BN + et], s_red[3 * BN + et]));
+    s_inv[et] = amax > 0.f ? 448.0f / amax : 0.f;
+    if (et < t.nvalid) p.c_scale[static_cast<int64_t>(t.blk) * p.cap + t.row0 + et] = amax * (1.0f / 448.0f);
+  }
+  named_bar_sync(1, epi_threads);
+  const int col = t.blk * kBlk + row_in_tile;
+#pragma unroll
+  for (int c = 0; c < CPT; ++c) {
+    if (col0 + c < t.nvalid) {
+      const float x = acc0[c] * s_inv[col0 + c];
+      const __nv_fp8_e4m3 qh(x);
+      const float r = x - static_cast<float>(qh);
+      const __nv_fp8_e4m3 ql(r);
+      const int64_t off = static_cast<int64_t>(t.row0 + col0 + c) * kInter + col;
+      p.c_hi[off] = qh.__x;
+      p.c_lo[off] = ql.__x;
+    }
+  }
+}
+
 template <int kKind, int BN, int kStages, int kEpiWarps>
 __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_b0,
-                    const __grid_constant__ CUtensorMap tm_b1, const GemmParams p) {
+                    const __grid_constant__ CUtensorMap tm_b1, const GemmParams p,
+                    const int early_tables) {
   using Tr = GemmTraits<kKind, BN, kStages, kEpiWarps>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -230,7 +274,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       mbar_init(smem_u32(&acce_bar[b]), Tr::kEpiWarps);
     }
     for (int s = 0; s < Tr::kScaleSlots; ++s) {
-      mbar_init(smem_u32(&sraw_bar[s]), 2);
+      mbar_init(smem_u32(&sraw_bar[s]), 2);   // bulk copy's expect_tx + one cp.async arrival
       mbar_init(smem_u32(&sfull_bar[s]), 1);
       mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
     }
@@ -247,11 +291,13 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     tmem_relinquish();
   }
   // Everything up to pdl_wait() overlaps the previous kernel's tail
-  // (programmatic dependent launch). The segment table comes from the
-  // permutation, which has completed before this grid is launched (the
-  // kernels between release their dependents only after their own wait), so
-  // it can be read here; the producer also issues the first stages' weight
-  // tiles, which no earlier kernel writes, before waiting.
+  // (programmatic dependent launch). With early_tables the permutation has
+  // completed before this grid is launched (the kernels in between release
+  // their dependents only after their own wait), so the segment table can be
+  // read here and the producer issues the first stages' weight tiles, which
+  // no earlier kernel writes, before waiting. Without it (the decode GEMM1
+  // follows the permutation directly) everything waits first.
+  if (!early_tables) pdl_wait();
   if (warp == 2) {
     // per-expert tile counts -> prefix over experts of the work units
     const int lo = p.seg_off[lane];
@@ -285,7 +331,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     u = __shfl_sync(0xffffffffu, u, 0);
     if (u >= total_units) u = -1;
     int pre_issued = 0;
-    if (u >= 0) {
+    if (u >= 0 && early_tables) {
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
       const int nkb = t.kb1 - t.kb0;
@@ -504,6 +550,15 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     const int et = ew * 32 + lane;            // 0.. inside the epilogue group
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     constexpr uint32_t kEpiThreads = 32 * Tr::kEpiWarps;
+    if constexpr (kKind == kGemm1Split) {
+      // The decode plan clears GEMM2's combine buffer here, spread over all
+      // CTAs while they wait for their first accumulator.
+      const int64_t n4 = static_cast<int64_t>(p.num_tokens) * (kHidden / 4);
+      float4* y4 = reinterpret_cast<float4*>(p.y_acc);
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * kEpiThreads + et; i < n4;
+           i += static_cast<int64_t>(gridDim.x) * kEpiThreads)
+        y4[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     int slot = 0;
     uint32_t sph = 0;
     int abuf = 0;
@@ -585,39 +640,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
 
       // ------------------------------------------------- final epilogue
       if constexpr (kKind == kGemm1Fused) {
-        // h = silu(gate) * up, kept in acc0
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) acc0[c] = silu_mul(acc1[c], acc0[c]);
-        named_bar_sync(1, kEpiThreads);
-#pragma unroll
-        for (int g = 0; g < (CPT + 31) / 32; ++g) {
-          float v[32];
-#pragma unroll
-          for (int c = 0; c < 32; ++c) v[c] = (g * 32 + c < CPT) ? fabsf(acc0[min(g * 32 + c, CPT - 1)]) : 0.f;
-          const float m = warp_colmax32(v, lane);
-          if (g * 32 + lane < CPT) s_red[q * BN + col0 + g * 32 + lane] = m;
-        }
-        named_bar_sync(1, kEpiThreads);
-        if (et < BN) {
-          const float amax = fmaxf(fmaxf(s_red[et], s_red[BN + et]), fmaxf(s_red[2 * BN + et], s_red[3 * BN + et]));
-          s_inv[et] = amax > 0.f ? 448.0f / amax : 0.f;
-          if (et < t.nvalid) p.c_scale[static_cast<int64_t>(t.blk) * p.cap + t.row0 + et] = amax * (1.0f / 448.0f);
-        }
-        named_bar_sync(1, kEpiThreads);
-        const int col = t.blk * kBlk + row_in_tile;
-#pragma unroll
-        for (int c = 0; c < CPT; ++c) {
-          if (col0 + c < t.nvalid) {
-            const float x = acc0[c] * s_inv[col0 + c];
-            const __nv_fp8_e4m3 qh(x);
-            const float r = x - static_cast<float>(qh);
-            const __nv_fp8_e4m3 ql(r);
-            const int64_t off = static_cast<int64_t>(t.row0 + col0 + c) * kInter + col;
-            p.c_hi[off] = qh.__x;
-            p.c_lo[off] = ql.__x;
-          }
-        }
+        swiglu_quant_store<BN, CPT>(acc0, acc1, t, q, col0, lane, et, row_in_tile, s_red, s_inv, p, kEpiThreads);
       } else if constexpr (kKind == kGemm1Split) {
+        // Add this K slice into g1_acc (rows cleared by the decode front end);
+        // swiglu_quant_kernel converts the sums once every slice is in.
         const int col = t.blk * kBlk + row_in_tile;
 #pragma unroll
         for (int c = 0; c < CPT; ++c) {
@@ -666,7 +692,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
 // ---------------------------------------------------------------- launchers
 template <int kKind, int BN, int kStages, int kEpiWarps>
 static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const CUtensorMap& b1,
-                              const GemmParams& p, int grid, cudaStream_t stream) {
+                              const GemmParams& p, int grid, bool early_tables, cudaStream_t stream) {
   using Tr = GemmTraits<kKind, BN, kStages, kEpiWarps>;
   auto kern = moe_gemm_kernel<kKind, BN, kStages, kEpiWarps>;
   static int checked_device = -1;
@@ -686,7 +712,8 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
     }
     checked_device = dev;
   }
-  return launch_kernel(kern, grid, Tr::kThreads, Tr::kSmemBytes, stream, true, w, b0, b1, p);
+  return launch_kernel(kern, grid, Tr::kThreads, Tr::kSmemBytes, stream, true, w, b0, b1, p,
+                       early_tables ? 1 : 0);
 }
 
 #define MOE_GEMM_CONFIGS(X)            \
@@ -701,9 +728,9 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
 
 cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtensorMap& b0,
                             const CUtensorMap& b1, const GemmParams& p, int grid,
-                            cudaStream_t stream) {
+                            bool early_tables, cudaStream_t stream) {
 #define MOE_GEMM_DISPATCH(K, BN_, S, E) \
-  if (kind == K && bn == BN_) return launch_one<K, BN_, S, E>(w, b0, b1, p, grid, stream);
+  if (kind == K && bn == BN_) return launch_one<K, BN_, S, E>(w, b0, b1, p, grid, early_tables, stream);
   MOE_GEMM_CONFIGS(MOE_GEMM_DISPATCH)
 #undef MOE_GEMM_DISPATCH
   return cudaErrorInvalidValue;

@@ -10,10 +10,13 @@ namespace moe {
 
 // Launches one grouped GEMM flavour (GemmKind) with token-tile width `bn`
 // on `grid` persistent CTAs. Returns cudaErrorInvalidValue for an
-// unsupported (kind, bn) pair.
+// unsupported (kind, bn) pair. With `early_tables` the kernel reads the
+// segment table (and issues its first weight tiles) before waiting for its
+// predecessor; that is only correct when the permutation finished before the
+// predecessor released its dependents (every kernel between them waits first).
 cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtensorMap& b0,
                             const CUtensorMap& b1, const GemmParams& p, int grid,
-                            cudaStream_t stream);
+                            bool early_tables, cudaStream_t stream);
 
 bool gemm_config_supported(int kind, int bn);
 

@@ -32,39 +32,29 @@ size_t align_up(size_t x) { return (x + kAlign - 1) / kAlign * kAlign; }
 // Execution plan for one call, a function of T only (so workspace size and
 // launch shapes are known without reading device data).
 struct Plan {
-  bool split_g1;   // decode: K-split GEMM1 + separate SwiGLU
+  bool decode;     // T <= kDecodeMaxTokens: single-CTA front end, stream-K GEMMs
   int g1_bn;
-  int g1_splits;
   int g2_bn;
-  int g2_splits;
   bool g2_wide;    // two W2 row blocks per GEMM2 tile
   bool token_major;  // prefill: token-major GEMMs (gemm_tm_sm100.cu)
 };
-
-// Up to this many tokens per call routing and permutation share one kernel.
-// (one warp routes T/32 tokens in turn there, so it only pays off for tiny T)
-constexpr int64_t kFusedFrontMaxTokens = 8;
 
 // From this many tokens per call the prefill (token-major) GEMMs are used.
 constexpr int64_t kTokenMajorMinTokens = 512;
 
 Plan choose_plan(int64_t T) {
   Plan p{};
-  if (T <= 64) {
-    p.split_g1 = true;
+  if (T <= kDecodeMaxTokens) {
+    // Both GEMMs stream 16-token column groups against 256 weight rows
+    // (six 32 KB weight stages in flight per SM); GEMM1 splits K 8 ways.
+    p.decode = true;
     p.g1_bn = 16;
-    p.g1_splits = 8;
     p.g2_bn = 16;
-    p.g2_splits = 2;
-    // Two W2 blocks per tile: the weight bytes in flight per SM (six 32 KB
-    // stages) match GEMM1's, which is what sets the streaming rate here.
     p.g2_wide = true;
   } else {
-    p.split_g1 = false;
+    p.decode = false;
     p.g1_bn = T >= 1024 ? 128 : 64;
-    p.g1_splits = 1;
     p.g2_bn = T >= 1024 ? 128 : 64;
-    p.g2_splits = 1;
     p.g2_wide = T >= 1024;
     p.token_major = T >= kTokenMajorMinTokens;
   }
@@ -113,7 +103,7 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   off = align_up(off + cap * kInterBlocks * sizeof(float));
   l.y_acc = off;
   off = align_up(off + static_cast<size_t>(T) * kHidden * sizeof(float));
-  if (plan.split_g1) {
+  if (plan.decode) {
     l.g1_acc = off;
     off = align_up(off + cap * kGemm1Out * sizeof(float));
   }
@@ -233,6 +223,127 @@ void mark_stage(int i, cudaStream_t s) {
     cudaEventRecord(t_stage_events[i], s);
 }
 
+// Decode plan (T <= kDecodeMaxTokens): four launches,
+//   route_permute_decode (one 8-CTA cluster: routing, permutation, permuted
+//     row copy, clears of the unit counters and of the g1_acc rows)
+//   -> K-split GEMM1 (red.add into g1_acc; also clears y_acc)
+//   -> swiglu_quant (C = silu(gate) * up as the hi/lo e4m3 pair)
+//   -> GEMM2 (two W2 blocks per tile, K split 2 ways, red.add into y_acc)
+//   -> finalize (bf16).
+int run_decode(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+               const void* hidden_states, const float* hidden_states_scale, const void* gemm1_weights,
+               const float* gemm1_weights_scale, const void* gemm2_weights,
+               const float* gemm2_weights_scale, int local_off, float rsf, int T, void* output,
+               uint8_t* ws, const moe_b200_workspace_layout& l, const DeviceInfo& di, cudaStream_t s) {
+  constexpr int kG1Splits = 8;
+  constexpr int kG2Splits = 2;
+  constexpr int kBN = 16;
+  const int cap = static_cast<int>(l.cap_rows);
+  int* counts = reinterpret_cast<int*>(ws + l.counts);
+  uint32_t* status = reinterpret_cast<uint32_t*>(ws + l.status);
+  int* sched = reinterpret_cast<int*>(ws + l.sched);
+  int* seg_off = reinterpret_cast<int*>(ws + l.seg_off);
+  int32_t* perm_tok = reinterpret_cast<int32_t*>(ws + l.perm_tok);
+  float* perm_w = reinterpret_cast<float*>(ws + l.perm_w);
+  uint8_t* c_hi = ws + l.c_hi;
+  uint8_t* c_lo = ws + l.c_lo;
+  float* c_scale = reinterpret_cast<float*>(ws + l.c_scale);
+  float* y_acc = reinterpret_cast<float*>(ws + l.y_acc);
+  float* g1_acc = reinterpret_cast<float*>(ws + l.g1_acc);
+
+  uint8_t* a_perm = ws + l.a_perm;
+  float* sa_perm = reinterpret_cast<float*>(ws + l.sa_perm);
+  CUtensorMap tm_aperm, tm_w13, tm_w2, tm_chi, tm_clo;
+  if (!encode_u8_2d(&tm_aperm, a_perm, kHidden, cap, 128, kBN) ||
+      !encode_u8_2d(&tm_w13, gemm1_weights, kHidden, static_cast<uint64_t>(kExpertsLocal) * kGemm1Out,
+                    128, 128) ||
+      !encode_u8_2d(&tm_w2, gemm2_weights, kInter, static_cast<uint64_t>(kExpertsLocal) * kHidden, 128,
+                    128) ||
+      !encode_u8_2d(&tm_chi, c_hi, kInter, cap, 128, kBN) ||
+      !encode_u8_2d(&tm_clo, c_lo, kInter, cap, 128, kBN))
+    return MOE_B200_ERR_DRIVER;
+
+  mark_stage(0, s);
+  mark_stage(1, s);
+  RouteParams rp;
+  rp.logits = routing_logits;
+  rp.bias = routing_bias;
+  rp.bias_is_fp32 = routing_bias_dtype == MOE_B200_BIAS_FP32 ? 1 : 0;
+  rp.num_tokens = T;
+  rp.routed_scaling_factor = rsf;
+  rp.local_expert_offset = local_off;
+  rp.topk_idx = reinterpret_cast<int32_t*>(ws + l.topk_idx);
+  rp.topk_w = reinterpret_cast<float*>(ws + l.topk_w);
+  DecodeFrontParams dp;
+  dp.counts = counts;
+  dp.seg_off = seg_off;
+  dp.perm_tok = perm_tok;
+  dp.perm_w = perm_w;
+  dp.status = status;
+  dp.sched = sched;
+  dp.g1_acc = g1_acc;
+  dp.hidden = static_cast<const uint8_t*>(hidden_states);
+  dp.hidden_scale = hidden_states_scale;
+  dp.a_perm = a_perm;
+  dp.sa_perm = sa_perm;
+  dp.cap = cap;
+  dp.local_expert_offset = local_off;
+  // First kernel of the call: no dependent-launch attribute. The cluster
+  // shape is compiled into the kernel.
+  route_permute_decode_kernel<<<kDecodeClusterCtas, 256, 0, s>>>(rp, dp);
+  if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+  mark_stage(2, s);
+  mark_stage(3, s);
+
+  GemmParams g1;
+  std::memset(&g1, 0, sizeof(g1));
+  g1.seg_off = seg_off;
+  g1.counts = counts;
+  g1.perm_tok = perm_tok;
+  g1.perm_w = perm_w;
+  g1.act_scale = sa_perm;
+  g1.w_scale = gemm1_weights_scale;
+  g1.num_tokens = T;
+  g1.cap = cap;
+  g1.splits = kG1Splits;
+  g1.c_hi = c_hi;
+  g1.c_lo = c_lo;
+  g1.c_scale = c_scale;
+  g1.g1_acc = g1_acc;
+  g1.y_acc = y_acc;
+  g1.status = status;
+  g1.sched = sched;
+  // GEMM1 follows the permutation directly, so it must wait before reading
+  // the segment table (no early tables).
+  const int grid1 = grid_for(T, kBN, kInterBlocks, kG1Splits, di.sm_count);
+  if (launch_moe_gemm(kGemm1Split, kBN, tm_w13, tm_aperm, tm_aperm, g1, grid1, false, s) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  if (launch_kernel(swiglu_quant_kernel, di.sm_count * 2, 256, 0, s, true, static_cast<const int*>(seg_off),
+                    static_cast<const float*>(g1_acc), c_hi, c_lo, c_scale, cap) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  mark_stage(4, s);
+
+  GemmParams g2 = g1;
+  g2.act_scale = c_scale;
+  g2.w_scale = gemm2_weights_scale;
+  g2.splits = kG2Splits;
+  g2.sched = sched + 1;
+  g2.g1_acc = nullptr;
+  const int grid2 = grid_for(T, kBN, kHiddenBlocks / 2, kG2Splits, di.sm_count);
+  if (launch_moe_gemm(kGemm2Wide, kBN, tm_w2, tm_chi, tm_clo, g2, grid2, true, s) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  mark_stage(5, s);
+
+  const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
+  int fgrid = static_cast<int>(div_up(n4, 256));
+  if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
+  if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
+                    static_cast<uint16_t*>(output), n4) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  mark_stage(6, s);
+  return MOE_B200_OK;
+}
+
 }  // namespace
 }  // namespace moe
 
@@ -240,7 +351,7 @@ using namespace moe;
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 4; }
+int moe_b200_abi_version(void) { return 5; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
@@ -363,7 +474,11 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   uint8_t* c_lo = ws + l.c_lo;
   float* c_scale = reinterpret_cast<float*>(ws + l.c_scale);
   float* y_acc = reinterpret_cast<float*>(ws + l.y_acc);
-  float* g1_acc = plan.split_g1 ? reinterpret_cast<float*>(ws + l.g1_acc) : nullptr;
+
+  if (plan.decode)
+    return run_decode(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
+                      static_cast<float>(routed_scaling_factor), T, output, ws, l, di, s);
 
   // ---- tensor maps ---------------------------------------------------------
   CUtensorMap tm_aperm, tm_w13, tm_w2, tm_chi, tm_clo;
@@ -384,13 +499,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   // buffers, so the workspace may hold anything when the call starts.
   mark_stage(0, s);
   mark_stage(1, s);
-  // Small batches route and permute in one single-CTA kernel.
-  const bool fused_front = T <= kFusedFrontMaxTokens;
-  if (!fused_front) {
-    st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
-                      static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
-    if (st != MOE_B200_OK) return st;
-  }
+  st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
+                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
+  if (st != MOE_B200_OK) return st;
   mark_stage(2, s);
 
   PermuteParams pp;
@@ -405,20 +516,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.seg_off = seg_off;
   pp.perm_tok = perm_tok;
   pp.perm_w = perm_w;
-  if (fused_front) {
-    RouteParams rp;
-    rp.logits = routing_logits;
-    rp.bias = routing_bias;
-    rp.bias_is_fp32 = routing_bias_dtype == MOE_B200_BIAS_FP32 ? 1 : 0;
-    rp.num_tokens = T;
-    rp.routed_scaling_factor = static_cast<float>(routed_scaling_factor);
-    rp.local_expert_offset = local_off;
-    rp.topk_idx = topk_idx;
-    rp.topk_w = topk_w;
-    // first kernel of the call: no dependent-launch attribute
-    route_permute_kernel<<<1, 1024, 0, s>>>(rp, pp);
-    if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
-  } else if (T <= 1024) {
+  if (T <= 1024) {
     if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
     const int chunks = static_cast<int>(div_up(T, 1024));
@@ -436,7 +534,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   gp.a_perm = a_perm;
   gp.sa_perm = sa_perm;
   gp.y_acc = y_acc;
-  gp.g1_acc = g1_acc;
+  gp.g1_acc = nullptr;
   int ggrid = static_cast<int>(div_up(cap, 8));
   if (ggrid < di.sm_count) ggrid = di.sm_count;
   if (ggrid > di.sm_count * 4) ggrid = di.sm_count * 4;
@@ -453,26 +551,20 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g1.w_scale = gemm1_weights_scale;
   g1.num_tokens = T;
   g1.cap = cap;
-  g1.splits = plan.g1_splits;
+  g1.splits = 1;
   g1.c_hi = c_hi;
   g1.c_lo = c_lo;
   g1.c_scale = c_scale;
-  g1.g1_acc = g1_acc;
+  g1.g1_acc = nullptr;
   g1.status = status;
   g1.sched = sched;
-  const int grid1 = grid_for(num_tokens, plan.g1_bn, kInterBlocks, plan.g1_splits, di.sm_count);
-  if (plan.split_g1) {
-    if (launch_moe_gemm(kGemm1Split, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
-      return MOE_B200_ERR_CUDA;
-    if (launch_kernel(swiglu_quant_kernel, di.sm_count * 2, 256, 0, s, true, static_cast<const int*>(seg_off),
-                      static_cast<const float*>(g1_acc), c_hi, c_lo, c_scale, cap) != cudaSuccess)
-      return MOE_B200_ERR_CUDA;
-  } else if (plan.token_major) {
+  const int grid1 = grid_for(num_tokens, plan.g1_bn, kInterBlocks, 1, di.sm_count);
+  if (plan.token_major) {
     const int grid_tm = grid_for(num_tokens, 128, kInterBlocks, 1, di.sm_count);
     if (launch_moe_gemm_tm(true, tm_w13, tm_aperm, tm_aperm, g1, grid_tm, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
   } else {
-    if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, s) != cudaSuccess)
+    if (launch_moe_gemm(kGemm1Fused, plan.g1_bn, tm_w13, tm_aperm, tm_aperm, g1, grid1, true, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
   }
 
@@ -481,16 +573,16 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g2.act_scale = c_scale;
   g2.sched = sched + 1;
   g2.w_scale = gemm2_weights_scale;
-  g2.splits = plan.g2_splits;
+  g2.splits = 1;
   g2.y_acc = y_acc;
   const int g2_kind = plan.g2_wide ? kGemm2Wide : kGemm2;
   const int grid2 = grid_for(num_tokens, plan.g2_bn, plan.g2_wide ? kHiddenBlocks / 2 : kHiddenBlocks,
-                             plan.g2_splits, di.sm_count);
+                             1, di.sm_count);
   if (plan.token_major) {
     const int grid_tm = grid_for(num_tokens, 128, kHiddenBlocks / 2, 1, di.sm_count);
     if (launch_moe_gemm_tm(false, tm_w2, tm_chi, tm_clo, g2, grid_tm, s) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
-  } else if (launch_moe_gemm(g2_kind, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, s) != cudaSuccess) {
+  } else if (launch_moe_gemm(g2_kind, plan.g2_bn, tm_w2, tm_chi, tm_clo, g2, grid2, true, s) != cudaSuccess) {
     return MOE_B200_ERR_CUDA;
   }
   mark_stage(5, s);

@@ -5,6 +5,8 @@
 #include <utility>
 #include <cuda_runtime.h>
 
+#include "moe_shapes.cuh"
+
 namespace moe {
 
 struct RouteParams {
@@ -45,10 +47,32 @@ struct GatherParams {
   float* g1_acc;            // [cap, 4096] used rows cleared; null unless K-split
 };
 
+// Decode batches (num_tokens <= kDecodeMaxTokens) use a dedicated front end:
+// one 8-CTA cluster does routing, permutation, the permuted row copy and the
+// clears the K-split GEMM1 needs.
+constexpr int kDecodeMaxTokens = 64;
+constexpr int kDecodeClusterCtas = 8;
+
+struct DecodeFrontParams {
+  int* counts;              // [32] assignments per local expert (written)
+  int* seg_off;             // [33] padded segment starts (written)
+  int32_t* perm_tok;        // [cap] token of each permuted row, -1 for padding
+  float* perm_w;            // [cap] routing weight of each permuted row
+  uint32_t* status;         // device status word (cleared)
+  int* sched;               // [4] GEMM unit counters (cleared)
+  float* g1_acc;            // [cap, 4096] rows of valid (token, expert) pairs cleared
+  const uint8_t* hidden;    // [T, 7168] e4m3
+  const float* hidden_scale;  // [56, T]
+  uint8_t* a_perm;          // [cap, 7168] valid rows copied from hidden
+  float* sa_perm;           // [56, cap] their block scales
+  int cap;
+  int local_expert_offset;
+};
+
 // The three grouped-GEMM flavours built from one kernel template.
 enum GemmKind : int {
   kGemm1Fused = 0,  // GEMM1 over the full K, SwiGLU + hi/lo e4m3 split in the epilogue
-  kGemm1Split = 1,  // GEMM1 over a K slice, fp32 red.add into g1_acc
+  kGemm1Split = 1,  // decode GEMM1 over a K slice, fp32 red.add into g1_acc
   kGemm2 = 2,       // GEMM2 (hi + lo operands), weighted fp32 red.add into y_acc
   kGemm2Wide = 3,   // GEMM2 over two 128-row W2 blocks per tile (M = 256)
 };
@@ -67,7 +91,7 @@ struct GemmParams {
   uint8_t* c_lo;            // [cap, 2048] e4m3
   float* c_scale;           // [16, cap] written by kGemm1Fused / swiglu_quant
   float* g1_acc;            // [cap, 4096] fp32 (kGemm1Split)
-  float* y_acc;             // [T, 7168] fp32 (kGemm2)
+  float* y_acc;             // [T, 7168] fp32 (kGemm2; kGemm1Split clears it)
   uint32_t* status;         // device status word
   int* sched;               // this GEMM's unit counter (cleared by the permutation)
 };
@@ -94,12 +118,12 @@ cudaError_t launch_kernel(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t 
 
 __global__ void route_kernel(RouteParams p);
 __global__ void permute_kernel(PermuteParams p);
-__global__ void route_permute_kernel(RouteParams rp, PermuteParams pp);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
 __global__ void swiglu_quant_kernel(const int* seg_off, const float* g1_acc, uint8_t* c_hi,
                                     uint8_t* c_lo, float* c_scale, int cap);
 __global__ void finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4);
+__global__ void route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp);
 
 }  // namespace moe

@@ -21,6 +21,7 @@ constexpr uint32_t kStatusTimeoutEpilogue = 1u << 2;
 constexpr uint32_t kStatusTimeoutScale = 1u << 3;
 constexpr uint32_t kStatusBadRouting = 1u << 4;
 constexpr uint32_t kStatusTimeoutUnit = 1u << 5;
+constexpr uint32_t kStatusTimeoutFixup = 1u << 6;   // stream-K partial tile never arrived
 
 // A wait longer than this is treated as a hang (1 s).
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
@@ -140,6 +141,11 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
       "l"(src), "r"(bytes), "r"(bar)
       : "memory");
+}
+
+// Hint: bring the 128-byte line holding `p` into L2.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {

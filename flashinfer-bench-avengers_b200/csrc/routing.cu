@@ -24,11 +24,21 @@ __device__ __forceinline__ bool ranks_before(float va, int ia, float vb, int ib)
   return (va > vb) || (va == vb && ia < ib);
 }
 
+// Unsigned key with the order of the float values (for non-NaN inputs; -0.0
+// cannot occur here since scores are strictly positive).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
 }  // namespace
 
 // Routes token t with one warp: lane l owns experts 8l .. 8l+7, so group g
 // (32 experts) is owned by lanes 4g .. 4g+3.
-__device__ __forceinline__ void route_token(const RouteParams& p, int t, int lane) {
+// Lanes 0..7 return the token's k-th selection (expert id and weight) in
+// out_idx / out_w and also store them to topk_idx / topk_w.
+__device__ __forceinline__ void route_token(const RouteParams& p, int t, int lane, int& out_idx,
+                                            float& out_w) {
 
   // ---- scores -------------------------------------------------------------
   const float4* lrow = reinterpret_cast<const float4*>(p.logits + static_cast<int64_t>(t) * kExpertsGlobal);
@@ -86,6 +96,12 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
   const bool keep = rank < kTopKGroups;
 
   // ---- top-8 experts among the kept groups --------------------------------
+  // Each round takes the largest remaining candidate: every lane offers its
+  // best untaken one (lowest index on equal values), one warp max over an
+  // order-preserving integer key finds the value, and the lowest lane
+  // offering it wins -- lanes own increasing expert ranges, so that is the
+  // lowest expert index among equal values, the same total order as
+  // ranks_before.
   float cand[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) cand[j] = keep ? sb[j] : -INFINITY;
@@ -95,27 +111,22 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
 #pragma unroll
   for (int k = 0; k < kTopK; ++k) {
     float bv = -INFINITY;
-    int bi = 0x7fffffff;
+    int bj = -1;
     float bs = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const int idx = 8 * lane + j;
-      if (!((taken >> j) & 1u) && ranks_before(cand[j], idx, bv, bi)) {
+      if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) {
         bv = cand[j];
-        bi = idx;
+        bj = j;
         bs = s[j];
       }
     }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      const float os = __shfl_xor_sync(0xffffffffu, bs, off);
-      if (ranks_before(ov, oi, bv, bi)) { bv = ov; bi = oi; bs = os; }
-    }
-    if ((bi >> 3) == lane) taken |= 1u << (bi & 7);
-    sel_idx[k] = bi;
-    sel_s[k] = bs;
+    const uint32_t key = bj >= 0 ? order_key(bv) : 0u;
+    const uint32_t best = __reduce_max_sync(0xffffffffu, key);
+    const int wl = __ffs(__ballot_sync(0xffffffffu, key == best)) - 1;
+    if (lane == wl) taken |= 1u << bj;
+    sel_idx[k] = __shfl_sync(0xffffffffu, 8 * lane + bj, wl);
+    sel_s[k] = __shfl_sync(0xffffffffu, bs, wl);
   }
 
   // ---- weights: unbiased scores renormalised over the selection ------------
@@ -123,16 +134,17 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
 #pragma unroll
   for (int k = 0; k < kTopK; ++k) sum += sel_s[k];
   sum = fmaxf(sum, 1e-20f);
-  if (lane < kTopK) {
-    int my_idx = sel_idx[0];
-    float my_s = sel_s[0];
+  int my_idx = sel_idx[0];
+  float my_s = sel_s[0];
 #pragma unroll
-    for (int k = 1; k < kTopK; ++k) {
-      if (lane == k) { my_idx = sel_idx[k]; my_s = sel_s[k]; }
-    }
-    const float w = (my_s / sum) * p.routed_scaling_factor;
-    p.topk_idx[t * kTopK + lane] = my_idx;
-    p.topk_w[t * kTopK + lane] = w;
+  for (int k = 1; k < kTopK; ++k) {
+    if (lane == k) { my_idx = sel_idx[k]; my_s = sel_s[k]; }
+  }
+  out_idx = my_idx;
+  out_w = (my_s / sum) * p.routed_scaling_factor;
+  if (lane < kTopK) {
+    p.topk_idx[t * kTopK + lane] = out_idx;
+    p.topk_w[t * kTopK + lane] = out_w;
   }
 }
 
@@ -140,7 +152,9 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
 __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   pdl_launch_next();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (t < p.num_tokens) route_token(p, t, threadIdx.x & 31);
+  int idx;
+  float w;
+  if (t < p.num_tokens) route_token(p, t, threadIdx.x & 31, idx, w);
 }
 
 namespace {
@@ -300,15 +314,207 @@ __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
   permute_body(p);
 }
 
-// Tiny batches: routing and permutation in one CTA (saves a launch and a
-// round trip through global memory). Warp w routes tokens w, w+32, ..., then
-// the CTA permutes.
-__global__ void __launch_bounds__(1024) route_permute_kernel(RouteParams rp, PermuteParams pp) {
+namespace {
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Every thread of every CTA of the cluster arrives; memory operations before
+// the barrier (shared::cluster and global) are visible to all CTAs after it.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// 32-bit store into the shared memory of CTA `rank` of this cluster, at the
+// offset `local` has in the calling CTA.
+__device__ __forceinline__ void st_cluster_u32(const void* local, uint32_t rank, uint32_t v) {
+  uint32_t remote;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(remote) : "r"(smem_u32(local)), "r"(rank));
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(remote), "r"(v) : "memory");
+}
+
+}  // namespace
+
+// Decode batches (T <= kDecodeMaxTokens = 64): routing, permutation and the
+// clears the decode GEMMs rely on, in one cluster of 8 CTAs x 256 threads.
+//   1. warp w of CTA r routes token 8r + w and stores its eight selections
+//      into CTA 0's shared memory (distributed shared memory);
+//   2. CTA 0 places the local picks with warp ballots (deterministic,
+//      segments in increasing token order, padded to kSegAlign rows, same
+//      result as permute_kernel) while CTA 1 clears the GEMM unit counters
+//      and the status word;
+//   3. all CTAs copy the valid (token, expert) rows of the hidden states and
+//      their block scales into the permuted buffers (a_perm, sa_perm) and
+//      clear their g1_acc rows, which the K-split GEMM1 accumulates into.
+// Routing runs on eight SMs instead of one: one warp issues about a thousand
+// instructions per token, which on a single SM would serialise 64 tokens.
+__global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256)
+    route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp) {
+  __shared__ int s_idx[kDecodeMaxTokens * kTopK];     // filled in CTA 0 only
+  __shared__ float s_w[kDecodeMaxTokens * kTopK];
+  __shared__ int s_wcnt[2][kExpertsLocal];
+  __shared__ int s_start[kExpertsLocal];
+  __shared__ int s_cnt[kExpertsLocal];
   pdl_launch_next();
-  const int warp = threadIdx.x >> 5;
-  for (int t = warp; t < rp.num_tokens; t += 32) route_token(rp, t, threadIdx.x & 31);
-  __syncthreads();
-  permute_body(pp);
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int T = rp.num_tokens;
+  const uint32_t rank = cluster_rank();
+
+  // ---- 1. routing -----------------------------------------------------------
+  {
+    const int t = static_cast<int>(rank) * 8 + warp;
+    if (t < T) {
+      int idx;
+      float w;
+      route_token(rp, t, lane, idx, w);
+      if (lane < kTopK) {
+        st_cluster_u32(&s_idx[t * kTopK + lane], 0, static_cast<uint32_t>(idx));
+        st_cluster_u32(&s_w[t * kTopK + lane], 0, __float_as_uint(w));
+      }
+      // A token with a local pick has its row copied in phase 3: start
+      // pulling its 7 KB row and 56 block scales into L2 now.
+      const int le = idx - dp.local_expert_offset;
+      if (__ballot_sync(0xffffffffu, lane < kTopK && le >= 0 && le < kExpertsLocal)) {
+        const uint8_t* row = dp.hidden + static_cast<int64_t>(t) * kHidden;
+        prefetch_l2(row + lane * 128);
+        prefetch_l2(row + (lane + 32) * 128);
+        prefetch_l2(dp.hidden_scale + static_cast<int64_t>(lane) * T + t);
+        if (lane + 32 < kHiddenBlocks) prefetch_l2(dp.hidden_scale + static_cast<int64_t>(lane + 32) * T + t);
+      }
+    }
+  }
+  cluster_sync_all();
+
+  // ---- 2. permutation (CTA 0) / counter clears (CTAs 1..7) ------------------
+  if (rank == 0) {
+    const int t = tid;   // token of this thread (warps 0 and 1)
+    int sidx[kTopK];
+    float sw[kTopK];
+    uint32_t mask = 0;
+    uint64_t ranks = 0;
+    if (warp < 2) {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        sidx[k] = -1;
+        sw[k] = 0.f;
+        if (t < T) {
+          const int le = s_idx[t * kTopK + k] - dp.local_expert_offset;
+          if (le >= 0 && le < kExpertsLocal) {
+            sidx[k] = le;
+            sw[k] = s_w[t * kTopK + k];
+            mask |= 1u << le;
+          }
+        }
+      }
+      const uint32_t lt_mask = (1u << lane) - 1u;
+      int nset = 0;
+#pragma unroll
+      for (int e = 0; e < kExpertsLocal; ++e) {
+        const uint32_t bal = __ballot_sync(0xffffffffu, (mask >> e) & 1u);
+        if (lane == e) s_wcnt[warp][e] = __popc(bal);
+        if ((mask >> e) & 1u) {
+          ranks |= static_cast<uint64_t>(__popc(bal & lt_mask)) << (5 * nset);
+          ++nset;
+        }
+      }
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int c = s_wcnt[0][lane] + s_wcnt[1][lane];
+      const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+      int incl = padded;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      s_start[lane] = incl - padded;
+      s_cnt[lane] = c;
+      dp.counts[lane] = c;
+      dp.seg_off[lane + 1] = incl;
+      if (lane == 0) dp.seg_off[0] = 0;
+    }
+    __syncthreads();
+    if (warp < 2) {
+      if (t < T) {
+        uint32_t m = mask;
+        int j = 0;
+        while (m) {
+          const int e = __ffs(m) - 1;
+          m &= m - 1;
+          const int r = static_cast<int>((ranks >> (5 * j)) & 31u) + (warp == 1 ? s_wcnt[0][e] : 0);
+          ++j;
+          float w = 0.f;
+#pragma unroll
+          for (int k = 0; k < kTopK; ++k) {
+            if (sidx[k] == e) w = sw[k];
+          }
+          dp.perm_tok[s_start[e] + r] = t;
+          dp.perm_w[s_start[e] + r] = w;
+        }
+      }
+    } else {
+      // padding rows: 32 experts x kSegAlign slots over threads 64..575
+      for (int i = tid - 64; i < kExpertsLocal * kSegAlign; i += blockDim.x - 64) {
+        const int e = i / kSegAlign;
+        const int j = i % kSegAlign;
+        const int c = s_cnt[e];
+        const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+        if (c + j < padded) {
+          dp.perm_tok[s_start[e] + c + j] = -1;
+          dp.perm_w[s_start[e] + c + j] = 0.f;
+        }
+      }
+    }
+  } else {
+    if (rank == 1 && tid < 4) dp.sched[tid] = 0;
+    if (rank == 1 && tid == 4) *dp.status = 0;
+  }
+  cluster_sync_all();
+
+  // ---- 3. permuted rows and g1_acc clears of the valid pairs ---------------
+  // Valid pair v (0 <= v < sum of counts) is row seg_off[e] + v - cpre[e] of
+  // expert e, cpre = exclusive prefix of the counts. One warp per row.
+  {
+    const int cnt = __ldcg(dp.counts + lane);
+    const int seg = __ldcg(dp.seg_off + lane);
+    int incl = cnt;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    const int total = __shfl_sync(0xffffffffu, incl, 31);
+    const int gw = static_cast<int>(rank) * 8 + warp;
+    for (int v = gw; v < total; v += kDecodeClusterCtas * 8) {
+      // expert of pair v: the number of experts whose inclusive prefix is <= v
+      const int e = __popc(__ballot_sync(0xffffffffu, incl <= v));
+      const int row = __shfl_sync(0xffffffffu, seg, e) + v - (__shfl_sync(0xffffffffu, incl, e) -
+                                                                __shfl_sync(0xffffffffu, cnt, e));
+      const int tok = __ldcg(dp.perm_tok + row);
+      // every load first, then the stores (the clears do not wait for them)
+      const uint4* src = reinterpret_cast<const uint4*>(dp.hidden + static_cast<int64_t>(tok) * kHidden);
+      uint4 rowv[kHidden / 16 / 32];
+#pragma unroll
+      for (int i = 0; i < kHidden / 16 / 32; ++i) rowv[i] = src[lane + 32 * i];
+      const float sc0 = dp.hidden_scale[static_cast<int64_t>(lane) * T + tok];
+      const float sc1 = lane + 32 < kHiddenBlocks ? dp.hidden_scale[static_cast<int64_t>(lane + 32) * T + tok] : 0.f;
+      float4* g = reinterpret_cast<float4*>(dp.g1_acc + static_cast<int64_t>(row) * kGemm1Out);
+#pragma unroll 8
+      for (int i = lane; i < kGemm1Out / 4; i += 32) g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+      uint4* dst = reinterpret_cast<uint4*>(dp.a_perm + static_cast<int64_t>(row) * kHidden);
+#pragma unroll
+      for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = rowv[i];
+      dp.sa_perm[static_cast<int64_t>(lane) * dp.cap + row] = sc0;
+      if (lane + 32 < kHiddenBlocks) dp.sa_perm[static_cast<int64_t>(lane + 32) * dp.cap + row] = sc1;
+    }
+  }
 }
 
 // Multi-CTA permutation for batches of more than 1024 tokens, one 1024-token

@@ -122,8 +122,8 @@ typedef struct moe_b200_workspace_layout {
   size_t c_hi;        /* e4m3[cap_rows, 2048] */
   size_t c_lo;        /* e4m3[cap_rows, 2048] */
   size_t c_scale;     /* fp32[16, cap_rows] */
-  size_t y_acc;       /* fp32[T, 7168] */
-  size_t g1_acc;      /* fp32[cap_rows, 4096], 0 when the plan for T does not split K */
+  size_t y_acc;       /* fp32[T, 7168] combine buffer */
+  size_t g1_acc;      /* fp32[cap_rows, 4096] K-split GEMM1 sums (decode plan, T <= 64; else 0) */
   int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
   size_t chunk_counts; /* int32[ceil(T/1024), 32] per-chunk expert counts */
   size_t sched;       /* int32[4] work-unit counters of the GEMM kernels */

@@ -60,11 +60,19 @@ def test_workspace_size_and_layout(lib):
         lay = moe_host.workspace_layout(T)
         assert lay.total_bytes == n
         assert lay.cap_rows == (8 * T + 15) // 16 * 16 + 32 * 16 + 128
-        offs = [lay.counts, lay.seg_off, lay.chunk_counts, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w, lay.a_perm,
-                lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
+        decode = T <= 64
+        offs = [lay.counts, lay.seg_off, lay.chunk_counts, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w,
+                lay.a_perm, lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
+        if decode:
+            offs += [lay.g1_acc]
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
+        assert offs[-1] < n
         assert lay.c_lo - lay.c_hi >= lay.cap_rows * 2048
-        assert (lay.g1_acc != 0) == (T <= 64)
+        if decode:
+            assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
+            assert n - lay.g1_acc >= lay.cap_rows * 4096 * 4
+        else:
+            assert lay.g1_acc == 0
         if T > 65:  # plans without the decode scratch grow with T
             assert n >= prev
         prev = n
@@ -106,4 +114,4 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 4
+    assert lib.moe_b200_abi_version() == 5
