@@ -11,10 +11,15 @@ N>1 GPUs (torchrun) every rank owns a different 32-expert shard of the
 partial bf16 outputs are summed with an NCCL all-reduce: expert parallelism
 with fixed work per GPU ("weak" scaling).
 
-A step is one layer call. Timing: W untimed warm-up steps, then K steps,
-each preceded by an L2 flush (256 MB write) outside its CUDA-event pair;
-the steps are bracketed by a barrier and device synchronisation; the
-reported time is the max over ranks. `value` is microseconds per call.
+A step is one layer call. Timing: W untimed warm-up steps, then K steps
+bracketed by a barrier and device synchronisation; the reported time is the
+max over ranks. `value` is microseconds per call. L2: a call whose active
+experts' weights exceed twice the 126 MB L2 (705 MB at T=64) cannot find
+any weight byte in L2 from the previous call, so those calls run back to
+back ("inputs larger than L2"); smaller calls get a 256 MB write flush
+before each timed call. The headline line also reports the same call after
+a 256 MB write flush (`value_l2_write_flushed`): the write-back of the
+dirty flush lines then shares HBM with the weight stream.
 
 At N=1 the line also carries the decode sweep T in {1,4,16,64} (config 1),
 the prefill point (config 2, T=4096 with 4 hot experts) and the stress
@@ -183,13 +188,23 @@ def layer_bytes(st: dict) -> int:
     return st["E_act"] * LAYER_BYTES_PER_EXPERT + st["T"] * LAYER_BYTES_PER_TOKEN + 512
 
 
-def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=None) -> dict:
-    """Device time of `steps` layer calls, each replayed from a CUDA graph
-    after an L2 flush. A second graph of the same call records the library's
-    stage events and gives the per-stage breakdown (its event nodes add a
-    little latency, so the headline time comes from the graph without them).
-    With a process group the NCCL all-reduce of the partial outputs follows
-    each replay eagerly."""
+L2_BYTES = 126 * 1024 * 1024
+
+
+def weights_exceed_l2(st: dict) -> bool:
+    """True when one call streams more than twice the L2 in expert weights."""
+    return st["E_act"] * (W13_BYTES + W2_BYTES) > 2 * L2_BYTES
+
+
+def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=None,
+               do_flush: bool = True) -> dict:
+    """Device time of `steps` layer calls replayed from a CUDA graph, each
+    after a 256 MB write flush when `do_flush` (otherwise back to back; the
+    flushed timing is then taken as well, as `call_ms_flushed`). A second
+    graph of the same call records the library's stage events and gives the
+    per-stage breakdown (its event nodes add a little latency, so the
+    headline time comes from the graph without them). With a process group
+    the NCCL all-reduce of the partial outputs follows each replay eagerly."""
     import moe_host
     import torch.distributed as dist
 
@@ -222,29 +237,35 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
     if group is not None:
         dist.barrier(group=group)
     torch.cuda.synchronize()
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
-    for i in range(steps):
-        flush.zero_()
-        starts[i].record()
-        plain.replay()
+    def timed(flushed: bool) -> list:
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        for i in range(steps):
+            if flushed:
+                flush.zero_()
+            starts[i].record()
+            plain.replay()
+            if group is not None:
+                dist.all_reduce(out, group=group)
+            ends[i].record()
+        torch.cuda.synchronize()
         if group is not None:
-            dist.all_reduce(out, group=group)
-        ends[i].record()
-    torch.cuda.synchronize()
-    if group is not None:
-        dist.barrier(group=group)
-    call_ms = [a.elapsed_time(b) for a, b in zip(starts, ends)]
+            dist.barrier(group=group)
+        return [a.elapsed_time(b) for a, b in zip(starts, ends)]
+
+    call_ms = timed(do_flush)
+    call_ms_flushed = call_ms if do_flush else timed(True)
     stage_ms = {n: [] for n in moe_host.STAGE_NAMES}
     for _ in range(max(3, steps // 4)):
-        flush.zero_()
+        if do_flush:
+            flush.zero_()
         staged.replay()
         torch.cuda.synchronize()  # the stage events are reused every replay
         for j, name in enumerate(moe_host.STAGE_NAMES):
             stage_ms[name].append(ev[j].elapsed_time(ev[j + 1]))
     del plain, staged
-    return {"call_ms": call_ms, "stage_ms": {k: statistics.mean(v) for k, v in stage_ms.items()},
-            "out": out}
+    return {"call_ms": call_ms, "call_ms_flushed": call_ms_flushed,
+            "stage_ms": {k: statistics.mean(v) for k, v in stage_ms.items()}, "out": out}
 
 
 def time_e2e(inp: dict, steps: int, warmup: int, group=None) -> dict:
@@ -363,14 +384,16 @@ def roofline_entry(ms: float, nbytes: int, flops: int, peaks: dict, bound: str) 
 def point(T: int, variant: str, steps: int, warmup: int, flush, peaks, device, seed=SEED) -> dict:
     inp = workloads.make_inputs(T, seed, device, variant)
     st = routing_stats(inp)
-    r = time_layer(inp, steps, warmup, flush)
+    r = time_layer(inp, steps, warmup, flush, do_flush=not weights_exceed_l2(st))
     us = statistics.mean(r["call_ms"]) * 1e3
     kb, kf = kernel_bytes(st), kernel_flops(st)
     lb = layer_bytes(st)
     lf = kf["gemm1"] + kf["gemm2"]
     res = {"T": T, "variant": variant, "us_per_call": round(us, 2), **st,
            "layer_GBps": round(lb / (us * 1e-6) / 1e9, 1), "layer_TFLOPs": round(lf / (us * 1e-6) / 1e12, 2),
-           "stages_us": {k: round(v * 1e3, 2) for k, v in r["stage_ms"].items()}}
+           "stages_us": {k: round(v * 1e3, 2) for k, v in r["stage_ms"].items()},
+           "l2": "back to back (weights > 2x L2)" if weights_exceed_l2(st) else "256 MB write flush",
+           "us_per_call_l2_write_flushed": round(statistics.mean(r["call_ms_flushed"]) * 1e3, 2)}
     t_hbm = lb / (peaks["hbm_gbs"] * 1e9)
     t_tc = lf / (2.0 * peaks["bf16_tflops"] * 1e12)
     res["roofline_us"] = round(max(t_hbm, t_tc) * 1e6, 2)
@@ -422,13 +445,21 @@ def main() -> None:
     inp = workloads.make_inputs(HEADLINE_T, SEED, device, variant, offset, 2.5, weight_seed=SEED + 1 + rank)
     st = routing_stats(inp)
 
+    # every rank must take the same timing path (the all-reduces inside it)
+    b2b = torch.tensor(1 if weights_exceed_l2(st) else 0, device=device)
+    if group is not None:
+        dist.all_reduce(b2b, op=dist.ReduceOp.MIN, group=group)
+    back_to_back = bool(b2b.item())
     with ClockSampler(device) as clocks:
-        r = time_layer(inp, args.steps, warmup, flush, group)
+        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back)
     call_ms = torch.tensor(r["call_ms"], dtype=torch.float64, device=device)
     mean_ms = call_ms.mean()
     if group is not None:
         dist.all_reduce(mean_ms, op=dist.ReduceOp.MAX, group=group)
     mean_ms = float(mean_ms)
+    flushed_ms = torch.tensor(r["call_ms_flushed"], dtype=torch.float64, device=device).mean()
+    if group is not None:
+        dist.all_reduce(flushed_ms, op=dist.ReduceOp.MAX, group=group)
 
     e2e = time_e2e(inp, args.steps, warmup, group)
     e2e_ms = torch.tensor(e2e["ms"], dtype=torch.float64, device=device)
@@ -451,7 +482,9 @@ def main() -> None:
                                 "2 x measured cuBLAS bf16 burst (MEASURED_PEAKS.json bf16_tflops): dense e4m3")
                                if peaks["source"] == "measured" else "fallback 6.65 TB/s / 1.59 PFLOP/s")})
 
-    launches_per_call = 6 if HEADLINE_T <= 64 else 5  # route, permute, gemm1, [swiglu], gemm2, finalize
+    # decode (T <= 64): front end, GEMM1, GEMM2, finalize; larger T: route,
+    # permute (two kernels above 1024 tokens), gather, GEMM1, GEMM2, finalize
+    launches_per_call = 4 if HEADLINE_T <= 64 else (6 if HEADLINE_T <= 1024 else 7)
     line = {
         "metric": METRIC,
         "value": round(mean_ms * 1e3, 2),
@@ -469,7 +502,12 @@ def main() -> None:
         "config": {"workload": f"{desc}, 32 local experts per GPU",
                    "T": HEADLINE_T, "local_expert_offset": offset, "E_act": st["E_act"],
                    "sum_Tk": st["sum_Tk"], "parallelism": f"ep{world}" + (" + NCCL all-reduce" if world > 1 else ""),
-                   "l2": "flushed (256 MB write) before every timed call"},
+                   "l2": ("back to back: each call streams the active experts' weights "
+                          f"({st['E_act'] * (W13_BYTES + W2_BYTES) / 1e6:.0f} MB > 2 x 126 MB L2), so no "
+                          "weight byte is L2-resident from the previous call; value_l2_write_flushed is the "
+                          "same call after a 256 MB write flush" if back_to_back else
+                          "flushed (256 MB write) before every timed call")},
+        "value_l2_write_flushed": round(float(flushed_ms) * 1e3, 2),
         "roofline": rl,
         "stages_us": {k: round(v * 1e3, 2) for k, v in stage.items()},
         "e2e": {"value": round(float(e2e_ms) * 1e3, 2), "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"],

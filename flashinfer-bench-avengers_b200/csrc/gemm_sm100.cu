@@ -224,6 +224,37 @@ __device__ __forceinline__ void swiglu_quant_store(float (&acc0)[CPT], const flo
   }
 }
 
+// Decode SwiGLU of one (row, 128-block) of the K-split GEMM1 sums, by one
+// warp: C = silu(gate) * up (solution/cuda/kernel.h:207) for intermediate
+// columns ib*128 + 4l .. +3 in lane l, written as the e4m3 pair
+// C = s * (hi + lo), s = amax / 448 over the block. Same arithmetic as
+// swiglu_quant_store.
+__device__ __forceinline__ void swiglu_quant_row_block(const GemmParams& p, int row, int ib, int lane) {
+  const float* g = p.g1_acc + static_cast<int64_t>(row) * kGemm1Out + ib * kBlk + 4 * lane;
+  const float4 up = __ldcg(reinterpret_cast<const float4*>(g));
+  const float4 gate = __ldcg(reinterpret_cast<const float4*>(g + kInter));
+  const float h[4] = {silu_mul(gate.x, up.x), silu_mul(gate.y, up.y), silu_mul(gate.z, up.z),
+                      silu_mul(gate.w, up.w)};
+  float amax = fmaxf(fmaxf(fabsf(h[0]), fabsf(h[1])), fmaxf(fabsf(h[2]), fabsf(h[3])));
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  const float inv = amax > 0.f ? 448.0f / amax : 0.f;
+  uint32_t phi = 0, plo = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float x = h[j] * inv;
+    const __nv_fp8_e4m3 qh(x);
+    const float r = x - static_cast<float>(qh);
+    const __nv_fp8_e4m3 ql(r);
+    phi |= static_cast<uint32_t>(qh.__x) << (8 * j);
+    plo |= static_cast<uint32_t>(ql.__x) << (8 * j);
+  }
+  const int64_t off = static_cast<int64_t>(row) * kInter + ib * kBlk + 4 * lane;
+  *reinterpret_cast<uint32_t*>(p.c_hi + off) = phi;
+  *reinterpret_cast<uint32_t*>(p.c_lo + off) = plo;
+  if (lane == 0) p.c_scale[static_cast<int64_t>(ib) * p.cap + row] = amax * (1.0f / 448.0f);
+}
+
 template <int kKind, int BN, int kStages, int kEpiWarps>
 __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kThreads, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tm_w,
@@ -366,6 +397,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     uint32_t uph = 0;
     int iter = 0;
     bool ok = true;
+    bool c_ready = p.grid_sync == nullptr;   // decode GEMM2: C is produced in this kernel
     while (ok) {
       // publish the unit (or the end marker -1) to the other roles
       if (!mbar_wait(smem_u32(&uempty_bar[uslot]), uph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) break;
@@ -405,6 +437,31 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
             !mbar_wait(smem_u32(&sempty_bar[slot]), sph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) {
           ok = false;
           break;
+        }
+        if (!c_ready) {
+          // The token tiles (C) and their scales are written by every CTA of
+          // this grid: wait until all have counted themselves on grid_sync.
+          if (lane == 0) {
+            const uint64_t t0 = globaltimer_ns();
+            uint32_t spins = 0;
+            while (ld_acquire_gpu(p.grid_sync) < static_cast<int>(gridDim.x)) {
+              if ((++spins & 63u) == 0u) {
+                if (*s_abort) break;
+                if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+                  atomicOr(p.status, kStatusTimeoutGridSync);
+                  *s_abort = 1;
+                  break;
+                }
+              }
+            }
+            fence_proxy_async_global();
+          }
+          __syncwarp();
+          if (*s_abort) {
+            ok = false;
+            break;
+          }
+          c_ready = true;
         }
         if (lane == 0) {
           uint8_t* st = smem + Tr::kOffStages + stage * Tr::kStageBytes;
@@ -550,6 +607,35 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     const int et = ew * 32 + lane;            // 0.. inside the epilogue group
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
     constexpr uint32_t kEpiThreads = 32 * Tr::kEpiWarps;
+    if constexpr (kKind == kGemm2Wide) {
+      if (p.grid_sync != nullptr) {
+        // Decode plan: convert the K-split GEMM1 sums of every valid
+        // (token, expert) row into C, one (row, 128-block) per warp task over
+        // the whole grid, then count this CTA on grid_sync. The producer
+        // streams its first weight tiles meanwhile. Valid pair v is row
+        // seg[e] + v - cpre[e] of expert e (cpre = exclusive prefix of counts).
+        const int cnt = s_cnt[lane];
+        int incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int o = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += o;
+        }
+        const int pairs = __shfl_sync(0xffffffffu, incl, 31);
+        const int nwarps = static_cast<int>(gridDim.x) * Tr::kEpiWarps;
+        for (int task = static_cast<int>(blockIdx.x) * Tr::kEpiWarps + ew; task < pairs * kInterBlocks;
+             task += nwarps) {
+          const int v = task / kInterBlocks;
+          const int e = __popc(__ballot_sync(0xffffffffu, incl <= v));
+          const int row = s_seg[e] + v - (__shfl_sync(0xffffffffu, incl, e) - __shfl_sync(0xffffffffu, cnt, e));
+          swiglu_quant_row_block(p, row, task % kInterBlocks, lane);
+        }
+        fence_proxy_async_global();   // C is read back through TMA
+        __threadfence();
+        named_bar_sync(1, kEpiThreads);
+        if (et == 0) red_release_gpu_add(p.grid_sync, 1);
+      }
+    }
     if constexpr (kKind == kGemm1Split) {
       // The decode plan clears GEMM2's combine buffer here, spread over all
       // CTAs while they wait for their first accumulator.

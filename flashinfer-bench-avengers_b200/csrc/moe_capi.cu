@@ -46,7 +46,7 @@ Plan choose_plan(int64_t T) {
   Plan p{};
   if (T <= kDecodeMaxTokens) {
     // Both GEMMs stream 16-token column groups against 256 weight rows
-    // (six 32 KB weight stages in flight per SM); GEMM1 splits K 8 ways.
+    // (six 32 KB weight stages in flight per SM); GEMM1 splits K 4 ways.
     p.decode = true;
     p.g1_bn = 16;
     p.g2_bn = 16;
@@ -227,15 +227,19 @@ void mark_stage(int i, cudaStream_t s) {
 //   route_permute_decode (one 8-CTA cluster: routing, permutation, permuted
 //     row copy, clears of the unit counters and of the g1_acc rows)
 //   -> K-split GEMM1 (red.add into g1_acc; also clears y_acc)
-//   -> swiglu_quant (C = silu(gate) * up as the hi/lo e4m3 pair)
-//   -> GEMM2 (two W2 blocks per tile, K split 2 ways, red.add into y_acc)
+//   -> GEMM2: first C = silu(gate) * up as the hi/lo e4m3 pair from the
+//      GEMM1 sums (all CTAs, then a grid-wide count before any C tile is
+//      loaded; W2 tiles stream meanwhile), then two W2 blocks per tile, K
+//      split 2 ways, red.add into y_acc
 //   -> finalize (bf16).
 int run_decode(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
                const void* hidden_states, const float* hidden_states_scale, const void* gemm1_weights,
                const float* gemm1_weights_scale, const void* gemm2_weights,
                const float* gemm2_weights_scale, int local_off, float rsf, int T, void* output,
                uint8_t* ws, const moe_b200_workspace_layout& l, const DeviceInfo& di, cudaStream_t s) {
-  constexpr int kG1Splits = 8;
+  // Four K slices: 2048 units of ~0.9 MB keep the SMs evenly loaded; more
+  // slices add red.add and unit-switch overhead.
+  constexpr int kG1Splits = 4;
   constexpr int kG2Splits = 2;
   constexpr int kBN = 16;
   const int cap = static_cast<int>(l.cap_rows);
@@ -318,9 +322,6 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   const int grid1 = grid_for(T, kBN, kInterBlocks, kG1Splits, di.sm_count);
   if (launch_moe_gemm(kGemm1Split, kBN, tm_w13, tm_aperm, tm_aperm, g1, grid1, false, s) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
-  if (launch_kernel(swiglu_quant_kernel, di.sm_count * 2, 256, 0, s, true, static_cast<const int*>(seg_off),
-                    static_cast<const float*>(g1_acc), c_hi, c_lo, c_scale, cap) != cudaSuccess)
-    return MOE_B200_ERR_CUDA;
   mark_stage(4, s);
 
   GemmParams g2 = g1;
@@ -328,7 +329,7 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   g2.w_scale = gemm2_weights_scale;
   g2.splits = kG2Splits;
   g2.sched = sched + 1;
-  g2.g1_acc = nullptr;
+  g2.grid_sync = sched + 2;
   const int grid2 = grid_for(T, kBN, kHiddenBlocks / 2, kG2Splits, di.sm_count);
   if (launch_moe_gemm(kGemm2Wide, kBN, tm_w2, tm_chi, tm_clo, g2, grid2, true, s) != cudaSuccess)
     return MOE_B200_ERR_CUDA;

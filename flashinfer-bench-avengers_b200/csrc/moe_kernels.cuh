@@ -94,6 +94,10 @@ struct GemmParams {
   float* y_acc;             // [T, 7168] fp32 (kGemm2; kGemm1Split clears it)
   uint32_t* status;         // device status word
   int* sched;               // this GEMM's unit counter (cleared by the permutation)
+  // Decode GEMM2 only: when g1_acc is set, the CTAs first convert the K-split
+  // GEMM1 sums into C (SwiGLU, hi/lo e4m3) and count themselves on grid_sync
+  // (cleared by the front end); no C tile is loaded before all have.
+  int* grid_sync;
 };
 
 // Launches `kern` on `stream`; with `dependent` set the launch carries the
@@ -121,8 +125,6 @@ __global__ void permute_kernel(PermuteParams p);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
-__global__ void swiglu_quant_kernel(const int* seg_off, const float* g1_acc, uint8_t* c_hi,
-                                    uint8_t* c_lo, float* c_scale, int cap);
 __global__ void finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4);
 __global__ void route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp);
 

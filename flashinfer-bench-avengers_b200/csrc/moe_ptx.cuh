@@ -21,7 +21,7 @@ constexpr uint32_t kStatusTimeoutEpilogue = 1u << 2;
 constexpr uint32_t kStatusTimeoutScale = 1u << 3;
 constexpr uint32_t kStatusBadRouting = 1u << 4;
 constexpr uint32_t kStatusTimeoutUnit = 1u << 5;
-constexpr uint32_t kStatusTimeoutFixup = 1u << 6;   // stream-K partial tile never arrived
+constexpr uint32_t kStatusTimeoutGridSync = 1u << 6;   // a grid-wide arrival count never completed
 
 // A wait longer than this is treated as a hang (1 s).
 constexpr uint64_t kWaitBudgetNs = 1000000000ull;
@@ -256,6 +256,23 @@ __host__ __device__ constexpr uint32_t idesc_e4m3_f32() {
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Acquire load / release reduction at GPU scope (cross-CTA hand-offs).
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses with its async-proxy
+// (TMA) accesses to global memory.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
 __device__ __forceinline__ void red_add_f32(float* addr, float v) {
