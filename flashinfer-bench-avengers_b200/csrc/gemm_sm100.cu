@@ -56,7 +56,13 @@ struct GemmTraits {
   static constexpr int kStageBytes = kNumA * kATileBytes + kNumB * kBTileBytes;
   static constexpr int kKBlocks = kIsG1 ? kHiddenBlocks : kInterBlocks;
   static constexpr int kRowBlocks = kIsG1 ? kInterBlocks : kHiddenBlocks / kNumA;
-  static constexpr int kAccCols = kNumA * BN;     // fp32 TMEM columns per accumulator buffer
+  // GEMM2's hi and lo token tiles sit back to back in shared memory with the
+  // same swizzled layout, so one MMA with N = 2 * BN covers both: half the
+  // MMA instructions (the decode GEMM2 is issue-bound at N = 16), and the
+  // epilogue adds the two column halves.
+  static constexpr bool kMergeB = kNumB == 2;
+  static constexpr int kMmaN = kMergeB ? 2 * BN : BN;
+  static constexpr int kAccCols = kNumA * kMmaN;  // fp32 TMEM columns per accumulator buffer
   static constexpr int kTmemCols = (2 * kAccCols <= 32) ? 32
                                    : (2 * kAccCols <= 64) ? 64
                                    : (2 * kAccCols <= 128) ? 128
@@ -75,17 +81,7 @@ struct GemmTraits {
   static constexpr int kCPT = BN / kWarpsPerQuarter;   // token columns per epilogue thread
   static constexpr int kThreads = (kRoleWarps + kEpiWarps) * 32;
   static constexpr int kColsPerLane = BN >= 32 ? BN / 32 : 1;
-  static constexpr uint32_t kIdesc = idesc_e4m3_f32<128, BN>();
-  // Register split for the widest epilogue (GEMM1, BN = 128, 8 epilogue warps):
-  // the block launches with kLaunchRegs per thread; the role warpgroup gives
-  // registers back and the epilogue warpgroups take them.
-  static constexpr bool kSplitRegs = kNumA == 2 && kEpiWarps == 8 && BN == 128;
-  static constexpr int kLaunchRegs = 168;
-  static constexpr int kRoleRegs = 56;
-  static constexpr int kEpiRegs = 224;
-  static_assert(!kSplitRegs || kRoleRegs * 128 + kEpiRegs * 32 * kEpiWarps <= kLaunchRegs * kThreads,
-                "register split exceeds the block's launch registers");
-
+  static constexpr uint32_t kIdesc = idesc_e4m3_f32<128, kMmaN>();
   // shared memory layout (offsets from the 1024-aligned base)
   static constexpr int kOffStages = 0;
   static constexpr int kOffRing = kStages * kStageBytes;
@@ -107,7 +103,8 @@ struct GemmTraits {
   static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
   static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;  // + alignment slack
 
-  static_assert(BN % 16 == 0 && BN >= 16 && BN <= 128, "BN");
+  static_assert(BN % 16 == 0 && BN >= 16 && kMmaN <= 256, "BN");
+  static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static_assert(kEpiWarps % 4 == 0 && kCPT >= 16 && kCPT % 16 == 0, "epilogue column split");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
@@ -353,7 +350,6 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
 
   if (warp == 0) {
     // ======================================================== TMA producer
-    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     // The first unit and the weight tiles of its first stages are taken
     // before waiting for the previous kernel (the stages are fresh, so no
     // empty-slot wait; the unit counter was cleared by the permutation).
@@ -496,7 +492,6 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     }
   } else if (warp == 1) {
     // ========================================================== MMA issuer
-    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     pdl_wait();
     pdl_launch_next();
     int stage = 0;
@@ -525,19 +520,15 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         if (lane == 0) {
           const uint32_t st = smem_u32(smem + Tr::kOffStages + stage * Tr::kStageBytes);
           const uint32_t d = tmem_base + abuf * Tr::kAccCols;
-          // accumulator a (columns a*BN..) = sum over the token tiles b of
-          // A_a . B_b (GEMM2: hi + lo), fresh at k = 0 of every K block
+          // accumulator a (columns a*kMmaN..) = A_a . [token tiles], fresh at
+          // k = 0 of every K block (GEMM2: columns BN.. hold the lo part)
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
 #pragma unroll
             for (int a = 0; a < Tr::kNumA; ++a) {
               const uint64_t adesc = sw128_kmajor_desc(st + a * Tr::kATileBytes + 32 * k);
-#pragma unroll
-              for (int b = 0; b < Tr::kNumB; ++b) {
-                const uint64_t bdesc =
-                    sw128_kmajor_desc(st + Tr::kNumA * Tr::kATileBytes + b * Tr::kBTileBytes + 32 * k);
-                umma_f8(d + a * BN, adesc, bdesc, Tr::kIdesc, (k > 0 || b > 0) ? 1u : 0u);
-              }
+              const uint64_t bdesc = sw128_kmajor_desc(st + Tr::kNumA * Tr::kATileBytes + 32 * k);
+              umma_f8(d + a * Tr::kMmaN, adesc, bdesc, Tr::kIdesc, k > 0 ? 1u : 0u);
             }
           }
           umma_commit(smem_u32(&empty_bar[stage]));
@@ -550,7 +541,6 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     }
   } else if (warp == 2) {
     // ======================================================= scale combiner
-    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     pdl_wait();
     pdl_launch_next();
     int slot = 0;
@@ -591,12 +581,10 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     }
   } else if (warp < Tr::kRoleWarps) {
     // spare warp of the role warpgroup
-    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
     pdl_wait();
     pdl_launch_next();
   } else {
     // ============================================================ epilogue
-    if constexpr (Tr::kSplitRegs) asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(Tr::kEpiRegs));
     pdl_wait();
     pdl_launch_next();
     constexpr int CPT = Tr::kCPT;
@@ -687,30 +675,47 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
         tc_fence_after();
         const float* comb0 = ring + slot * Tr::kSlotFloats + BN + 4 + col0;
         const uint32_t taddr = lane_base + abuf * Tr::kAccCols + col0;
-        // One phase per accumulator (up, gate): every TMEM load of the phase is
-        // issued before a single wait, then the promotion FMAs run.
+        // One phase per accumulator (up, gate / the two W2 blocks): every TMEM
+        // load of the phase is issued before a single wait, then the
+        // promotion FMAs run (GEMM2: of hi + lo, in chunks of 32 columns).
+        constexpr int kChunk = Tr::kMergeB ? (CPT < 32 ? CPT : 32) : CPT;
 #pragma unroll
         for (int ph_i = 0; ph_i < Tr::kNumA; ++ph_i) {
           float* acc = (ph_i == 0) ? acc0 : acc1;
           const float4* sc4 = reinterpret_cast<const float4*>(comb0 + ph_i * BN);
-          uint32_t v[CPT];
-          if constexpr (CPT % 32 == 0) {
 #pragma unroll
-            for (int ch = 0; ch < CPT / 32; ++ch)
-              tmem_ld32(taddr + ph_i * BN + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[ch * 32]));
-          } else {
+          for (int c0 = 0; c0 < CPT; c0 += kChunk) {
+            uint32_t v[kChunk];
+            uint32_t vlo[Tr::kMergeB ? kChunk : 1];
+            const uint32_t ta = taddr + ph_i * Tr::kMmaN + c0;
+            if constexpr (kChunk % 32 == 0) {
 #pragma unroll
-            for (int ch = 0; ch < CPT / 16; ++ch)
-              tmem_ld16(taddr + ph_i * BN + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[ch * 16]));
-          }
-          tmem_wait_ld();
+              for (int ch = 0; ch < kChunk / 32; ++ch) {
+                tmem_ld32(ta + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&v[ch * 32]));
+                if constexpr (Tr::kMergeB)
+                  tmem_ld32(ta + BN + ch * 32, *reinterpret_cast<uint32_t(*)[32]>(&vlo[ch * 32]));
+              }
+            } else {
 #pragma unroll
-          for (int c4 = 0; c4 < CPT / 4; ++c4) {
-            const float4 sc = sc4[c4];
-            acc[4 * c4 + 0] = fmaf(__uint_as_float(v[4 * c4 + 0]), sc.x, acc[4 * c4 + 0]);
-            acc[4 * c4 + 1] = fmaf(__uint_as_float(v[4 * c4 + 1]), sc.y, acc[4 * c4 + 1]);
-            acc[4 * c4 + 2] = fmaf(__uint_as_float(v[4 * c4 + 2]), sc.z, acc[4 * c4 + 2]);
-            acc[4 * c4 + 3] = fmaf(__uint_as_float(v[4 * c4 + 3]), sc.w, acc[4 * c4 + 3]);
+              for (int ch = 0; ch < kChunk / 16; ++ch) {
+                tmem_ld16(ta + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&v[ch * 16]));
+                if constexpr (Tr::kMergeB)
+                  tmem_ld16(ta + BN + ch * 16, *reinterpret_cast<uint32_t(*)[16]>(&vlo[ch * 16]));
+              }
+            }
+            tmem_wait_ld();
+#pragma unroll
+            for (int c4 = 0; c4 < kChunk / 4; ++c4) {
+              const float4 sc = sc4[c0 / 4 + c4];
+              const float scv[4] = {sc.x, sc.y, sc.z, sc.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int c = 4 * c4 + j;
+                float x = __uint_as_float(v[c]);
+                if constexpr (Tr::kMergeB) x += __uint_as_float(vlo[c]);
+                acc[c0 + c] = fmaf(x, scv[j], acc[c0 + c]);
+              }
+            }
           }
         }
         tc_fence_before();
@@ -788,29 +793,20 @@ static cudaError_t launch_one(const CUtensorMap& w, const CUtensorMap& b0, const
   if (checked_device != dev) {
     err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Tr::kSmemBytes);
     if (err != cudaSuccess) return err;
-    if constexpr (Tr::kSplitRegs) {
-      // The warpgroup register split is only safe if the block launches with
-      // exactly the registers it was sized for.
-      cudaFuncAttributes attr;
-      err = cudaFuncGetAttributes(&attr, kern);
-      if (err != cudaSuccess) return err;
-      if (attr.numRegs != Tr::kLaunchRegs) return cudaErrorInvalidConfiguration;
-    }
     checked_device = dev;
   }
   return launch_kernel(kern, grid, Tr::kThreads, Tr::kSmemBytes, stream, true, w, b0, b1, p,
                        early_tables ? 1 : 0);
 }
 
+// Decode (T <= 64): kGemm1Split / kGemm2Wide with 16-token tiles; mid-size
+// batches (64 < T < 512): kGemm1Fused / kGemm2 with 64-token tiles; larger
+// batches use the token-major kernels (gemm_tm_sm100.cu).
 #define MOE_GEMM_CONFIGS(X)            \
-  X(kGemm1Fused, 128, 4, 8)            \
   X(kGemm1Fused, 64, 5, 4)             \
   X(kGemm1Split, 16, 6, 4)             \
-  X(kGemm2, 128, 4, 8)                 \
-  X(kGemm2Wide, 128, 3, 8)             \
   X(kGemm2Wide, 16, 6, 4)              \
-  X(kGemm2, 64, 6, 4)                  \
-  X(kGemm2, 16, 10, 4)
+  X(kGemm2, 64, 6, 4)
 
 cudaError_t launch_moe_gemm(int kind, int bn, const CUtensorMap& w, const CUtensorMap& b0,
                             const CUtensorMap& b1, const GemmParams& p, int grid,

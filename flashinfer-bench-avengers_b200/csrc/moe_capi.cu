@@ -53,9 +53,9 @@ Plan choose_plan(int64_t T) {
     p.g2_wide = true;
   } else {
     p.decode = false;
-    p.g1_bn = T >= 1024 ? 128 : 64;
-    p.g2_bn = T >= 1024 ? 128 : 64;
-    p.g2_wide = T >= 1024;
+    p.g1_bn = 64;
+    p.g2_bn = 64;
+    p.g2_wide = false;
     p.token_major = T >= kTokenMajorMinTokens;
   }
   return p;
