@@ -69,7 +69,13 @@ struct TmTraits {
   static constexpr int kOffCnt = kOffSeg + 34 * 4;
   static constexpr int kOffUnits = kOffCnt + 32 * 4;
   static constexpr int kOffRed = kOffUnits + kUnitSlots * 4;   // [2][BM] row maxima (GEMM1)
-  static constexpr int kSmemBytes = kOffRed + 2 * BM * 4 + 1024;
+  // GEMM2 combine staging: per epilogue warp 32 rows x 16 floats, rows
+  // kStagePitch bytes apart (64 B of data + 16 B pad: conflict-free float4
+  // stores from lanes that each own a row).
+  static constexpr int kStagePitch = 80;
+  static constexpr int kOffStage = kOffRed + 2 * BM * 4;
+  static constexpr int kStageWarpBytes = 32 * kStagePitch;
+  static constexpr int kSmemBytes = kOffStage + (kG1 ? 0 : kEpiWarps * kStageWarpBytes) + 1024;
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -79,6 +85,31 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c),
                "f"(d)
                : "memory");
+}
+
+// Two fp32 lanes in one 64-bit register pair, for the packed FMA below.
+__device__ __forceinline__ uint64_t pack_f32x2(uint32_t lo_bits, uint32_t hi_bits) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo_bits), "r"(hi_bits));
+  return r;
+}
+
+__device__ __forceinline__ void unpack_f32x2(uint64_t p, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(p));
+}
+
+// d = a * b + c on two fp32 lanes at once (two IEEE round-to-nearest FMAs in
+// one instruction): halves the promotion's FMA issue slots.
+__device__ __forceinline__ uint64_t ffma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
+// silu(g) * u with the fast exponential and division (relative error ~1e-7,
+// far below the 8-bit precision C keeps as the hi/lo e4m3 pair).
+__device__ __forceinline__ float silu_mul_fast(float g, float u) {
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
 __device__ __forceinline__ uint32_t pack_e4m3x4(float a, float b, float c, float d) {
@@ -315,7 +346,8 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     bool ok = true;
     // GEMM1: acc0 = up, acc1 = gate for intermediate columns hf*64 .. +64.
     // GEMM2: acc0 / acc1 = W2 rows (2*blk + hf)*128 + [0, 64) / [64, 128).
-    float acc0[64], acc1[64];
+    // Kept as packed pairs (column 2i in the low half) for f32x2 FMAs.
+    uint64_t acc0p[32], acc1p[32];
     while (ok) {
       if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
       const int u = s_units[uslot];
@@ -335,20 +367,32 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         }
       }
 #pragma unroll
-      for (int c = 0; c < 64; ++c) { acc0[c] = 0.f; acc1[c] = 0.f; }
-      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
-        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue)) {
-          ok = false;
-          break;
-        }
+      for (int i = 0; i < 32; ++i) { acc0p[i] = 0ull; acc1p[i] = 0ull; }
+      // Scales of one K block (token scale x weight-block scale): GEMM1 up /
+      // gate, GEMM2 this half's W2 block for both phases. They are read one
+      // K block ahead, while the MMA of the current block still runs.
+      auto read_scales = [&](float& a0, float& a1) -> bool {
+        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue)) return false;
         const float* sp = ring + slot * Tr::kSlotFloats;
         const float ts = sp[r];
-        // GEMM1: up / gate scales; GEMM2: this half's W2 block scale for both phases
-        const float s0 = ts * (kG1 ? sp[Tr::BM] : sp[Tr::BM + hf]);
-        const float s1 = kG1 ? ts * sp[Tr::BM + 1] : s0;
+        a0 = ts * (kG1 ? sp[Tr::BM] : sp[Tr::BM + hf]);
+        a1 = kG1 ? ts * sp[Tr::BM + 1] : a0;
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sempty_bar[slot]));
         if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+        return true;
+      };
+      float ns0 = 0.f, ns1 = 0.f;
+      if (!read_scales(ns0, ns1)) {
+        ok = false;
+        break;
+      }
+      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+        const float s0 = ns0, s1 = ns1;
+        if (kb + 1 < Tr::kKBlocks && !read_scales(ns0, ns1)) {
+          ok = false;
+          break;
+        }
         if (!mbar_wait(smem_u32(&accf_bar[abuf]), aph, s_abort, p.status, kStatusTimeoutEpilogue)) {
           ok = false;
           break;
@@ -357,12 +401,14 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         const uint32_t tb = lane_base + abuf * Tr::kAccCols;
         const uint32_t col_a = kG1 ? hf * 64 : hf * 128;
         const uint32_t col_b = kG1 ? 128 + hf * 64 : hf * 128 + 64;
+        const uint64_t s0p = pack_f32x2(__float_as_uint(s0), __float_as_uint(s0));
+        const uint64_t s1p = pack_f32x2(__float_as_uint(s1), __float_as_uint(s1));
         uint32_t v[64];
         tmem_ld32(tb + col_a, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_ld32(tb + col_a + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc0[c] = fmaf(__uint_as_float(v[c]), s0, acc0[c]);
+        for (int i = 0; i < 32; ++i) acc0p[i] = ffma_f32x2(pack_f32x2(v[2 * i], v[2 * i + 1]), s0p, acc0p[i]);
         tmem_ld32(tb + col_b, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_ld32(tb + col_b + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
         tmem_wait_ld();
@@ -371,9 +417,15 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         if (lane == 0) mbar_arrive(smem_u32(&acce_bar[abuf]));
         if (++abuf == 2) { abuf = 0; aph ^= 1; }
 #pragma unroll
-        for (int c = 0; c < 64; ++c) acc1[c] = fmaf(__uint_as_float(v[c]), s1, acc1[c]);
+        for (int i = 0; i < 32; ++i) acc1p[i] = ffma_f32x2(pack_f32x2(v[2 * i], v[2 * i + 1]), s1p, acc1p[i]);
       }
       if (!ok) break;
+      float acc0[64], acc1[64];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        unpack_f32x2(acc0p[i], acc0[2 * i], acc0[2 * i + 1]);
+        unpack_f32x2(acc1p[i], acc1[2 * i], acc1[2 * i + 1]);
+      }
 
       // ------------------------------------------------- final epilogue
       const int64_t row = t.row0 + r;
@@ -381,8 +433,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         float m = 0.f;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {
-          const float g = acc1[c];
-          acc0[c] = g / (1.0f + expf(-g)) * acc0[c];
+          acc0[c] = silu_mul_fast(acc1[c], acc0[c]);
           m = fmaxf(m, fabsf(acc0[c]));
         }
         named_bar_sync(1, 32 * Tr::kEpiWarps);
@@ -413,14 +464,35 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
           }
         }
       } else {
-        if (valid) {
-          float* dst = p.y_acc + static_cast<int64_t>(my_tok) * kHidden + (2 * t.blk + hf) * kBlk;
+        // w * O into the combine rows. Lane l holds 128 consecutive columns
+        // of token row r; red.adds from that layout would send 32 scattered
+        // 16-byte requests per instruction. Instead each 16-column chunk goes
+        // through this warp's staging rows and is read back transposed, so
+        // one instruction adds 64 contiguous bytes to each of 8 rows.
+        uint8_t* stage_w = smem + Tr::kOffStage + (warp - 4) * Tr::kStageWarpBytes;
+        const int rr = lane >> 2;        // row (of 8) this lane reads back
+        const int cq = lane & 3;         // its 16-byte column quad
+        const float w = valid ? my_w : 0.f;
+        int toks[4];
 #pragma unroll
-          for (int c = 0; c < 64; c += 4)
-            red_add_v4(dst + c, acc0[c] * my_w, acc0[c + 1] * my_w, acc0[c + 2] * my_w, acc0[c + 3] * my_w);
+        for (int j = 0; j < 4; ++j) toks[j] = __shfl_sync(0xffffffffu, valid ? my_tok : -1, 8 * j + rr);
+        float* ybase = p.y_acc + (2 * t.blk + hf) * kBlk + 4 * cq;
 #pragma unroll
-          for (int c = 0; c < 64; c += 4)
-            red_add_v4(dst + 64 + c, acc1[c] * my_w, acc1[c + 1] * my_w, acc1[c + 2] * my_w, acc1[c + 3] * my_w);
+        for (int ch = 0; ch < 8; ++ch) {
+          const float* a = ch < 4 ? &acc0[16 * ch] : &acc1[16 * (ch - 4)];
+          float4* srow = reinterpret_cast<float4*>(stage_w + lane * Tr::kStagePitch);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            srow[j] = make_float4(a[4 * j] * w, a[4 * j + 1] * w, a[4 * j + 2] * w, a[4 * j + 3] * w);
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int row8 = 8 * j + rr;
+            const float4 v4 = *reinterpret_cast<const float4*>(stage_w + row8 * Tr::kStagePitch + 16 * cq);
+            if (toks[j] >= 0)
+              red_add_v4(ybase + static_cast<int64_t>(toks[j]) * kHidden + 16 * ch, v4.x, v4.y, v4.z, v4.w);
+          }
+          __syncwarp();
         }
       }
     }

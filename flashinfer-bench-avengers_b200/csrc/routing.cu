@@ -339,26 +339,33 @@ __device__ __forceinline__ void st_cluster_u32(const void* local, uint32_t rank,
 
 }  // namespace
 
-// Decode batches (T <= kDecodeMaxTokens = 64): routing, permutation and the
-// clears the decode GEMMs rely on, in one cluster of 8 CTAs x 256 threads.
+// Decode batches (T <= kDecodeMaxTokens = 64): routing, permutation, the
+// permuted row copy and the clears the decode GEMMs rely on, in one cluster
+// of 8 CTAs x 256 threads with a single cluster barrier.
 //   1. warp w of CTA r routes token 8r + w and stores its eight selections
-//      into CTA 0's shared memory (distributed shared memory);
-//   2. CTA 0 places the local picks with warp ballots (deterministic,
-//      segments in increasing token order, padded to kSegAlign rows, same
-//      result as permute_kernel) while CTA 1 clears the GEMM unit counters
-//      and the status word;
-//   3. all CTAs copy the valid (token, expert) rows of the hidden states and
-//      their block scales into the permuted buffers (a_perm, sa_perm) and
-//      clear their g1_acc rows, which the K-split GEMM1 accumulates into.
-// Routing runs on eight SMs instead of one: one warp issues about a thousand
+//      into the shared memory of every CTA of the cluster (distributed
+//      shared memory), then starts pulling the token's row into L2 if it
+//      has a local pick;
+//   2. every CTA derives the whole permutation from its own copy of the
+//      selections (warp ballots over 64 tokens: deterministic, segments in
+//      increasing token order, padded to kSegAlign rows, the same result as
+//      permute_kernel) and writes its share of the permuted index arrays;
+//   3. the valid (token, expert) rows are spread over the cluster's 64
+//      warps: each copies its rows of the hidden states and their block
+//      scales into a_perm / sa_perm and clears the matching g1_acc rows.
+// Routing runs on eight SMs rather than one: a warp issues about a thousand
 // instructions per token, which on a single SM would serialise 64 tokens.
+constexpr int kDecodeMaxRows = kDecodeMaxTokens * kTopK + kExpertsLocal * (kSegAlign - 1);
 __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256)
     route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp) {
-  __shared__ int s_idx[kDecodeMaxTokens * kTopK];     // filled in CTA 0 only
+  __shared__ int s_idx[kDecodeMaxTokens * kTopK];   // every CTA holds all selections
   __shared__ float s_w[kDecodeMaxTokens * kTopK];
+  __shared__ int s_ptok[kDecodeMaxRows];             // the permutation, per CTA
+  __shared__ float s_pw[kDecodeMaxRows];
   __shared__ int s_wcnt[2][kExpertsLocal];
   __shared__ int s_start[kExpertsLocal];
   __shared__ int s_cnt[kExpertsLocal];
+  __shared__ int s_cpre[kExpertsLocal];
   pdl_launch_next();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -374,10 +381,13 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
       float w;
       route_token(rp, t, lane, idx, w);
       if (lane < kTopK) {
-        st_cluster_u32(&s_idx[t * kTopK + lane], 0, static_cast<uint32_t>(idx));
-        st_cluster_u32(&s_w[t * kTopK + lane], 0, __float_as_uint(w));
+#pragma unroll
+        for (uint32_t q = 0; q < kDecodeClusterCtas; ++q) {
+          st_cluster_u32(&s_idx[t * kTopK + lane], q, static_cast<uint32_t>(idx));
+          st_cluster_u32(&s_w[t * kTopK + lane], q, __float_as_uint(w));
+        }
       }
-      // A token with a local pick has its row copied in phase 3: start
+      // A token with a local pick has its row copied in step 3: start
       // pulling its 7 KB row and 56 block scales into L2 now.
       const int le = idx - dp.local_expert_offset;
       if (__ballot_sync(0xffffffffu, lane < kTopK && le >= 0 && le < kExpertsLocal)) {
@@ -391,8 +401,8 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
   }
   cluster_sync_all();
 
-  // ---- 2. permutation (CTA 0) / counter clears (CTAs 1..7) ------------------
-  if (rank == 0) {
+  // ---- 2. permutation (every CTA, from its own copy) ------------------------
+  {
     const int t = tid;   // token of this thread (warps 0 and 1)
     int sidx[kTopK];
     float sw[kTopK];
@@ -429,16 +439,27 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
       const int c = s_wcnt[0][lane] + s_wcnt[1][lane];
       const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
       int incl = padded;
+      int cincl = c;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int o = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += o;
+        const int co = __shfl_up_sync(0xffffffffu, cincl, off);
+        if (lane >= off) {
+          incl += o;
+          cincl += co;
+        }
       }
       s_start[lane] = incl - padded;
       s_cnt[lane] = c;
-      dp.counts[lane] = c;
-      dp.seg_off[lane + 1] = incl;
-      if (lane == 0) dp.seg_off[0] = 0;
+      s_cpre[lane] = cincl - c;
+      if (rank == 0) {
+        dp.counts[lane] = c;
+        dp.seg_off[lane + 1] = incl;
+        if (lane == 0) dp.seg_off[0] = 0;
+      }
+    } else if (rank == 1 && warp == 2) {
+      if (lane < 4) dp.sched[lane] = 0;
+      if (lane == 4) *dp.status = 0;
     }
     __syncthreads();
     if (warp < 2) {
@@ -455,49 +476,42 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
           for (int k = 0; k < kTopK; ++k) {
             if (sidx[k] == e) w = sw[k];
           }
-          dp.perm_tok[s_start[e] + r] = t;
-          dp.perm_w[s_start[e] + r] = w;
+          s_ptok[s_start[e] + r] = t;
+          s_pw[s_start[e] + r] = w;
         }
       }
     } else {
-      // padding rows: 32 experts x kSegAlign slots over threads 64..575
+      // padding rows: 32 experts x kSegAlign slots over threads 64..255
       for (int i = tid - 64; i < kExpertsLocal * kSegAlign; i += blockDim.x - 64) {
         const int e = i / kSegAlign;
         const int j = i % kSegAlign;
         const int c = s_cnt[e];
         const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
         if (c + j < padded) {
-          dp.perm_tok[s_start[e] + c + j] = -1;
-          dp.perm_w[s_start[e] + c + j] = 0.f;
+          s_ptok[s_start[e] + c + j] = -1;
+          s_pw[s_start[e] + c + j] = 0.f;
         }
       }
     }
-  } else {
-    if (rank == 1 && tid < 4) dp.sched[tid] = 0;
-    if (rank == 1 && tid == 4) *dp.status = 0;
+    __syncthreads();
+    // this CTA's share of the permuted index arrays
+    const int nrows = s_start[kExpertsLocal - 1] + (s_cnt[kExpertsLocal - 1] + kSegAlign - 1) / kSegAlign * kSegAlign;
+    for (int i = static_cast<int>(rank) * blockDim.x + tid; i < nrows; i += kDecodeClusterCtas * blockDim.x) {
+      dp.perm_tok[i] = s_ptok[i];
+      dp.perm_w[i] = s_pw[i];
+    }
   }
-  cluster_sync_all();
 
   // ---- 3. permuted rows and g1_acc clears of the valid pairs ---------------
-  // Valid pair v (0 <= v < sum of counts) is row seg_off[e] + v - cpre[e] of
-  // expert e, cpre = exclusive prefix of the counts. One warp per row.
+  // Valid pair v (0 <= v < sum of counts) is row s_start[e] + v - s_cpre[e]
+  // of expert e. One warp per row.
   {
-    const int cnt = __ldcg(dp.counts + lane);
-    const int seg = __ldcg(dp.seg_off + lane);
-    int incl = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
-    }
-    const int total = __shfl_sync(0xffffffffu, incl, 31);
-    const int gw = static_cast<int>(rank) * 8 + warp;
-    for (int v = gw; v < total; v += kDecodeClusterCtas * 8) {
-      // expert of pair v: the number of experts whose inclusive prefix is <= v
+    const int incl = s_cpre[lane] + s_cnt[lane];
+    const int pairs = __shfl_sync(0xffffffffu, incl, 31);
+    for (int v = static_cast<int>(rank) * 8 + warp; v < pairs; v += kDecodeClusterCtas * 8) {
       const int e = __popc(__ballot_sync(0xffffffffu, incl <= v));
-      const int row = __shfl_sync(0xffffffffu, seg, e) + v - (__shfl_sync(0xffffffffu, incl, e) -
-                                                                __shfl_sync(0xffffffffu, cnt, e));
-      const int tok = __ldcg(dp.perm_tok + row);
+      const int row = s_start[e] + v - s_cpre[e];
+      const int tok = s_ptok[row];
       // every load first, then the stores (the clears do not wait for them)
       const uint4* src = reinterpret_cast<const uint4*>(dp.hidden + static_cast<int64_t>(tok) * kHidden);
       uint4 rowv[kHidden / 16 / 32];
