@@ -76,10 +76,7 @@ PUBLISHED_US = {1: 551.0, 7: 1034.0, 14: 1609.0, 15: 850.0, 16: 1727.0, 32: 2803
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
 # the ncu captures summarised in profiles/, keyed by (kernel, T) of the bench
 # workloads; None when no capture of that launch exists.
-NCU_TRAFFIC_BYTES = {
-    ("gemm1", 64): 472_598_016 + 4_210_944,        # profiles/decode_gemms_T64.md
-    ("gemm1", 4096): 947_077_376 + 75_514_368,     # profiles/gemm1_token_major_prefill_T4096_hot.md
-}
+NCU_TRAFFIC_BYTES = {("gemm1", 64): 472_755_200 + 6_154_240, ("gemm1", 4096): 869_044_736 + 74_441_216}
 
 
 def load_peaks() -> dict:

@@ -352,7 +352,7 @@ using namespace moe;
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 5; }
+int moe_b200_abi_version(void) { return 4; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
