@@ -11,19 +11,38 @@
 
 namespace moe {
 
-// n4 = number of float4 groups (T * 7168 / 4).
-__global__ void __launch_bounds__(256) finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4) {
+// Output row t comes from combine row tok_slot[t] (zeros when -1: the token
+// has no local pick), or from row t when tok_slot is null. A CTA step covers
+// one 2048-column segment of a row (4 per row); a thread converts 8 columns
+// (two float4 loads, one 16-byte store).
+__global__ void __launch_bounds__(256) finalize_kernel(const float* y_acc, const int32_t* tok_slot,
+                                                       uint16_t* out, int num_tokens) {
   pdl_launch_next();
   pdl_wait();
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n4; i += stride) {
-    const float4 v = reinterpret_cast<const float4*>(y_acc)[i];
-    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y);
-    const __nv_bfloat162 b = __floats2bfloat162_rn(v.z, v.w);
-    uint2 o;
-    o.x = *reinterpret_cast<const uint32_t*>(&a);
-    o.y = *reinterpret_cast<const uint32_t*>(&b);
-    reinterpret_cast<uint2*>(out)[i] = o;
+  constexpr int kOcts = kHidden / 8;   // 896 groups of 8 columns per row
+  constexpr int kSegs = 4;             // ceil(896 / 256)
+  const int items = num_tokens * kSegs;
+  for (int it = blockIdx.x; it < items; it += gridDim.x) {
+    const int t = it / kSegs;
+    const int j = (it % kSegs) * 256 + threadIdx.x;
+    if (j >= kOcts) continue;
+    const int slot = tok_slot != nullptr ? __ldg(tok_slot + t) : t;
+    uint4* orow = reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * kHidden);
+    if (slot < 0) {
+      orow[j] = make_uint4(0u, 0u, 0u, 0u);
+      continue;
+    }
+    const float4* yrow = reinterpret_cast<const float4*>(y_acc + static_cast<int64_t>(slot) * kHidden);
+    {
+      const float4 a = yrow[2 * j];
+      const float4 b = yrow[2 * j + 1];
+      const __nv_bfloat162 p0 = __floats2bfloat162_rn(a.x, a.y);
+      const __nv_bfloat162 p1 = __floats2bfloat162_rn(a.z, a.w);
+      const __nv_bfloat162 p2 = __floats2bfloat162_rn(b.x, b.y);
+      const __nv_bfloat162 p3 = __floats2bfloat162_rn(b.z, b.w);
+      orow[j] = make_uint4(*reinterpret_cast<const uint32_t*>(&p0), *reinterpret_cast<const uint32_t*>(&p1),
+                           *reinterpret_cast<const uint32_t*>(&p2), *reinterpret_cast<const uint32_t*>(&p3));
+    }
   }
 }
 

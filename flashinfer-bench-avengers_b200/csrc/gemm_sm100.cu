@@ -656,7 +656,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       float my_w = 0.f;
       if constexpr (!Tr::kIsG1) {
         if (et < BN && et < t.nvalid) {
-          my_tok = p.perm_tok[t.row0 + et];
+          my_tok = p.perm_row[t.row0 + et];
           my_w = p.perm_w[t.row0 + et];
         }
       }

@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       float my_w = 0.f;
       if constexpr (!kG1) {
         if (valid) {
-          my_tok = p.perm_tok[t.row0 + r];
+          my_tok = p.perm_row[t.row0 + r];
           my_w = p.perm_w[t.row0 + r];
         }
       }

@@ -78,11 +78,12 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   l.counts = off;
   l.status = off + kExpertsLocal * sizeof(int);
   l.sched = l.status + 16;
-  off = align_up(l.sched + 4 * sizeof(int));
+  l.n_touched = l.sched + 4 * sizeof(int);
+  off = align_up(l.n_touched + sizeof(int));
   l.seg_off = off;
   off = align_up(off + (kExpertsLocal + 1) * sizeof(int));
   l.chunk_counts = off;
-  off = align_up(off + static_cast<size_t>((T + 1023) / 1024) * kExpertsLocal * sizeof(int));
+  off = align_up(off + static_cast<size_t>((T + 1023) / 1024) * (kExpertsLocal + 1) * sizeof(int));
   l.topk_idx = off;
   off = align_up(off + cap * sizeof(int32_t));
   l.topk_w = off;
@@ -91,6 +92,10 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   off = align_up(off + cap * sizeof(int32_t));
   l.perm_w = off;
   off = align_up(off + cap * sizeof(float));
+  l.perm_row = off;
+  off = align_up(off + cap * sizeof(int32_t));
+  l.tok_slot = off;
+  off = align_up(off + static_cast<size_t>(T) * sizeof(int32_t));
   l.a_perm = off;
   off = align_up(off + cap * kHidden);
   l.sa_perm = off;
@@ -304,6 +309,7 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   g1.seg_off = seg_off;
   g1.counts = counts;
   g1.perm_tok = perm_tok;
+  g1.perm_row = perm_tok;   // decode: y_acc has one row per token
   g1.perm_w = perm_w;
   g1.act_scale = sa_perm;
   g1.w_scale = gemm1_weights_scale;
@@ -335,11 +341,9 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
     return MOE_B200_ERR_CUDA;
   mark_stage(5, s);
 
-  const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
-  int fgrid = static_cast<int>(div_up(n4, 256));
-  if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
+  const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
   if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
-                    static_cast<uint16_t*>(output), n4) != cudaSuccess)
+                    static_cast<const int32_t*>(nullptr), static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;
@@ -352,7 +356,7 @@ using namespace moe;
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 4; }
+int moe_b200_abi_version(void) { return 5; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
@@ -475,6 +479,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   uint8_t* c_lo = ws + l.c_lo;
   float* c_scale = reinterpret_cast<float*>(ws + l.c_scale);
   float* y_acc = reinterpret_cast<float*>(ws + l.y_acc);
+  int32_t* perm_row = reinterpret_cast<int32_t*>(ws + l.perm_row);
+  int32_t* tok_slot = reinterpret_cast<int32_t*>(ws + l.tok_slot);
+  int* n_touched = reinterpret_cast<int*>(ws + l.n_touched);
 
   if (plan.decode)
     return run_decode(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale,
@@ -517,6 +524,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.seg_off = seg_off;
   pp.perm_tok = perm_tok;
   pp.perm_w = perm_w;
+  pp.perm_row = perm_row;
+  pp.tok_slot = tok_slot;
+  pp.n_touched = n_touched;
   if (T <= 1024) {
     if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
@@ -527,6 +537,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   }
   GatherParams gp;
   gp.seg_off = seg_off;
+  gp.n_touched = n_touched;
   gp.perm_tok = perm_tok;
   gp.hidden = static_cast<const uint8_t*>(hidden_states);
   gp.hidden_scale = hidden_states_scale;
@@ -535,7 +546,6 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   gp.a_perm = a_perm;
   gp.sa_perm = sa_perm;
   gp.y_acc = y_acc;
-  gp.g1_acc = nullptr;
   int ggrid = static_cast<int>(div_up(cap, 8));
   if (ggrid < di.sm_count) ggrid = di.sm_count;
   if (ggrid > di.sm_count * 4) ggrid = di.sm_count * 4;
@@ -547,6 +557,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g1.seg_off = seg_off;
   g1.counts = counts;
   g1.perm_tok = perm_tok;
+  g1.perm_row = perm_row;
   g1.perm_w = perm_w;
   g1.act_scale = sa_perm;
   g1.w_scale = gemm1_weights_scale;
@@ -588,11 +599,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   }
   mark_stage(5, s);
 
-  const int64_t n4 = static_cast<int64_t>(T) * kHidden / 4;
-  int fgrid = static_cast<int>(div_up(n4, 256));
-  if (fgrid > di.sm_count * 8) fgrid = di.sm_count * 8;
+  const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
   if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
-                    static_cast<uint16_t*>(output), n4) != cudaSuccess)
+                    static_cast<const int32_t*>(tok_slot), static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;

@@ -24,7 +24,7 @@ struct PermuteParams {
   const int32_t* topk_idx;  // [T, 8]
   const float* topk_w;      // [T, 8]
   int* counts;              // [32] assignments per local expert (written)
-  int* chunk_counts;        // [ceil(T/1024), 32] per-chunk counts (multi-CTA path)
+  int* chunk_counts;        // [ceil(T/1024), 33] per-chunk expert counts + touched tokens (multi-CTA path)
   uint32_t* status;         // device status word (cleared)
   int* sched;               // [4] GEMM unit counters (cleared)
   int num_tokens;
@@ -32,10 +32,16 @@ struct PermuteParams {
   int* seg_off;             // [33] segment starts (multiples of kSegAlign)
   int32_t* perm_tok;        // [cap] token of each permuted row, -1 for padding
   float* perm_w;            // [cap] routing weight of each permuted row
+  // Combine rows: only tokens with at least one local pick ("touched") get a
+  // row of the fp32 combine buffer, numbered in token order.
+  int32_t* tok_slot;        // [T] combine row of each token, -1 if untouched
+  int32_t* perm_row;        // [cap] combine row of each permuted row, -1 for padding
+  int* n_touched;           // [1] number of touched tokens
 };
 
 struct GatherParams {
   const int* seg_off;       // [33]
+  const int* n_touched;     // [1] rows of y_acc in use
   const int32_t* perm_tok;  // [cap]
   const uint8_t* hidden;    // [T, 7168] e4m3
   const float* hidden_scale;  // [56, T]
@@ -43,8 +49,7 @@ struct GatherParams {
   int cap;
   uint8_t* a_perm;          // [cap, 7168] e4m3
   float* sa_perm;           // [56, cap]
-  float* y_acc;             // [T, 7168] cleared
-  float* g1_acc;            // [cap, 4096] used rows cleared; null unless K-split
+  float* y_acc;             // [n_touched, 7168] cleared
 };
 
 // Decode batches (num_tokens <= kDecodeMaxTokens) use a dedicated front end:
@@ -81,6 +86,7 @@ struct GemmParams {
   const int* seg_off;       // [33] padded segment starts
   const int* counts;        // [32] valid rows per segment
   const int32_t* perm_tok;  // [cap]
+  const int32_t* perm_row;  // [cap] combine row of each permuted row (GEMM2 epilogues)
   const float* perm_w;      // [cap]
   const float* act_scale;   // GEMM1: sa_perm [56, cap]; GEMM2: c_scale [16, cap]
   const float* w_scale;     // GEMM1: [32, 32, 56]; GEMM2: [32, 56, 16]
@@ -125,7 +131,7 @@ __global__ void permute_kernel(PermuteParams p);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
-__global__ void finalize_kernel(const float* y_acc, uint16_t* out, int64_t n4);
+__global__ void finalize_kernel(const float* y_acc, const int32_t* tok_slot, uint16_t* out, int num_tokens);
 __global__ void route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp);
 
 }  // namespace moe

@@ -198,6 +198,7 @@ __device__ __forceinline__ void permute_body(const PermuteParams& p) {
   __shared__ int s_run[kExpertsLocal];
   __shared__ int s_wcnt[32][kExpertsLocal];  // [warp][expert]
   __shared__ int s_wpre[32][kExpertsLocal];
+  __shared__ int s_wtouch[32];               // touched tokens per warp
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -245,11 +246,13 @@ __device__ __forceinline__ void permute_body(const PermuteParams& p) {
     if (c + j < padded) {
       p.perm_tok[s_run[e] + c + j] = -1;
       p.perm_w[s_run[e] + c + j] = 0.f;
+      p.perm_row[s_run[e] + c + j] = -1;
     }
   }
 
-  // ---- pass 2: positions -------------------------------------------------
+  // ---- pass 2: positions and combine rows ---------------------------------
   const uint32_t lt_mask = (1u << lane) - 1u;
+  int trun = 0;   // touched tokens of earlier chunks (the same in every thread)
   for (int base = 0; base < p.num_tokens; base += 1024) {
     const int t = base + tid;
     int sidx[kTopK];
@@ -270,7 +273,25 @@ __device__ __forceinline__ void permute_body(const PermuteParams& p) {
         ++nset;
       }
     }
+    const uint32_t tbal = __ballot_sync(0xffffffffu, mask != 0u);
+    if (lane == 0) s_wtouch[warp] = __popc(tbal);
     __syncthreads();
+
+    // Combine row of this token: touched tokens numbered in token order.
+    int slot = -1;
+    {
+      const int wt = s_wtouch[lane];
+      int before = lane < warp ? wt : 0;
+      int total = wt;
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) {
+        before += __shfl_xor_sync(0xffffffffu, before, off);
+        total += __shfl_xor_sync(0xffffffffu, total, off);
+      }
+      if (mask != 0u) slot = trun + before + __popc(tbal & lt_mask);
+      if (t < p.num_tokens) p.tok_slot[t] = slot;
+      trun += total;
+    }
 
     // Warp w scans expert w over the 32 warps of the chunk.
     {
@@ -304,8 +325,10 @@ __device__ __forceinline__ void permute_body(const PermuteParams& p) {
       const int pos = s_wpre[warp][e] + r;
       p.perm_tok[pos] = t;
       p.perm_w[pos] = w;
+      p.perm_row[pos] = slot;
     }
   }
+  if (tid == 0) *p.n_touched = trun;
 }
 
 __global__ void __launch_bounds__(1024) permute_kernel(PermuteParams p) {
@@ -536,8 +559,11 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
 // each chunk's per-expert counts; permute_place_kernel derives the segment
 // starts from all chunks' counts and places its chunk's tokens after those
 // of earlier chunks.
+constexpr int kChunkStride = kExpertsLocal + 1;   // chunk_counts row: 32 expert counts + touched tokens
+
 __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
   __shared__ int s_wcnt[32][kExpertsLocal];
+  __shared__ int s_wtouch[32];
   pdl_launch_next();
   pdl_wait();
   const int tid = threadIdx.x;
@@ -553,12 +579,18 @@ __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
     if (lane == e) my_count = __popc(bal);
   }
   s_wcnt[warp][lane] = my_count;
+  const uint32_t tbal = __ballot_sync(0xffffffffu, mask != 0u);
+  if (lane == 0) s_wtouch[warp] = __popc(tbal);
   __syncthreads();
   if (warp == 0) {
     int c = 0;
 #pragma unroll 8
     for (int w = 0; w < 32; ++w) c += s_wcnt[w][lane];
-    p.chunk_counts[blockIdx.x * kExpertsLocal + lane] = c;
+    p.chunk_counts[blockIdx.x * kChunkStride + lane] = c;
+    int tt = s_wtouch[lane];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) tt += __shfl_xor_sync(0xffffffffu, tt, off);
+    if (lane == 0) p.chunk_counts[blockIdx.x * kChunkStride + kExpertsLocal] = tt;
   }
 }
 
@@ -568,16 +600,36 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
   __shared__ int s_base[kExpertsLocal];
   __shared__ int s_wcnt[32][kExpertsLocal];
   __shared__ int s_wpre[32][kExpertsLocal];
+  __shared__ int s_wtouch[32];
+  __shared__ int s_tbase;
   pdl_launch_next();
   pdl_wait();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const int chunk = blockIdx.x;
+  if (warp == 1) {
+    // touched tokens of earlier chunks (and in all chunks)
+    int tb = 0, tt = 0;
+    for (int c = lane; c < static_cast<int>(gridDim.x); c += 32) {
+      const int v = p.chunk_counts[c * kChunkStride + kExpertsLocal];
+      tt += v;
+      if (c < chunk) tb += v;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      tb += __shfl_xor_sync(0xffffffffu, tb, off);
+      tt += __shfl_xor_sync(0xffffffffu, tt, off);
+    }
+    if (lane == 0) {
+      s_tbase = tb;
+      if (chunk == 0) *p.n_touched = tt;
+    }
+  }
   if (warp == 0) {
     int total = 0, before = 0;
     for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
-      const int v = p.chunk_counts[c * kExpertsLocal + lane];
+      const int v = p.chunk_counts[c * kChunkStride + lane];
       total += v;
       if (c < chunk) before += v;
     }
@@ -610,6 +662,7 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
     if (c + j < padded) {
       p.perm_tok[s_start[e] + c + j] = -1;
       p.perm_w[s_start[e] + c + j] = 0.f;
+      p.perm_row[s_start[e] + c + j] = -1;
     }
   }
   const int t = chunk * 1024 + tid;
@@ -628,6 +681,8 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
       ++nset;
     }
   }
+  const uint32_t tbal = __ballot_sync(0xffffffffu, mask != 0u);
+  if (lane == 0) s_wtouch[warp] = __popc(tbal);
   __syncthreads();
   {
     const int e = warp;
@@ -639,6 +694,14 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
       if (lane >= off) incl += o;
     }
     s_wpre[lane][e] = s_base[e] + incl - c;
+  }
+  int slot = -1;
+  {
+    int before = lane < warp ? s_wtouch[lane] : 0;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) before += __shfl_xor_sync(0xffffffffu, before, off);
+    if (mask != 0u) slot = s_tbase + before + __popc(tbal & lt_mask);
+    if (t < p.num_tokens) p.tok_slot[t] = slot;
   }
   __syncthreads();
   uint32_t m = mask;
@@ -656,6 +719,7 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
     const int pos = s_wpre[warp][e] + r;
     p.perm_tok[pos] = t;
     p.perm_w[pos] = w;
+    p.perm_row[pos] = slot;
   }
 }
 
@@ -663,9 +727,8 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
 // buffers (one warp per row): a_perm[r, :] = hidden[tok(r), :] and
 // sa_perm[kb, r] = hidden_scale[kb, tok(r)].
 // This replaces per-row TMA gathers inside GEMM1 with plain 2-D tiles.
-// It also clears the buffers that the GEMMs accumulate into with fp32
-// reductions: every row of the combine buffer y_acc and, for the K-split
-// decode plan, the used rows of g1_acc.
+// It also clears the rows of the combine buffer y_acc that GEMM2 adds into
+// (one per token with a local pick).
 __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
   // Releases GEMM1 only after the permutation has completed: GEMM1 reads the
   // segment table before its own wait to prefetch weight tiles.
@@ -675,7 +738,7 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
   const int lane = threadIdx.x & 31;
   const int warps_total = gridDim.x * (blockDim.x >> 5);
   const int64_t nthreads = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const int64_t y4 = static_cast<int64_t>(p.num_tokens) * (kHidden / 4);
+  const int64_t y4 = static_cast<int64_t>(*p.n_touched) * (kHidden / 4);
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < y4; i += nthreads)
     reinterpret_cast<float4*>(p.y_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   // Padding rows are skipped: they only ever feed token columns or rows that
@@ -684,11 +747,6 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
   for (int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); r < rows; r += warps_total) {
     const int tok = p.perm_tok[r];
     if (tok < 0) continue;
-    if (p.g1_acc != nullptr) {
-      float4* g = reinterpret_cast<float4*>(p.g1_acc + static_cast<int64_t>(r) * kGemm1Out);
-#pragma unroll 4
-      for (int i = lane; i < kGemm1Out / 4; i += 32) g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    }
     uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(r) * kHidden);
     const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(tok) * kHidden);
 #pragma unroll

@@ -60,6 +60,9 @@ class WorkspaceLayout(ctypes.Structure):
         ("cap_rows", ctypes.c_int64),
         ("chunk_counts", ctypes.c_size_t),
         ("sched", ctypes.c_size_t),
+        ("perm_row", ctypes.c_size_t),
+        ("tok_slot", ctypes.c_size_t),
+        ("n_touched", ctypes.c_size_t),
     ]
 
 

@@ -122,11 +122,15 @@ typedef struct moe_b200_workspace_layout {
   size_t c_hi;        /* e4m3[cap_rows, 2048] */
   size_t c_lo;        /* e4m3[cap_rows, 2048] */
   size_t c_scale;     /* fp32[16, cap_rows] */
-  size_t y_acc;       /* fp32[T, 7168] combine buffer */
+  size_t y_acc;       /* fp32[T, 7168] combine buffer (decode: row t = token t; otherwise
+                         row tok_slot[t], the first n_touched rows in use) */
   size_t g1_acc;      /* fp32[cap_rows, 4096] K-split GEMM1 sums (decode plan, T <= 64; else 0) */
   int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
-  size_t chunk_counts; /* int32[ceil(T/1024), 32] per-chunk expert counts */
+  size_t chunk_counts; /* int32[ceil(T/1024), 33] per-chunk expert counts + touched tokens */
   size_t sched;       /* int32[4] work-unit counters of the GEMM kernels */
+  size_t perm_row;    /* int32[cap_rows] combine row of each permuted row, -1 in padding (not decode) */
+  size_t tok_slot;    /* int32[T] combine row of each token, -1 without a local pick (not decode) */
+  size_t n_touched;   /* int32 number of tokens with a local pick (not decode) */
 } moe_b200_workspace_layout;
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);

@@ -62,7 +62,9 @@ def test_workspace_size_and_layout(lib):
         assert lay.cap_rows == (8 * T + 15) // 16 * 16 + 32 * 16 + 128
         decode = T <= 64
         offs = [lay.counts, lay.seg_off, lay.chunk_counts, lay.topk_idx, lay.topk_w, lay.perm_tok, lay.perm_w,
-                lay.a_perm, lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
+                lay.perm_row, lay.tok_slot, lay.a_perm, lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
+        assert lay.status < lay.sched < lay.n_touched < lay.seg_off
+        assert lay.a_perm - lay.tok_slot >= 4 * T and lay.tok_slot - lay.perm_row >= 4 * lay.cap_rows
         if decode:
             offs += [lay.g1_acc]
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
@@ -114,4 +116,4 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 4
+    assert lib.moe_b200_abi_version() == 5

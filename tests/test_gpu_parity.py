@@ -107,6 +107,18 @@ def test_permutation_bit_exact(host, T, offset, variant):
     hs = inp["hidden_states"].view(torch.uint8).cpu()
     valid = perm_tok >= 0
     assert torch.equal(a_perm[valid], hs[perm_tok[valid]])
+    if T > 64:
+        # combine rows: tokens with a local pick numbered in token order
+        local = (ridx >= offset) & (ridx < offset + 32)
+        touched = local.any(dim=1)
+        expect_slot = torch.where(touched, torch.cumsum(touched.long(), 0) - 1, torch.full_like(touched.long(), -1))
+        tok_slot = ws[lay.tok_slot: lay.tok_slot + 4 * T].view(torch.int32).cpu().long()
+        assert torch.equal(tok_slot, expect_slot)
+        n_touched = int(ws[lay.n_touched: lay.n_touched + 4].view(torch.int32).cpu()[0])
+        assert n_touched == int(touched.sum())
+        perm_row = ws[lay.perm_row: lay.perm_row + 4 * n].view(torch.int32).cpu().long()
+        assert torch.equal(perm_row[valid], expect_slot[perm_tok[valid]])
+        assert bool((perm_row[~valid] == -1).all())
     assert host.read_status(ws) == 0
 
 
