@@ -7,9 +7,10 @@ Workload (the single-B200 decode path): one call of the
 layer on T=64 tokens, 32 local experts, seeded synthetic inputs with the
 benchmark distributions (flashinfer-bench-avengers_b200/workloads.py). With
 N>1 GPUs (torchrun) every rank owns a different 32-expert shard of the
-256 experts (local_expert_offset = 32*rank) over the same tokens and the
-partial bf16 outputs are summed with an NCCL all-reduce: expert parallelism
-with fixed work per GPU ("weak" scaling).
+256 experts (local_expert_offset = 32*rank) over the same tokens; the
+library's NVLink combine (moe_b200_ep_combine, workspaces in symmetric
+memory) forms the summed bf16 output on every rank: expert parallelism with
+fixed work per GPU ("weak" scaling).
 
 A step is one layer call. Timing: W untimed warm-up steps, then K steps
 bracketed by a barrier and device synchronisation; the reported time is the
@@ -193,19 +194,39 @@ def weights_exceed_l2(st: dict) -> bool:
     return st["E_act"] * (W13_BYTES + W2_BYTES) > 2 * L2_BYTES
 
 
+def layer_call(inp: dict, combiner=None):
+    """One call of the layer on inp's tokens into `out`: the library entry
+    point at N=1, this rank's shard plus the NVLink combine at N>1."""
+    import moe_host
+
+    if combiner is None:
+        args = workloads.as_args(inp)
+        return lambda tokens, out: moe_host.run_dps(tokens["routing_logits"], inp["routing_bias"],
+                                                    tokens["hidden_states"], tokens["hidden_states_scale"],
+                                                    *args[4:], out)
+    return lambda tokens, out: combiner.forward(
+        {"routing_logits": tokens["routing_logits"], "routing_bias": inp["routing_bias"],
+         "hidden_states": tokens["hidden_states"], "hidden_states_scale": tokens["hidden_states_scale"],
+         "routed_scaling_factor": inp["routed_scaling_factor"]},
+        inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"], inp["gemm2_weights_scale"],
+        inp["local_expert_offset"], out)
+
+
 def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=None,
-               do_flush: bool = True) -> dict:
+               do_flush: bool = True, combiner=None) -> dict:
     """Device time of `steps` layer calls replayed from a CUDA graph, each
     after a 256 MB write flush when `do_flush` (otherwise back to back; the
     flushed timing is then taken as well, as `call_ms_flushed`). A second
     graph of the same call records the library's stage events and gives the
     per-stage breakdown (its event nodes add a little latency, so the
-    headline time comes from the graph without them). With a process group
-    the NCCL all-reduce of the partial outputs follows each replay eagerly."""
+    headline time comes from the graph without them). With a combiner (N>1)
+    each call is this rank's shard plus the NVLink combine, both in the
+    graph."""
     import moe_host
     import torch.distributed as dist
 
-    args = workloads.as_args(inp)
+    call = layer_call(inp, combiner)
+    tokens = {k: inp[k] for k in ("routing_logits", "hidden_states", "hidden_states_scale")}
     T = inp["routing_logits"].shape[0]
     dev = inp["routing_logits"].device
     out = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
@@ -213,23 +234,21 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
     for e in ev:
         e.record()
     for _ in range(warmup):
-        moe_host.run_dps(*args, out)
+        call(tokens, out)
     torch.cuda.synchronize()
     cap_stream = torch.cuda.Stream(dev)
     plain, staged = torch.cuda.CUDAGraph(), torch.cuda.CUDAGraph()
     with torch.cuda.stream(cap_stream):
         with torch.cuda.graph(plain, stream=cap_stream):
-            moe_host.run_dps(*args, out)
+            call(tokens, out)
         moe_host.set_stage_events(ev)
         try:
             with torch.cuda.graph(staged, stream=cap_stream):
-                moe_host.run_dps(*args, out)
+                call(tokens, out)
         finally:
             moe_host.set_stage_events(None)
     for _ in range(warmup):
         plain.replay()
-        if group is not None:
-            dist.all_reduce(out, group=group)
     torch.cuda.synchronize()
     if group is not None:
         dist.barrier(group=group)
@@ -242,8 +261,6 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
                 flush.zero_()
             starts[i].record()
             plain.replay()
-            if group is not None:
-                dist.all_reduce(out, group=group)
             ends[i].record()
         torch.cuda.synchronize()
         if group is not None:
@@ -265,16 +282,14 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
             "stage_ms": {k: statistics.mean(v) for k, v in stage_ms.items()}, "out": out}
 
 
-def time_e2e(inp: dict, steps: int, warmup: int, group=None) -> dict:
+def time_e2e(inp: dict, steps: int, warmup: int, group=None, combiner=None) -> dict:
     """The public API call with host buffers: every step copies its
     activations host->device from pinned memory, runs the layer through
     moe_host.run_dps and copies the bf16 result device->host. Copies run on
     their own streams with two buffer sets, so step i+1's upload and step
     i-1's download overlap step i's compute; the timed region spans the first
     upload to the last download."""
-    import moe_host
-    import torch.distributed as dist
-
+    call = layer_call(inp, combiner)
     dev = inp["routing_logits"].device
     T = inp["routing_logits"].shape[0]
     keys = ("routing_logits", "hidden_states", "hidden_states_scale")
@@ -302,12 +317,7 @@ def time_e2e(inp: dict, steps: int, warmup: int, group=None) -> dict:
             uploaded[b].record(up)
         compute.wait_event(uploaded[b])
         compute.wait_event(downloaded[b])        # out[b] has been read back
-        moe_host.run_dps(dev_in[b]["routing_logits"], inp["routing_bias"], dev_in[b]["hidden_states"],
-                         dev_in[b]["hidden_states_scale"], inp["gemm1_weights"], inp["gemm1_weights_scale"],
-                         inp["gemm2_weights"], inp["gemm2_weights_scale"], inp["local_expert_offset"],
-                         inp["routed_scaling_factor"], out[b])
-        if group is not None:
-            dist.all_reduce(out[b], group=group)
+        call(dev_in[b], out[b])
         computed[b].record(compute)
         with torch.cuda.stream(down):
             down.wait_event(computed[b])
@@ -447,18 +457,30 @@ def main() -> None:
     if group is not None:
         dist.all_reduce(b2b, op=dist.ReduceOp.MIN, group=group)
     back_to_back = bool(b2b.item())
+    combiner = None
+    if group is not None:
+        import expert_parallel
+        combiner = expert_parallel.NvlinkCombiner(HEADLINE_T, device, group)
     with ClockSampler(device) as clocks:
-        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back)
+        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back, combiner=combiner)
     call_ms = torch.tensor(r["call_ms"], dtype=torch.float64, device=device)
     mean_ms = call_ms.mean()
     if group is not None:
         dist.all_reduce(mean_ms, op=dist.ReduceOp.MAX, group=group)
+    per_rank = None
+    if group is not None:
+        mine = torch.tensor([float(statistics.mean(r["call_ms"])) * 1e3, float(st["E_act"]), float(st["sum_Tk"])],
+                            dtype=torch.float64, device=device)
+        allr = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine, group=group)
+        per_rank = [{"rank": q, "us_per_call": round(float(v[0]), 2), "E_act": int(v[1]), "sum_Tk": int(v[2])}
+                    for q, v in enumerate(allr)]
     mean_ms = float(mean_ms)
     flushed_ms = torch.tensor(r["call_ms_flushed"], dtype=torch.float64, device=device).mean()
     if group is not None:
         dist.all_reduce(flushed_ms, op=dist.ReduceOp.MAX, group=group)
 
-    e2e = time_e2e(inp, args.steps, warmup, group)
+    e2e = time_e2e(inp, args.steps, warmup, group, combiner)
     e2e_ms = torch.tensor(e2e["ms"], dtype=torch.float64, device=device)
     if group is not None:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX, group=group)
@@ -498,7 +520,8 @@ def main() -> None:
                 "e4m3 1x128 / 128x128 block-scaled N(0,1) activations and N(0,0.02) weights",
         "config": {"workload": f"{desc}, 32 local experts per GPU",
                    "T": HEADLINE_T, "local_expert_offset": offset, "E_act": st["E_act"],
-                   "sum_Tk": st["sum_Tk"], "parallelism": f"ep{world}" + (" + NCCL all-reduce" if world > 1 else ""),
+                   "sum_Tk": st["sum_Tk"],
+                   "parallelism": f"ep{world}" + (" + NVLink combine (peer loads/stores, one kernel)" if world > 1 else ""),
                    "l2": ("back to back: each call streams the active experts' weights "
                           f"({st['E_act'] * (W13_BYTES + W2_BYTES) / 1e6:.0f} MB > 2 x 126 MB L2), so no "
                           "weight byte is L2-resident from the previous call; value_l2_write_flushed is the "
@@ -510,6 +533,7 @@ def main() -> None:
         "e2e": {"value": round(float(e2e_ms) * 1e3, 2), "unit": UNIT, "h2d_bytes_per_step": e2e["h2d"],
                 "d2h_bytes_per_step": e2e["d2h"]},
         "gpu_launches": launches_per_call * args.steps,
+        **({"per_rank": per_rank} if per_rank is not None else {}),
         "clocks": clocks.summary(),
     }
 
@@ -525,6 +549,9 @@ def main() -> None:
     if rank == 0:
         print(json.dumps(line), flush=True)
     if group is not None:
+        del combiner   # release the symmetric workspace before the group goes
+        torch.cuda.synchronize()
+        dist.barrier(group=group)
         dist.destroy_process_group()
 
 

@@ -1,0 +1,224 @@
+// Expert-parallel combine over NVLink peer memory.
+//
+// With expert parallelism every rank runs the layer on the same tokens for
+// its own 32-expert shard and leaves the fp32 combine rows in its workspace
+// (moe_b200_run with a null output). This kernel then forms the bf16 output
+// of the whole layer on every rank in one launch:
+//   1. announce "my combine rows are final" to every peer (a release store at
+//      system scope of a call counter into the peer's flag array) and wait
+//      (bounded) until every peer has announced;
+//   2. reduce this rank's 1/W slice of the token rows: for each row, the fp32
+//      rows of all ranks are read over NVLink (plain loads of peer memory),
+//      summed in fp32 in rank order and rounded once to bf16; the result is
+//      stored into the output staging area of every rank (plain stores to
+//      peer memory) -- reduce-scatter and all-gather in one pass, with the
+//      sum formed before the single bf16 rounding;
+//   3. count this CTA's slice as written on every rank (release reduction at
+//      system scope), wait (bounded) until every CTA of every rank has
+//      written into this rank's staging area, and copy it to the caller's
+//      output.
+// Counters only grow (the call number is kept in the EP area), so nothing
+// has to be cleared between calls and the sequence can be captured in a CUDA
+// graph. No multicast and no library kernel touches peer memory; every wait
+// gives up after one second with a status bit instead of hanging.
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "../../include/moe_b200.h"
+#include "moe_kernels.cuh"
+#include "moe_ptx.cuh"
+#include "moe_shapes.cuh"
+
+namespace moe {
+
+namespace {
+
+constexpr uint32_t kStatusTimeoutPeer = 1u << 7;   // a peer never announced / wrote its slice
+constexpr int kEpMaxRanks = 8;
+constexpr int kEpThreads = 256;
+
+// Layout of a rank's expert-parallel area (moe_b200_ep_area_bytes): the
+// counters sit at fixed offsets, so calls with different token counts find
+// them in the same place.
+struct EpArea {
+  static constexpr size_t kFlags = 0;       // int32[kEpMaxRanks]: call number announced by each rank
+  static constexpr size_t kDone = 64;       // int32: CTAs (of all ranks) that wrote into this staging
+  static constexpr size_t kFinished = 68;   // int32: CTAs of this rank that finished a call
+  static constexpr size_t kCalls = 72;      // int32: completed calls of this rank
+  static constexpr size_t kStage = 256;     // bf16[T, 7168] output staging
+};
+
+struct EpParams {
+  uint8_t* area[kEpMaxRanks];          // each rank's EP area (this process's mapping)
+  const float* y[kEpMaxRanks];         // each rank's fp32 combine rows
+  const int32_t* slot[kEpMaxRanks];    // each rank's token -> combine row map, null: row = token
+  uint16_t* out;                       // this rank's output, bf16 [T, 7168]
+  uint32_t* status;                    // this rank's status word
+  int rank, world, num_tokens;
+};
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void red_release_sys_add(int* p, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Spins (bounded) until *p >= target. Returns false on timeout.
+__device__ __forceinline__ bool wait_at_least(const int* p, int target) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (ld_acquire_sys(p) < target) {
+    if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) return false;
+  }
+  return true;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
+  __shared__ int s_ok;
+  pdl_wait();   // this rank's layer (its GEMM2 reductions) has completed
+  const int W = p.world;
+  const int T = p.num_tokens;
+  uint8_t* mine = p.area[p.rank];
+  const int call = *reinterpret_cast<volatile int*>(mine + EpArea::kCalls) + 1;
+
+  // ---- 1. announce and wait for every rank -------------------------------
+  if (threadIdx.x == 0) s_ok = 1;
+  __syncthreads();
+  if (blockIdx.x == 0 && threadIdx.x < W)
+    st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, call);
+  if (threadIdx.x < W &&
+      !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kFlags) + threadIdx.x, call)) {
+    atomicOr(p.status, kStatusTimeoutPeer);
+    s_ok = 0;
+  }
+  __syncthreads();
+  if (!s_ok) return;
+
+  // ---- 2. reduce this rank's rows, store them on every rank ---------------
+  constexpr int kOcts = kHidden / 8;   // 8 columns (two float4 in, one 16-byte bf16 out)
+  const int r0 = static_cast<int>(static_cast<int64_t>(T) * p.rank / W);
+  const int r1 = static_cast<int>(static_cast<int64_t>(T) * (p.rank + 1) / W);
+  const int64_t items = static_cast<int64_t>(r1 - r0) * kOcts;
+  for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items;
+       it += static_cast<int64_t>(gridDim.x) * kEpThreads) {
+    const int t = r0 + static_cast<int>(it / kOcts);
+    const int j = static_cast<int>(it % kOcts);
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int q = 0; q < W; ++q) {
+      const int row = p.slot[q] != nullptr ? p.slot[q][t] : t;
+      if (row < 0) continue;
+      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row) * kHidden) + 2 * j;
+      const float4 u = src[0], v = src[1];
+      a[0] += u.x; a[1] += u.y; a[2] += u.z; a[3] += u.w;
+      a[4] += v.x; a[5] += v.y; a[6] += v.z; a[7] += v.w;
+    }
+    const __nv_bfloat162 b0 = __floats2bfloat162_rn(a[0], a[1]);
+    const __nv_bfloat162 b1 = __floats2bfloat162_rn(a[2], a[3]);
+    const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[4], a[5]);
+    const __nv_bfloat162 b3 = __floats2bfloat162_rn(a[6], a[7]);
+    const uint4 o = make_uint4(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1),
+                               *reinterpret_cast<const uint32_t*>(&b2), *reinterpret_cast<const uint32_t*>(&b3));
+    for (int q = 0; q < W; ++q)
+      reinterpret_cast<uint4*>(p.area[q] + EpArea::kStage + static_cast<int64_t>(t) * kHidden * 2)[j] = o;
+  }
+
+  // ---- 3. count this CTA's slice on every rank, wait for all, copy out -----
+  __syncthreads();
+  if (threadIdx.x < W) {
+    __threadfence_system();
+    red_release_sys_add(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kDone), 1);
+  }
+  if (threadIdx.x == 0 &&
+      !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone), call * W * static_cast<int>(gridDim.x))) {
+    atomicOr(p.status, kStatusTimeoutPeer);
+    s_ok = 0;
+  }
+  __syncthreads();
+  if (s_ok) {
+    const uint4* stage = reinterpret_cast<const uint4*>(mine + EpArea::kStage);
+    uint4* out = reinterpret_cast<uint4*>(p.out);
+    const int64_t n16 = static_cast<int64_t>(T) * kOcts;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; i < n16;
+         i += static_cast<int64_t>(gridDim.x) * kEpThreads)
+      out[i] = stage[i];
+  }
+  // The last CTA of this rank to finish advances the call number (every CTA
+  // has read it by then).
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int f = atomicAdd(reinterpret_cast<int*>(mine + EpArea::kFinished), 1) + 1;
+    if (f == call * static_cast<int>(gridDim.x)) *reinterpret_cast<volatile int*>(mine + EpArea::kCalls) = call;
+  }
+}
+
+}  // namespace moe
+
+using namespace moe;
+
+namespace {
+
+// CTAs of the combine: one constant for every call and rank, because the
+// counters accumulate W x (CTAs per call) per call and must keep the same
+// arithmetic across calls with different token counts.
+constexpr int kEpGrid = 128;
+
+}  // namespace
+
+extern "C" {
+
+size_t moe_b200_ep_area_bytes(int64_t num_tokens) {
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return 0;
+  return EpArea::kStage + (static_cast<size_t>(num_tokens) * kHidden * 2 + 255) / 256 * 256;
+}
+
+int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
+                        int64_t num_tokens, void* output, void* stream) {
+  if (rank_workspaces == nullptr || rank_areas == nullptr || output == nullptr || world < 1 ||
+      world > kEpMaxRanks || rank < 0 || rank >= world || num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MOE_B200_OK;
+  moe_b200_workspace_layout l;
+  if (moe_b200_get_workspace_layout(num_tokens, &l) != MOE_B200_OK) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(output) % 16 != 0) return MOE_B200_ERR_MISALIGNED;
+  EpParams p;
+  for (int q = 0; q < kEpMaxRanks; ++q) {
+    p.area[q] = nullptr;
+    p.y[q] = nullptr;
+    p.slot[q] = nullptr;
+  }
+  for (int q = 0; q < world; ++q) {
+    uint8_t* ws = static_cast<uint8_t*>(rank_workspaces[q]);
+    uint8_t* area = static_cast<uint8_t*>(rank_areas[q]);
+    if (ws == nullptr || area == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0 || reinterpret_cast<uintptr_t>(area) % 256 != 0)
+      return MOE_B200_ERR_MISALIGNED;
+    p.area[q] = area;
+    p.y[q] = reinterpret_cast<const float*>(ws + l.y_acc);
+    // decode-size calls keep one combine row per token
+    p.slot[q] = l.g1_acc != 0 ? nullptr : reinterpret_cast<const int32_t*>(ws + l.tok_slot);
+  }
+  p.out = static_cast<uint16_t*>(output);
+  p.status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_workspaces[rank]) + l.status);
+  p.rank = rank;
+  p.world = world;
+  p.num_tokens = static_cast<int>(num_tokens);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (launch_kernel(ep_combine_kernel, kEpGrid, kEpThreads, 0, s, true, p) != cudaSuccess)
+    return MOE_B200_ERR_CUDA;
+  return MOE_B200_OK;
+}
+
+}  // extern "C"

@@ -342,7 +342,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   mark_stage(5, s);
 
   const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
-  if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
+  if (output != nullptr &&
+      launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
                     static_cast<const int32_t*>(nullptr), static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
@@ -442,8 +443,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
   if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale ||
-      !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale ||
-      !output || !workspace)
+      !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !workspace)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
       !aligned(gemm1_weights, 16) || !aligned(gemm2_weights, 16) || !aligned(output, 16) ||
@@ -600,7 +600,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   mark_stage(5, s);
 
   const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
-  if (launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
+  if (output != nullptr &&
+      launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
                     static_cast<const int32_t*>(tok_slot), static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);

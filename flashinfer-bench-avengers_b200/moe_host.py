@@ -94,6 +94,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_set_stage_events.restype = ctypes.c_int
         lib.moe_b200_abi_version.argtypes = []
         lib.moe_b200_abi_version.restype = ctypes.c_int
+        lib.moe_b200_ep_area_bytes.argtypes = [_I64]
+        lib.moe_b200_ep_area_bytes.restype = ctypes.c_size_t
+        lib.moe_b200_ep_combine.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                            ctypes.c_int, ctypes.c_int, _I64, _P, _P]
+        lib.moe_b200_ep_combine.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -194,13 +199,19 @@ def _bias_arg(routing_bias: torch.Tensor) -> tuple[torch.Tensor, int]:
 def run_dps(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
             gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
             routed_scaling_factor, output, workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Destination-passing form: writes the bf16 [T, 7168] result into ``output``."""
+    """Destination-passing form: writes the bf16 [T, 7168] result into ``output``.
+
+    ``output=None`` (with an explicit ``workspace``) leaves the fp32 combine
+    rows in the workspace for ep_combine and writes no output."""
     T = _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale,
                       gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
-    _check(isinstance(output, torch.Tensor) and output.device == routing_logits.device,
-           "output must be a CUDA tensor on the inputs' device")
-    _check(tuple(output.shape) == (T, H) and output.dtype == torch.bfloat16 and output.is_contiguous(),
-           f"output must be a contiguous bf16 [T, {H}] tensor")
+    if output is None:
+        _check(workspace is not None, "output=None needs an explicit workspace")
+    else:
+        _check(isinstance(output, torch.Tensor) and output.device == routing_logits.device,
+               "output must be a CUDA tensor on the inputs' device")
+        _check(tuple(output.shape) == (T, H) and output.dtype == torch.bfloat16 and output.is_contiguous(),
+               f"output must be a contiguous bf16 [T, {H}] tensor")
     if T == 0:
         return output
     lib = load_library()
@@ -217,8 +228,30 @@ def run_dps(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
             logits.data_ptr(), bias.data_ptr(), bias_dtype, hidden_states.data_ptr(),
             hs_scale.data_ptr(), gemm1_weights.data_ptr(), s13.data_ptr(), gemm2_weights.data_ptr(),
             s2.data_ptr(), int(local_expert_offset), float(routed_scaling_factor), T,
-            output.data_ptr(), ws.data_ptr(), ws.numel(), stream)
+            output.data_ptr() if output is not None else None, ws.data_ptr(), ws.numel(), stream)
     _raise_on(code, "moe_b200_run")
+    return output
+
+
+def ep_area_bytes(num_tokens: int) -> int:
+    """EP area of one rank (counters + bf16 staging) for moe_b200_ep_combine."""
+    return int(load_library().moe_b200_ep_area_bytes(int(num_tokens)))
+
+
+def ep_combine(rank_workspace_ptrs: list[int], rank_area_ptrs: list[int], rank: int, num_tokens: int,
+               output: torch.Tensor) -> torch.Tensor:
+    """bf16 sum over the ranks of their layer outputs into ``output`` (see
+    moe_b200_ep_combine); ``rank_workspace_ptrs[q]`` / ``rank_area_ptrs[q]``
+    are rank q's workspace and EP area addresses in this process."""
+    _check(output.is_cuda and output.dtype == torch.bfloat16 and output.is_contiguous()
+           and tuple(output.shape) == (int(num_tokens), H), f"output must be a contiguous bf16 [T, {H}] tensor")
+    world = len(rank_workspace_ptrs)
+    _check(len(rank_area_ptrs) == world, "one EP area per rank")
+    ws = (ctypes.c_void_p * world)(*[ctypes.c_void_p(int(p)) for p in rank_workspace_ptrs])
+    areas = (ctypes.c_void_p * world)(*[ctypes.c_void_p(int(p)) for p in rank_area_ptrs])
+    stream = torch.cuda.current_stream(output.device).cuda_stream
+    _raise_on(load_library().moe_b200_ep_combine(ws, areas, int(rank), world, int(num_tokens),
+                                                   output.data_ptr(), stream), "moe_b200_ep_combine")
     return output
 
 

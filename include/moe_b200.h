@@ -66,7 +66,9 @@ MOE_B200_API size_t moe_b200_workspace_bytes(int64_t num_tokens);
  *   gemm2_weights_scale   [32, 56, 16]        fp32
  *   local_expert_offset   first global expert id owned by this call
  *   routed_scaling_factor multiplies the renormalised routing weights
- *   output                [T, 7168]           bf16, written in full
+ *   output                [T, 7168]           bf16, written in full; may be NULL, then
+ *                         the fp32 combine rows stay in the workspace (y_acc) for
+ *                         moe_b200_ep_combine and no output is written
  *
  * Alignment: hidden_states, gemm1_weights, gemm2_weights, routing_logits,
  * routing_bias and output 16 bytes; workspace 256 bytes.
@@ -181,6 +183,36 @@ MOE_B200_API int moe_b200_run_noalloc(const float* routing_logits, const void* r
                                       const float* gemm2_weights_scale, int64_t local_expert_offset,
                                       double routed_scaling_factor, int64_t num_tokens,
                                       void* output, void* stream);
+
+/*
+ * Expert-parallel combine over NVLink peer memory. No reference counterpart
+ * (the reference is single-GPU).
+ *
+ * With expert parallelism every rank calls moe_b200_run on the same tokens
+ * for its own expert shard (local_expert_offset) with output = NULL, on a
+ * workspace that every rank can address (e.g. symmetric memory: the same
+ * allocation mapped in every process). Each rank also owns an EP area of
+ * moe_b200_ep_area_bytes(max tokens) bytes, equally addressable by all.
+ * moe_b200_ep_combine then writes the bf16 sum over all ranks of the layer
+ * output into `output` (this rank's, bf16 [T, 7168]): each rank reduces 1/W
+ * of the token rows in fp32 from every rank's combine rows (peer loads),
+ * rounds once to bf16 and stores the rows into every rank's area (peer
+ * stores); the ranks synchronise through counters at the start of the areas.
+ *
+ *   rank_workspaces  host array of `world` pointers: rank q's workspace as
+ *                    mapped in this process
+ *   rank_areas       host array of `world` pointers: rank q's EP area
+ *   rank, world      this rank and the number of ranks (<= 8)
+ *
+ * Every rank must call it once per layer call, on the stream of its
+ * moe_b200_run, with the same num_tokens. Each EP area must be zero before
+ * the first call (its counters only grow, so later calls need no clearing).
+ * Each wait on a peer gives up after one second and sets a bit of the
+ * status word (moe_b200_read_status). Asynchronous, no host synchronisation.
+ */
+MOE_B200_API size_t moe_b200_ep_area_bytes(int64_t num_tokens);
+MOE_B200_API int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
+                                     int64_t num_tokens, void* output, void* stream);
 
 /* ABI version of this header (bumped on any signature change). */
 MOE_B200_API int moe_b200_abi_version(void);

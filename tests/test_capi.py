@@ -32,7 +32,7 @@ def test_header_declares_the_entry_points():
     names = declared_functions()
     for n in ("moe_b200_run", "moe_b200_route", "moe_b200_workspace_bytes", "moe_b200_read_status",
               "moe_b200_status_string", "moe_b200_get_workspace_layout", "moe_b200_set_stage_events",
-              "moe_b200_abi_version"):
+              "moe_b200_abi_version", "moe_b200_ep_area_bytes", "moe_b200_ep_combine"):
         assert n in names
 
 
