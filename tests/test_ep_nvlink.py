@@ -1,12 +1,12 @@
-"""Expert-parallel NVLink combine (moe_b200_ep_combine) on 2 GPUs.
+"""Expert-parallel NVLink combine (moe_b200_ep_combine) on 2-4 GPUs.
 
-Two processes, one per GPU, each own a different 32-expert shard
+One process per GPU (up to four), each owning a different 32-expert shard
 (local_expert_offset = 32 * rank) of the same tokens. The fused combine must
-equal, bit for bit, the bf16 rounding of the fp32 sum over the ranks of
-their own combine rows (read back from the workspaces, summed with an NCCL
-all-reduce), agree with an independent run of every shard within the
-operator's tolerance, be identical on both ranks and leave the status word
-clear. Runs only where two GPUs are visible.
+equal, bit for bit, the bf16 rounding of the fp32 sum in rank order of the
+ranks' own combine rows (read back from the workspaces and gathered), agree
+with an independent run of every shard within the operator's tolerance, be
+identical on all ranks and leave the status word clear. Runs only where at
+least two GPUs are visible.
 """
 import os
 import socket
@@ -63,8 +63,12 @@ def _worker(rank: int, world: int, port: int, cases, results):
             else:
                 slot = ws[lay.tok_slot: lay.tok_slot + 4 * T].view(torch.int32).long()
                 full = torch.where((slot >= 0)[:, None], y[slot.clamp(min=0)], torch.zeros_like(y))
-            dist.all_reduce(full)
-            exact = torch.equal(fused, full.to(torch.bfloat16))
+            rows = [torch.empty_like(full) for _ in range(world)]
+            dist.all_gather(rows, full)
+            total = torch.zeros_like(full)
+            for q in range(world):   # rank order, as the kernel adds them
+                total = total + rows[q]
+            exact = torch.equal(fused, total.to(torch.bfloat16))
             # the standard tolerance against an independent run of each shard
             part = moe_host.run(*workloads.as_args(inp)).float()
             ref = part.clone()
@@ -82,16 +86,17 @@ def _worker(rank: int, world: int, port: int, cases, results):
         dist.destroy_process_group()
 
 
-def test_nvlink_combine_two_ranks():
+def test_nvlink_combine_ranks():
     if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
         pytest.skip("needs two GPUs")
+    world = min(torch.cuda.device_count(), 4)
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
     cases = [(16, "uniform"), (200, "uniform")]   # decode plan; compact combine rows
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, cases, results)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cases, results)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -100,7 +105,7 @@ def test_nvlink_combine_two_ranks():
         if p.is_alive():
             p.kill()
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
-    got = [results.get(timeout=5) for _ in range(2 * len(cases))]
+    got = [results.get(timeout=5) for _ in range(world * len(cases))]
     for rank, T, variant, status, exact, within, same, amax in got:
         assert status == 0, (rank, T, status)
         assert exact, (rank, T, variant)
