@@ -18,10 +18,14 @@
 // parts of C accumulate into one accumulator; epilogue red.adds w * O into
 // the fp32 combine rows with 16-byte vector reductions.
 //
-// Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-3
-// spare, warps 4-11 epilogue (TMEM lane quarter w % 4, column half
-// (w - 4) / 4). The role warpgroup drops to 56 registers and the epilogue
-// warpgroups rise to 224.
+// Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warp 2 scale
+// combiner, warp 3 spare, warps 4-11 epilogue (TMEM lane quarter w % 4,
+// column half (w - 4) / 4). The scale combiner multiplies each K block's
+// token scales by its weight-block scales into a per-accumulator-buffer
+// array and arrives on the same barrier as the MMA's commit, so an epilogue
+// warp waits once per K block and reads its two scales with plain loads.
+// The role warpgroup drops to 56 registers and the epilogue warpgroups rise
+// to 224.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cstdint>
@@ -61,7 +65,7 @@ struct TmTraits {
   // Work units are handed out dynamically through a small ring (s_units +
   // full/empty barriers), like the swap-AB kernels.
   static constexpr int kUnitSlots = 4;
-  static constexpr int kUnitConsumers = 1 + kEpiWarps;   // MMA warp + epilogue warps
+  static constexpr int kUnitConsumers = 2 + kEpiWarps;   // MMA warp + scale warp + epilogue warps
   static constexpr int kNumBars = 2 * kStages + 4 + 2 * kScaleSlots + 2 * kUnitSlots;
   static constexpr int kOffMisc = kOffBars + kNumBars * 8;
   static constexpr int kOffUnitPre = kOffMisc + 16;
@@ -75,7 +79,10 @@ struct TmTraits {
   static constexpr int kStagePitch = 80;
   static constexpr int kOffStage = kOffRed + 2 * BM * 4;
   static constexpr int kStageWarpBytes = 32 * kStagePitch;
-  static constexpr int kSmemBytes = kOffStage + (kG1 ? 0 : kEpiWarps * kStageWarpBytes) + 1024;
+  // Combined scales of the two accumulator buffers: [buffer][column half][row].
+  static constexpr int kOffComb = kOffStage + (kG1 ? 0 : kEpiWarps * kStageWarpBytes);
+  static constexpr int kSmemBytes = kOffComb + 2 * 2 * BM * 4 + 1024;
+  static_assert(kOffComb % 16 == 0 && (kSlotFloats * 4) % 16 == 0, "float4 scale access");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
@@ -187,12 +194,12 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       mbar_init(smem_u32(&empty_bar[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&accf_bar[b]), 1);
+      mbar_init(smem_u32(&accf_bar[b]), 2);   // MMA commit + scale warp
       mbar_init(smem_u32(&acce_bar[b]), Tr::kEpiWarps);
     }
     for (int s = 0; s < Tr::kScaleSlots; ++s) {
       mbar_init(smem_u32(&sfull_bar[s]), 2);
-      mbar_init(smem_u32(&sempty_bar[s]), Tr::kEpiWarps);
+      mbar_init(smem_u32(&sempty_bar[s]), 1);
     }
     for (int s = 0; s < Tr::kUnitSlots; ++s) {
       mbar_init(smem_u32(&ufull_bar[s]), 1);
@@ -332,6 +339,44 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         if (++abuf == 2) { abuf = 0; aph ^= 1; }
       }
     }
+  } else if (warp == 2) {
+    // ====================================================== scale combiner
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
+    float* comb = reinterpret_cast<float*>(smem + Tr::kOffComb);
+    int slot = 0, abuf = 0, uslot = 0;
+    uint32_t sph = 0, aph = 0, uph = 0;
+    bool ok = true;
+    while (ok) {
+      if (!mbar_wait(smem_u32(&ufull_bar[uslot]), uph, s_abort, p.status, kStatusTimeoutUnit)) break;
+      const int u = s_units[uslot];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
+      if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
+      if (u < 0) break;
+      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+        // this K block's raw scales have landed, and the epilogue has read
+        // the combined scales this buffer held two K blocks ago
+        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue) ||
+            !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        const float* sp = ring + slot * Tr::kSlotFloats;
+        const float4 ts = reinterpret_cast<const float4*>(sp)[lane];   // token rows 4*lane .. +3
+        const float w0 = sp[Tr::BM], w1 = sp[Tr::BM + 1];
+        float4* c0 = reinterpret_cast<float4*>(comb + (abuf * 2) * Tr::BM);
+        float4* c1 = reinterpret_cast<float4*>(comb + (abuf * 2 + 1) * Tr::BM);
+        c0[lane] = make_float4(ts.x * w0, ts.y * w0, ts.z * w0, ts.w * w0);
+        c1[lane] = make_float4(ts.x * w1, ts.y * w1, ts.z * w1, ts.w * w1);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(smem_u32(&sempty_bar[slot]));
+          mbar_arrive(smem_u32(&accf_bar[abuf]));
+        }
+        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
+        if (++abuf == 2) { abuf = 0; aph ^= 1; }
+      }
+    }
   } else if (warp < 4) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(Tr::kRoleRegs));
   } else {
@@ -341,8 +386,9 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     const int hf = (warp - 4) >> 2;      // column half
     const int r = q * 32 + lane;         // token row inside the tile
     const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
-    int slot = 0, abuf = 0, uslot = 0;
-    uint32_t sph = 0, aph = 0, uph = 0;
+    const float* comb = reinterpret_cast<const float*>(smem + Tr::kOffComb);
+    int abuf = 0, uslot = 0;
+    uint32_t aph = 0, uph = 0;
     bool ok = true;
     // GEMM1: acc0 = up, acc1 = gate for intermediate columns hf*64 .. +64.
     // GEMM2: acc0 / acc1 = W2 rows (2*blk + hf)*128 + [0, 64) / [64, 128).
@@ -368,31 +414,9 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       }
 #pragma unroll
       for (int i = 0; i < 32; ++i) { acc0p[i] = 0ull; acc1p[i] = 0ull; }
-      // Scales of one K block (token scale x weight-block scale): GEMM1 up /
-      // gate, GEMM2 this half's W2 block for both phases. They are read one
-      // K block ahead, while the MMA of the current block still runs.
-      auto read_scales = [&](float& a0, float& a1) -> bool {
-        if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue)) return false;
-        const float* sp = ring + slot * Tr::kSlotFloats;
-        const float ts = sp[r];
-        a0 = ts * (kG1 ? sp[Tr::BM] : sp[Tr::BM + hf]);
-        a1 = kG1 ? ts * sp[Tr::BM + 1] : a0;
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sempty_bar[slot]));
-        if (++slot == Tr::kScaleSlots) { slot = 0; sph ^= 1; }
-        return true;
-      };
-      float ns0 = 0.f, ns1 = 0.f;
-      if (!read_scales(ns0, ns1)) {
-        ok = false;
-        break;
-      }
       for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
-        const float s0 = ns0, s1 = ns1;
-        if (kb + 1 < Tr::kKBlocks && !read_scales(ns0, ns1)) {
-          ok = false;
-          break;
-        }
+        // the accumulator of this K block is complete and its combined
+        // scales (token scale x weight-block scale) are in `comb`
         if (!mbar_wait(smem_u32(&accf_bar[abuf]), aph, s_abort, p.status, kStatusTimeoutEpilogue)) {
           ok = false;
           break;
@@ -401,11 +425,15 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         const uint32_t tb = lane_base + abuf * Tr::kAccCols;
         const uint32_t col_a = kG1 ? hf * 64 : hf * 128;
         const uint32_t col_b = kG1 ? 128 + hf * 64 : hf * 128 + 64;
-        const uint64_t s0p = pack_f32x2(__float_as_uint(s0), __float_as_uint(s0));
-        const uint64_t s1p = pack_f32x2(__float_as_uint(s1), __float_as_uint(s1));
         uint32_t v[64];
         tmem_ld32(tb + col_a, *reinterpret_cast<uint32_t(*)[32]>(&v[0]));
         tmem_ld32(tb + col_a + 32, *reinterpret_cast<uint32_t(*)[32]>(&v[32]));
+        // GEMM1: up / gate block scales; GEMM2: this half's W2 block for both
+        const float* cb = comb + abuf * 2 * Tr::BM;
+        const float s0 = cb[(kG1 ? 0 : hf) * Tr::BM + r];
+        const float s1 = kG1 ? cb[Tr::BM + r] : s0;
+        const uint64_t s0p = pack_f32x2(__float_as_uint(s0), __float_as_uint(s0));
+        const uint64_t s1p = pack_f32x2(__float_as_uint(s1), __float_as_uint(s1));
         tmem_wait_ld();
 #pragma unroll
         for (int i = 0; i < 32; ++i) acc0p[i] = ffma_f32x2(pack_f32x2(v[2 * i], v[2 * i + 1]), s0p, acc0p[i]);
