@@ -103,10 +103,14 @@ def test_permutation_bit_exact(host, T, offset, variant):
         torch.testing.assert_close(perm_w[lo: lo + cnt], rpw[rseg[e]: rseg[e + 1]], rtol=4e-6, atol=0)
         assert bool((perm_tok[lo + cnt: int(seg[e + 1])] == -1).all())
     # the gathered rows are the tokens' rows
+    valid = perm_tok >= 0
     a_perm = ws[lay.a_perm: lay.a_perm + n * 7168].view(n, 7168).cpu()
     hs = inp["hidden_states"].view(torch.uint8).cpu()
-    valid = perm_tok >= 0
     assert torch.equal(a_perm[valid], hs[perm_tok[valid]])
+    # the permuted block scales are the tokens' scales, [56, cap] K-block major
+    sa = ws[lay.sa_perm: lay.sa_perm + 56 * lay.cap_rows * 4].view(torch.float32).view(56, lay.cap_rows).cpu()
+    hss = inp["hidden_states_scale"].cpu()
+    assert torch.equal(sa[:, :n][:, valid], hss[:, perm_tok[valid]])
     if T > 64:
         # combine rows: tokens with a local pick numbered in token order
         local = (ridx >= offset) & (ridx < offset + 32)
