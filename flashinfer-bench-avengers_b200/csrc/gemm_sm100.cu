@@ -319,17 +319,20 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     tmem_relinquish();
   }
   // Everything up to pdl_wait() overlaps the previous kernel's tail
-  // (programmatic dependent launch). With early_tables the permutation has
-  // completed before this grid is launched (the kernels in between release
-  // their dependents only after their own wait), so the segment table can be
-  // read here and the producer issues the first stages' weight tiles, which
-  // no earlier kernel writes, before waiting. Without it (the decode GEMM1
-  // follows the permutation directly) everything waits first.
+  // (programmatic dependent launch). With early_tables the segment table is
+  // final before this grid is launched -- the non-decode permutation has
+  // completed (the kernels in between release their dependents only after
+  // their own wait), and the decode front end releases its dependents only
+  // after writing and fencing the table -- so it can be read here and the
+  // producer issues the first stages' weight tiles, which no earlier kernel
+  // writes, before waiting. Without it everything waits first.
   if (!early_tables) pdl_wait();
   if (warp == 2) {
     // per-expert tile counts -> prefix over experts of the work units
-    const int lo = p.seg_off[lane];
-    const int cnt = p.counts[lane];
+    // L2 reads: with early_tables the table may have been written by a grid
+    // that is still running
+    const int lo = __ldcg(p.seg_off + lane);
+    const int cnt = __ldcg(p.counts + lane);
     const int units = ((cnt + BN - 1) / BN) * Tr::kRowBlocks * splits;
     int incl = units;
 #pragma unroll

@@ -323,10 +323,11 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   g1.y_acc = y_acc;
   g1.status = status;
   g1.sched = sched;
-  // GEMM1 follows the permutation directly, so it must wait before reading
-  // the segment table (no early tables).
+  // The front end releases GEMM1 right after writing and fencing the segment
+  // table, so GEMM1 reads it and starts streaming weight tiles while the
+  // front end still copies the permuted rows (early tables).
   const int grid1 = grid_for(T, kBN, kInterBlocks, kG1Splits, di.sm_count);
-  if (launch_moe_gemm(kGemm1Split, kBN, tm_w13, tm_aperm, tm_aperm, g1, grid1, false, s) != cudaSuccess)
+  if (launch_moe_gemm(kGemm1Split, kBN, tm_w13, tm_aperm, tm_aperm, g1, grid1, true, s) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(4, s);
 

@@ -389,7 +389,6 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
   __shared__ int s_start[kExpertsLocal];
   __shared__ int s_cnt[kExpertsLocal];
   __shared__ int s_cpre[kExpertsLocal];
-  pdl_launch_next();
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -479,12 +478,19 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
         dp.counts[lane] = c;
         dp.seg_off[lane + 1] = incl;
         if (lane == 0) dp.seg_off[0] = 0;
+        __threadfence();
       }
     } else if (rank == 1 && warp == 2) {
       if (lane < 4) dp.sched[lane] = 0;
       if (lane == 4) *dp.status = 0;
+      __threadfence();
     }
     __syncthreads();
+    // GEMM1 may start now: the segment table, the cleared unit counter and
+    // status word are visible device-wide (fenced above), and GEMM1 reads
+    // them and issues its first weight tiles before it waits for this grid
+    // to complete (the permuted rows, scales and g1_acc clears below).
+    pdl_launch_next();
     if (warp < 2) {
       if (t < T) {
         uint32_t m = mask;
