@@ -93,25 +93,56 @@ def load_peaks() -> dict:
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons while running."""
+    """SM clock and throttle reasons of this rank's GPU during the timed region.
+
+    With NVML (nvidia-ml-py) a background thread polls every 0.25 ms and keeps
+    only the samples taken while the sampler is armed, which `time_layer` does
+    around its timed loops (a few milliseconds). Without NVML, nvidia-smi
+    samples every 200 ms for the whole block instead."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    POLL_S = 0.00025
+    # NVML clock-event reason bits
+    REASON_BITS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+                   "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, device: torch.device):
         self.dev = device
         self.proc = None
         self.lines: list[str] = []
         self.thread = None
+        self.nvml = None
+        self.handle = None
+        self.armed = False
+        self.stop = False
+        self.samples: list[tuple[float, int]] = []
+        self.max_mhz = None
 
-    def __enter__(self):
+    def _uuid(self) -> str | None:
         try:
             uuid = str(torch.cuda.get_device_properties(self.dev).uuid)
-            sel = uuid if uuid.startswith("GPU-") else "GPU-" + uuid
+            return uuid if uuid.startswith("GPU-") else "GPU-" + uuid
         except Exception:
-            sel = str(self.dev.index or 0)
+            return None
+
+    def __enter__(self):
+        uuid = self._uuid()
         try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.handle = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid is not None
+                           else pynvml.nvmlDeviceGetHandleByIndex(self.dev.index or 0))
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(self.handle, pynvml.NVML_CLOCK_SM))
+            self.nvml = pynvml
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
+        try:
+            sel = uuid if uuid is not None else str(self.dev.index or 0)
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", sel, f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                  "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
@@ -121,21 +152,63 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def arm(self):
+        self.armed = True
+
+    def sample_now(self):
+        """One sample from the calling thread (the timing loop calls this
+        after each step's end event, outside the [start, end] event pair)."""
+        if self.nvml is None:
+            return
+        try:
+            nv = self.nvml
+            self.samples.append((float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM)),
+                                 int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle))))
+        except Exception:
+            pass
+
+    def disarm(self):
+        self.armed = False
+
+    def _poll(self):
+        nv = self.nvml
+        while not self.stop:
+            if self.armed:
+                try:
+                    mhz = float(nv.nvmlDeviceGetClockInfo(self.handle, nv.NVML_CLOCK_SM))
+                    reasons = int(nv.nvmlDeviceGetCurrentClocksEventReasons(self.handle))
+                    self.samples.append((mhz, reasons))
+                except Exception:
+                    pass
+            time.sleep(self.POLL_S)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self.stop = True
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=5)
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if self.nvml is not None:
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self) -> dict:
+        if self.nvml is not None:
+            if not self.samples:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0, "source": "nvml"}
+            reasons = sorted(n for n, bit in self.REASON_BITS.items() if any(r & bit for _, r in self.samples))
+            return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.samples), "source": "nvml, timed region only"}
         sm, smax, reasons = [], [], set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         for line in self.lines:
@@ -151,9 +224,9 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0, "source": "nvidia-smi"}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax), "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvidia-smi, 200 ms"}
 
 
 # ------------------------------------------------------------------ helpers
@@ -213,7 +286,7 @@ def layer_call(inp: dict, combiner=None):
 
 
 def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=None,
-               do_flush: bool = True, combiner=None) -> dict:
+               do_flush: bool = True, combiner=None, clocks=None) -> dict:
     """Device time of `steps` layer calls replayed from a CUDA graph, each
     after a 256 MB write flush when `do_flush` (otherwise back to back; the
     flushed timing is then taken as well, as `call_ms_flushed`). A second
@@ -253,21 +326,27 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
     if group is not None:
         dist.barrier(group=group)
     torch.cuda.synchronize()
-    def timed(flushed: bool) -> list:
+    def timed(flushed: bool, sampler=None) -> list:
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        if sampler is not None:
+            sampler.arm()   # clock samples only while the timed calls run
         for i in range(steps):
             if flushed:
                 flush.zero_()
             starts[i].record()
             plain.replay()
             ends[i].record()
+            if sampler is not None:
+                sampler.sample_now()   # the GPU is still running the queued calls
         torch.cuda.synchronize()
+        if sampler is not None:
+            sampler.disarm()
         if group is not None:
             dist.barrier(group=group)
         return [a.elapsed_time(b) for a, b in zip(starts, ends)]
 
-    call_ms = timed(do_flush)
+    call_ms = timed(do_flush, clocks)
     call_ms_flushed = call_ms if do_flush else timed(True)
     stage_ms = {n: [] for n in moe_host.STAGE_NAMES}
     for _ in range(max(3, steps // 4)):
@@ -462,7 +541,8 @@ def main() -> None:
         import expert_parallel
         combiner = expert_parallel.NvlinkCombiner(HEADLINE_T, device, group)
     with ClockSampler(device) as clocks:
-        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back, combiner=combiner)
+        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back, combiner=combiner,
+                       clocks=clocks)
     call_ms = torch.tensor(r["call_ms"], dtype=torch.float64, device=device)
     mean_ms = call_ms.mean()
     if group is not None:
