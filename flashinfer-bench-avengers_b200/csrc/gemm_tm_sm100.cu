@@ -135,22 +135,31 @@ __device__ __forceinline__ float e4m3_round(float x) {
 // weight block through L2. Units are handed out in increasing order by an
 // atomic counter, so faster CTAs take more of them.
 struct TmTile {
-  int e, blk, row0, nvalid;
+  int e, blk, row0, nvalid, kb0, kb1;
 };
 
+// With `splits` > 1 (GEMM2 of batches with fewer units than CTAs) each
+// (expert, block, token tile) is split into K ranges of kblocks / splits
+// blocks, adjacent in the unit order; their partial sums meet in the
+// combine rows' fp32 reductions.
 __device__ __forceinline__ void tm_decode(int u, const int* s_unit_pre, const int* s_seg, const int* s_cnt,
-                                          TmTile& t) {
+                                          int splits, int kblocks, TmTile& t) {
   int e = 0;
 #pragma unroll 1
   while (s_unit_pre[e + 1] <= u) ++e;
   const int cnt = s_cnt[e];
   const int nt = (cnt + 127) / 128;
   const int local = u - s_unit_pre[e];
-  const int tt = local % nt;
+  const int ks = local % splits;
+  const int rest = local / splits;
+  const int tt = rest % nt;
   t.e = e;
-  t.blk = local / nt;
+  t.blk = rest / nt;
   t.row0 = s_seg[e] + tt * 128;
   t.nvalid = min(128, cnt - tt * 128);
+  const int per = kblocks / splits;
+  t.kb0 = ks * per;
+  t.kb1 = t.kb0 + per;
 }
 
 }  // namespace
@@ -220,8 +229,15 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
   if (warp == 2) {
     const int lo = p.seg_off[lane];
     const int cnt = p.counts[lane];
-    const int units = ((cnt + 127) / 128) * Tr::kRowBlocks;
-    int incl = units;
+    const int base = ((cnt + 127) / 128) * Tr::kRowBlocks;
+    // GEMM2 with fewer (expert, block, token tile) units than CTAs: split K
+    // 2 or 4 ways (the same choice in every CTA)
+    int total = base;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
+    int splits = 1;
+    if (!kG1 && total > 0 && total < static_cast<int>(gridDim.x)) splits = 2 * total < static_cast<int>(gridDim.x) ? 4 : 2;
+    int incl = base * splits;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, off);
@@ -230,7 +246,10 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     s_unit_pre[lane + 1] = incl;
     s_seg[lane] = lo;
     s_cnt[lane] = cnt;
-    if (lane == 0) s_unit_pre[0] = 0;
+    if (lane == 0) {
+      s_unit_pre[0] = 0;
+      s_unit_pre[kExpertsLocal + 1] = splits;
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -259,7 +278,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       TmTile t;
-      tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
+      tm_decode(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
       int brow0, brow1, wrow0, wrow1;
       if constexpr (kG1) {
         brow0 = t.e * kGemm1Out + t.blk * kBlk;
@@ -272,7 +291,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
         wrow0 = (t.e * kHiddenBlocks + 2 * t.blk) * kInterBlocks;
         wrow1 = wrow0 + kInterBlocks;
       }
-      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&empty_bar[stage]), ph ^ 1, s_abort, p.status, kStatusTimeoutProducer) ||
             !mbar_wait(smem_u32(&sempty_bar[slot]), sph ^ 1, s_abort, p.status, kStatusTimeoutProducer)) {
           ok = false;
@@ -314,7 +333,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
-      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+      for (int kb = 0, nkb = Tr::kKBlocks / s_unit_pre[kExpertsLocal + 1]; kb < nkb; ++kb) {
         if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
             !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
           ok = false;
@@ -353,7 +372,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&uempty_bar[uslot]));
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
-      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+      for (int kb = 0, nkb = Tr::kKBlocks / s_unit_pre[kExpertsLocal + 1]; kb < nkb; ++kb) {
         // this K block's raw scales have landed, and the epilogue has read
         // the combined scales this buffer held two K blocks ago
         if (!mbar_wait(smem_u32(&sfull_bar[slot]), sph, s_abort, p.status, kStatusTimeoutEpilogue) ||
@@ -402,7 +421,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       TmTile t;
-      tm_decode(u, s_unit_pre, s_seg, s_cnt, t);
+      tm_decode(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
       const bool valid = r < t.nvalid;
       int my_tok = 0;
       float my_w = 0.f;
@@ -414,7 +433,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       }
 #pragma unroll
       for (int i = 0; i < 32; ++i) { acc0p[i] = 0ull; acc1p[i] = 0ull; }
-      for (int kb = 0; kb < Tr::kKBlocks; ++kb) {
+      for (int kb = t.kb0; kb < t.kb1; ++kb) {
         // the accumulator of this K block is complete and its combined
         // scales (token scale x weight-block scale) are in `comb`
         if (!mbar_wait(smem_u32(&accf_bar[abuf]), aph, s_abort, p.status, kStatusTimeoutEpilogue)) {

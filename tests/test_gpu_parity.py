@@ -147,6 +147,26 @@ def test_layer_matches_oracle(host, T, seed, variant, offset):
     assert host.read_status(host.get_workspace(T, out.device)) == 0
 
 
+@pytest.mark.parametrize("T,seed,offset", [(600, 3, 128), (1024, 3, 224)])
+def test_token_major_k_split(host, T, seed, offset):
+    """Token-major GEMM2 splits K over 2 or 4 work units when the batch has
+    fewer (expert, block, token tile) units than CTAs. Inputs are generated
+    on the CPU (then copied) so that the routing is known: 3 local experts
+    with 3 token tiles (84 units -> 2 splits) and 2 experts with 2 tiles
+    (56 units -> 4 splits)."""
+    inp = {k: (v.cuda() if torch.is_tensor(v) else v)
+           for k, v in workloads.make_inputs(T, seed, "cpu", "zipf", offset, 2.5).items()}
+    idx, _ = moe_oracle.route(inp["routing_logits"].cpu(), inp["routing_bias"].cpu(), 2.5)
+    local = (idx >= offset) & (idx < offset + 32)
+    cnt = torch.bincount((idx[local] - offset).long(), minlength=32)
+    assert 0 < int(((cnt + 127) // 128).sum()) * 28 < 148   # fewer units than CTAs
+    out = host.run(*workloads.as_args(inp))
+    torch.cuda.synchronize()
+    ref = moe_oracle.moe_forward(*workloads.as_args(inp))
+    _check_output(out, ref, f"T={T} zipf offset={offset}")
+    assert host.read_status(host.get_workspace(T, out.device)) == 0
+
+
 def test_no_local_experts_gives_zeros(host):
     inp = _gpu_inputs(32, 9, "uniform", 256)  # offset past the last global expert
     out = host.run(*workloads.as_args(inp))
