@@ -34,6 +34,7 @@
 #include "moe_kernels.cuh"
 #include "moe_ptx.cuh"
 #include "moe_shapes.cuh"
+#include "swiglu.cuh"
 
 namespace moe {
 
@@ -236,7 +237,15 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) total += __shfl_xor_sync(0xffffffffu, total, off);
     int splits = 1;
-    if (!kG1 && total > 0 && total < static_cast<int>(gridDim.x)) splits = 2 * total < static_cast<int>(gridDim.x) ? 4 : 2;
+    if constexpr (kG1) {
+      // K-split GEMM1 of few token tiles (partial sums into g1_acc)
+      if (p.g1_acc != nullptr) splits = tm_gemm1_splits(total);
+    } else {
+      if (total > 0 && total < static_cast<int>(gridDim.x)) splits = 2 * total < static_cast<int>(gridDim.x) ? 4 : 2;
+    }
+    // GEMM2 after a K-split GEMM1: SwiGLU of the g1_acc sums runs here first
+    const int g1_units = total / Tr::kRowBlocks * kInterBlocks;
+    const int swiglu_phase = !kG1 && p.g1_acc != nullptr && p.grid_sync != nullptr && tm_gemm1_splits(g1_units) > 1;
     int incl = base * splits;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -249,6 +258,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     if (lane == 0) {
       s_unit_pre[0] = 0;
       s_unit_pre[kExpertsLocal + 1] = splits;
+      s_seg[kExpertsLocal + 1] = swiglu_phase;   // spare slot of the segment table
     }
   }
   tc_fence_before();
@@ -263,6 +273,24 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     int stage = 0, slot = 0, uslot = 0;
     uint32_t ph = 0, sph = 0, uph = 0;
     bool ok = true;
+    if (!kG1 && s_seg[kExpertsLocal + 1]) {
+      // C (tiles and scales) comes from this grid's SwiGLU phase: wait until
+      // every CTA has counted itself on grid_sync
+      if (lane == 0) {
+        const uint64_t t0 = globaltimer_ns();
+        uint32_t spins = 0;
+        while (ld_acquire_gpu(p.grid_sync) < static_cast<int>(gridDim.x)) {
+          if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+            atomicOr(p.status, kStatusTimeoutGridSync);
+            *s_abort = 1;
+            break;
+          }
+        }
+        fence_proxy_async_global();   // C is read through TMA
+      }
+      __syncwarp();
+      if (*s_abort) ok = false;
+    }
     while (ok) {
       int u = -1;
       if (lane == 0) u = atomicAdd(p.sched, 1);
@@ -409,6 +437,33 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
     int abuf = 0, uslot = 0;
     uint32_t aph = 0, uph = 0;
     bool ok = true;
+    if (!kG1 && s_seg[kExpertsLocal + 1]) {
+      // After a K-split GEMM1: C = SwiGLU of the g1_acc sums for every valid
+      // (token, expert) row and 128-block, one warp task each over the whole
+      // grid; then this CTA counts itself on grid_sync (the producers wait
+      // for all CTAs before their first C tile). Valid pair v is row
+      // seg[e] + v - cpre[e] of expert e (cpre = exclusive prefix of counts).
+      const int cnt = s_cnt[lane];
+      int incl = cnt;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int o = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += o;
+      }
+      const int pairs = __shfl_sync(0xffffffffu, incl, 31);
+      const int nwarps = static_cast<int>(gridDim.x) * Tr::kEpiWarps;
+      for (int task = static_cast<int>(blockIdx.x) * Tr::kEpiWarps + (warp - 4); task < pairs * kInterBlocks;
+           task += nwarps) {
+        const int v = task / kInterBlocks;
+        const int e = __popc(__ballot_sync(0xffffffffu, incl <= v));
+        const int row = s_seg[e] + v - (__shfl_sync(0xffffffffu, incl, e) - __shfl_sync(0xffffffffu, cnt, e));
+        swiglu_quant_row_block(p, row, task % kInterBlocks, lane);
+      }
+      fence_proxy_async_global();
+      __threadfence();
+      named_bar_sync(1, 32 * Tr::kEpiWarps);
+      if (warp == 4 && lane == 0) red_release_gpu_add(p.grid_sync, 1);
+    }
     // GEMM1: acc0 = up, acc1 = gate for intermediate columns hf*64 .. +64.
     // GEMM2: acc0 / acc1 = W2 rows (2*blk + hf)*128 + [0, 64) / [64, 128).
     // Kept as packed pairs (column 2i in the low half) for f32x2 FMAs.
@@ -476,7 +531,19 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
 
       // ------------------------------------------------- final epilogue
       const int64_t row = t.row0 + r;
-      if constexpr (kG1) {
+      if (kG1 && s_unit_pre[kExpertsLocal + 1] > 1) {
+        // K-split GEMM1: this K range's fp32 sums of up and gate into g1_acc
+        // (GEMM2 applies SwiGLU once all ranges are in)
+        if (valid) {
+          float* gu = p.g1_acc + row * kGemm1Out + t.blk * kBlk + hf * 64;
+          float* gg = gu + kInter;
+#pragma unroll
+          for (int c = 0; c < 64; c += 4) {
+            red_add_v4(gu + c, acc0[c], acc0[c + 1], acc0[c + 2], acc0[c + 3]);
+            red_add_v4(gg + c, acc1[c], acc1[c + 1], acc1[c + 2], acc1[c + 3]);
+          }
+        }
+      } else if constexpr (kG1) {
         float m = 0.f;
 #pragma unroll
         for (int c = 0; c < 64; ++c) {

@@ -111,6 +111,10 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   if (plan.decode) {
     l.g1_acc = off;
     off = align_up(off + cap * kGemm1Out * sizeof(float));
+  } else if (plan.token_major) {
+    // K-split GEMM1 sums of batches with few token tiles (kTmSplitRows rows)
+    l.g1_acc = off;
+    off = align_up(off + static_cast<size_t>(kTmSplitRows) * kGemm1Out * sizeof(float));
   }
   l.total_bytes = off;
   l.cap_rows = static_cast<int64_t>(cap);
@@ -547,6 +551,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   gp.a_perm = a_perm;
   gp.sa_perm = sa_perm;
   gp.y_acc = y_acc;
+  gp.counts = counts;
+  gp.g1_acc = plan.token_major ? reinterpret_cast<float*>(ws + l.g1_acc) : nullptr;
   int ggrid = static_cast<int>(div_up(cap, 8));
   if (ggrid < di.sm_count) ggrid = di.sm_count;
   if (ggrid > di.sm_count * 4) ggrid = di.sm_count * 4;
@@ -568,7 +574,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g1.c_hi = c_hi;
   g1.c_lo = c_lo;
   g1.c_scale = c_scale;
-  g1.g1_acc = nullptr;
+  g1.g1_acc = plan.token_major ? reinterpret_cast<float*>(ws + l.g1_acc) : nullptr;
   g1.status = status;
   g1.sched = sched;
   const int grid1 = grid_for(num_tokens, plan.g1_bn, kInterBlocks, 1, di.sm_count);
@@ -588,6 +594,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   g2.w_scale = gemm2_weights_scale;
   g2.splits = 1;
   g2.y_acc = y_acc;
+  // token-major GEMM2 counts its CTAs here after the SwiGLU phase of a
+  // K-split GEMM1 (cleared by the permutation)
+  g2.grid_sync = plan.token_major ? sched + 2 : nullptr;
   const int g2_kind = plan.g2_wide ? kGemm2Wide : kGemm2;
   const int grid2 = grid_for(num_tokens, plan.g2_bn, plan.g2_wide ? kHiddenBlocks / 2 : kHiddenBlocks,
                              1, di.sm_count);

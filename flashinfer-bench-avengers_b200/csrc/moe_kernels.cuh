@@ -50,7 +50,23 @@ struct GatherParams {
   uint8_t* a_perm;          // [cap, 7168] e4m3
   float* sa_perm;           // [56, cap]
   float* y_acc;             // [n_touched, 7168] cleared
+  const int* counts;        // [32] (token-major plans, for the GEMM1 K-split rule)
+  float* g1_acc;            // token-major GEMM1 K-split sums, cleared when the split is on; or null
 };
+
+// Token-major GEMMs of batches with few token tiles: when GEMM1 has fewer
+// than kTmSplitUnits (expert, 128-block, 128-token tile) units, it splits K
+// into tm_gemm1_splits() parts whose fp32 sums meet in g1_acc, and GEMM2
+// applies SwiGLU (grid-wide, before its first C tile) instead of GEMM1's
+// epilogue. Fewer than 148 units means at most 9 token tiles (1,152 pairs)
+// and at most 1,152 + 9 x 15 padded rows, within kTmSplitRows.
+constexpr int kTmSplitUnits = 148;
+constexpr int kTmSplitRows = 1664;
+
+__device__ __forceinline__ int tm_gemm1_splits(int units) {
+  if (units <= 0 || units >= kTmSplitUnits) return 1;
+  return 2 * units < kTmSplitUnits ? 4 : 2;
+}
 
 // Decode batches (num_tokens <= kDecodeMaxTokens) use a dedicated front end:
 // one 8-CTA cluster does routing, permutation, the permuted row copy and the

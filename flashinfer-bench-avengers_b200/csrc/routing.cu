@@ -747,6 +747,17 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
   const int64_t y4 = static_cast<int64_t>(*p.n_touched) * (kHidden / 4);
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < y4; i += nthreads)
     reinterpret_cast<float4*>(p.y_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (p.g1_acc != nullptr) {
+    // token-major GEMM1 K-split sums start from zero when the split is on
+    int units = 0;
+#pragma unroll 4
+    for (int e = 0; e < kExpertsLocal; ++e) units += (p.counts[e] + 127) / 128 * kInterBlocks;
+    if (tm_gemm1_splits(units) > 1) {
+      const int64_t g4 = static_cast<int64_t>(rows) * (kGemm1Out / 4);
+      for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < g4; i += nthreads)
+        reinterpret_cast<float4*>(p.g1_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
   // Padding rows are skipped: they only ever feed token columns or rows that
   // the GEMM epilogues discard, and every output column depends on its own
   // token row alone.

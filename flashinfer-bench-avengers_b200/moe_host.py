@@ -26,6 +26,9 @@ HIDDEN_BLOCKS = H // 128
 INTER_BLOCKS = I // 128
 GEMM1_OUT_BLOCKS = 2 * I // 128
 MAX_TOKENS = 262144
+# Calls with at least this many tokens run the token-major prefill GEMMs
+# (kTokenMajorMinTokens, moe_capi.cu).
+TOKEN_MAJOR_MIN_TOKENS = 512
 
 BIAS_BF16 = 0
 BIAS_FP32 = 1

@@ -65,7 +65,8 @@ def test_workspace_size_and_layout(lib):
                 lay.perm_row, lay.tok_slot, lay.a_perm, lay.sa_perm, lay.c_hi, lay.c_lo, lay.c_scale, lay.y_acc]
         assert lay.status < lay.sched < lay.n_touched < lay.seg_off
         assert lay.a_perm - lay.tok_slot >= 4 * T and lay.tok_slot - lay.perm_row >= 4 * lay.cap_rows
-        if decode:
+        token_major = T >= moe_host.TOKEN_MAJOR_MIN_TOKENS
+        if decode or token_major:
             offs += [lay.g1_acc]
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
         assert offs[-1] < n
@@ -73,6 +74,10 @@ def test_workspace_size_and_layout(lib):
         if decode:
             assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
             assert n - lay.g1_acc >= lay.cap_rows * 4096 * 4
+        elif token_major:
+            # K-split GEMM1 sums of batches with few token tiles: 1,664 rows
+            assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
+            assert n - lay.g1_acc >= 1664 * 4096 * 4
         else:
             assert lay.g1_acc == 0
         if T > 65:  # plans without the decode scratch grow with T
