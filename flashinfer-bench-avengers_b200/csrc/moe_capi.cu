@@ -83,7 +83,7 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   l.seg_off = off;
   off = align_up(off + (kExpertsLocal + 1) * sizeof(int));
   l.chunk_counts = off;
-  off = align_up(off + static_cast<size_t>((T + 1023) / 1024) * (kExpertsLocal + 1) * sizeof(int));
+  off = align_up(off + static_cast<size_t>((T + kPermChunk - 1) / kPermChunk) * (kExpertsLocal + 1) * sizeof(int));
   l.topk_idx = off;
   off = align_up(off + cap * sizeof(int32_t));
   l.topk_w = off;
@@ -535,9 +535,9 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   if (T <= 1024) {
     if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
-    const int chunks = static_cast<int>(div_up(T, 1024));
-    if (launch_kernel(permute_count_kernel, chunks, 1024, 0, s, true, pp) != cudaSuccess ||
-        launch_kernel(permute_place_kernel, chunks, 1024, 0, s, true, pp) != cudaSuccess)
+    const int chunks = static_cast<int>(div_up(T, kPermChunk));
+    if (launch_kernel(permute_count_kernel, chunks, kPermChunk, 0, s, true, pp) != cudaSuccess ||
+        launch_kernel(permute_place_kernel, chunks, kPermChunk, 0, s, true, pp) != cudaSuccess)
       return MOE_B200_ERR_CUDA;
   }
   GatherParams gp;

@@ -61,6 +61,8 @@ struct GatherParams {
 // epilogue. Fewer than 148 units means at most 9 token tiles (1,152 pairs)
 // and at most 1,152 + 9 x 15 padded rows, within kTmSplitRows.
 constexpr int kTmSplitUnits = 148;
+// Tokens (and threads) per CTA of the multi-CTA permutation (T > 1024).
+constexpr int kPermChunk = 256;
 constexpr int kTmSplitRows = 1664;
 
 __device__ __forceinline__ int tm_gemm1_splits(int units) {

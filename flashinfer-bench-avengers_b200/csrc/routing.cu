@@ -560,16 +560,17 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
   }
 }
 
-// Multi-CTA permutation for batches of more than 1024 tokens, one 1024-token
-// chunk per CTA, same result as permute_kernel. permute_count_kernel writes
-// each chunk's per-expert counts; permute_place_kernel derives the segment
-// starts from all chunks' counts and places its chunk's tokens after those
-// of earlier chunks.
+// Multi-CTA permutation for batches of more than 1024 tokens, one chunk of
+// kPermChunk tokens (one per thread) per CTA, same result as permute_kernel.
+// permute_count_kernel writes each chunk's per-expert counts;
+// permute_place_kernel derives the segment starts from all chunks' counts
+// and places its chunk's tokens after those of earlier chunks.
 constexpr int kChunkStride = kExpertsLocal + 1;   // chunk_counts row: 32 expert counts + touched tokens
+constexpr int kPermWarps = kPermChunk / 32;
 
-__global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
-  __shared__ int s_wcnt[32][kExpertsLocal];
-  __shared__ int s_wtouch[32];
+__global__ void __launch_bounds__(kPermChunk) permute_count_kernel(PermuteParams p) {
+  __shared__ int s_wcnt[kPermWarps][kExpertsLocal];
+  __shared__ int s_wtouch[kPermWarps];
   pdl_launch_next();
   pdl_wait();
   const int tid = threadIdx.x;
@@ -577,7 +578,7 @@ __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
   const int lane = tid & 31;
   int sidx[kTopK];
   float sw[kTopK];
-  const uint32_t mask = token_selection(p, blockIdx.x * 1024 + tid, sidx, sw);
+  const uint32_t mask = token_selection(p, blockIdx.x * kPermChunk + tid, sidx, sw);
   int my_count = 0;
 #pragma unroll
   for (int e = 0; e < kExpertsLocal; ++e) {
@@ -590,23 +591,23 @@ __global__ void __launch_bounds__(1024) permute_count_kernel(PermuteParams p) {
   __syncthreads();
   if (warp == 0) {
     int c = 0;
-#pragma unroll 8
-    for (int w = 0; w < 32; ++w) c += s_wcnt[w][lane];
+#pragma unroll
+    for (int w = 0; w < kPermWarps; ++w) c += s_wcnt[w][lane];
     p.chunk_counts[blockIdx.x * kChunkStride + lane] = c;
-    int tt = s_wtouch[lane];
+    int tt = lane < kPermWarps ? s_wtouch[lane] : 0;
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) tt += __shfl_xor_sync(0xffffffffu, tt, off);
     if (lane == 0) p.chunk_counts[blockIdx.x * kChunkStride + kExpertsLocal] = tt;
   }
 }
 
-__global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
+__global__ void __launch_bounds__(kPermChunk) permute_place_kernel(PermuteParams p) {
   __shared__ int s_start[kExpertsLocal];
   __shared__ int s_total[kExpertsLocal];
   __shared__ int s_base[kExpertsLocal];
-  __shared__ int s_wcnt[32][kExpertsLocal];
-  __shared__ int s_wpre[32][kExpertsLocal];
-  __shared__ int s_wtouch[32];
+  __shared__ int s_wcnt[kPermWarps][kExpertsLocal];
+  __shared__ int s_wpre[kPermWarps][kExpertsLocal];
+  __shared__ int s_wtouch[kPermWarps];
   __shared__ int s_tbase;
   pdl_launch_next();
   pdl_wait();
@@ -632,12 +633,26 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
       if (chunk == 0) *p.n_touched = tt;
     }
   }
-  if (warp == 0) {
+  {
+    // per-expert totals over all chunks and over earlier chunks, each warp
+    // taking every kPermWarps-th chunk
     int total = 0, before = 0;
-    for (int c = 0; c < static_cast<int>(gridDim.x); ++c) {
+#pragma unroll 4
+    for (int c = warp; c < static_cast<int>(gridDim.x); c += kPermWarps) {
       const int v = p.chunk_counts[c * kChunkStride + lane];
       total += v;
       if (c < chunk) before += v;
+    }
+    s_wcnt[warp][lane] = total;
+    s_wpre[warp][lane] = before;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int total = 0, before = 0;
+#pragma unroll
+    for (int w = 0; w < kPermWarps; ++w) {
+      total += s_wcnt[w][lane];
+      before += s_wpre[w][lane];
     }
     const int padded = (total + kSegAlign - 1) / kSegAlign * kSegAlign;
     int incl = padded;
@@ -660,18 +675,21 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
     }
   }
   __syncthreads();
-  if (chunk == 0 && tid < kExpertsLocal * kSegAlign) {
-    const int e = tid / kSegAlign;
-    const int j = tid % kSegAlign;
-    const int c = s_total[e];
-    const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
-    if (c + j < padded) {
-      p.perm_tok[s_start[e] + c + j] = -1;
-      p.perm_w[s_start[e] + c + j] = 0.f;
-      p.perm_row[s_start[e] + c + j] = -1;
+  if (chunk == 0) {
+    // padding rows: expert e = i / kSegAlign, slot j = i % kSegAlign
+    for (int i = tid; i < kExpertsLocal * kSegAlign; i += kPermChunk) {
+      const int e = i / kSegAlign;
+      const int j = i % kSegAlign;
+      const int c = s_total[e];
+      const int padded = (c + kSegAlign - 1) / kSegAlign * kSegAlign;
+      if (c + j < padded) {
+        p.perm_tok[s_start[e] + c + j] = -1;
+        p.perm_w[s_start[e] + c + j] = 0.f;
+        p.perm_row[s_start[e] + c + j] = -1;
+      }
     }
   }
-  const int t = chunk * 1024 + tid;
+  const int t = chunk * kPermChunk + tid;
   int sidx[kTopK];
   float sw[kTopK];
   const uint32_t mask = token_selection(p, t, sidx, sw);
@@ -691,15 +709,11 @@ __global__ void __launch_bounds__(1024) permute_place_kernel(PermuteParams p) {
   if (lane == 0) s_wtouch[warp] = __popc(tbal);
   __syncthreads();
   {
-    const int e = warp;
-    const int c = s_wcnt[lane][e];
-    int incl = c;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int o = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += o;
-    }
-    s_wpre[lane][e] = s_base[e] + incl - c;
+    // first row of this warp's tokens of expert `lane`: after earlier chunks'
+    // and this chunk's earlier warps' tokens of that expert
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += s_wcnt[w][lane];
+    s_wpre[warp][lane] = s_base[lane] + before;
   }
   int slot = -1;
   {
