@@ -763,9 +763,9 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
     reinterpret_cast<float4*>(p.y_acc)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   if (p.g1_acc != nullptr) {
     // token-major GEMM1 K-split sums start from zero when the split is on
-    int units = 0;
-#pragma unroll 4
-    for (int e = 0; e < kExpertsLocal; ++e) units += (p.counts[e] + 127) / 128 * kInterBlocks;
+    int units = (p.counts[lane] + 127) / 128 * kInterBlocks;   // lane = expert
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) units += __shfl_xor_sync(0xffffffffu, units, off);
     if (tm_gemm1_splits(units) > 1) {
       const int64_t g4 = static_cast<int64_t>(rows) * (kGemm1Out / 4);
       for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < g4; i += nthreads)
