@@ -123,17 +123,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// Four rows (y0..y3) of a box that is one row high, written to dst as four
-// consecutive rows with the tensor map's swizzle.
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const void* tmap, uint32_t bar, int x,
-                                            int y0, int y1, int y2, int y3) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(dst),
-      "l"(tmap), "r"(bar), "r"(x), "r"(y0), "r"(y1), "r"(y2), "r"(y3)
-      : "memory");
-}
-
 // Plain (untiled) bulk copy global -> shared; both addresses 16-byte
 // aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {

@@ -126,7 +126,8 @@ typedef struct moe_b200_workspace_layout {
   size_t c_scale;     /* fp32[16, cap_rows] */
   size_t y_acc;       /* fp32[T, 7168] combine buffer (decode: row t = token t; otherwise
                          row tok_slot[t], the first n_touched rows in use) */
-  size_t g1_acc;      /* fp32[cap_rows, 4096] K-split GEMM1 sums (decode plan, T <= 64; else 0) */
+  size_t g1_acc;      /* fp32 K-split GEMM1 sums: [cap_rows, 4096] for T <= 64, [1664, 4096] for
+                         T >= 512 (used when a batch has few token tiles); 0 for 64 < T < 512 */
   int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
   size_t chunk_counts; /* int32[ceil(T/1024), 33] per-chunk expert counts + touched tokens */
   size_t sched;       /* int32[4] work-unit counters of the GEMM kernels */
