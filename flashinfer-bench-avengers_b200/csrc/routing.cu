@@ -95,16 +95,34 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
   }
   const bool keep = rank < kTopKGroups;
 
+  // ---- the 128 candidates of the 4 kept groups, 4 per lane ------------------
+  // Lane L takes experts 32g + 4(L & 7) .. +3 of the (L >> 3)-th kept group g
+  // in increasing group order (owned by lane 4g + (L & 7) / 2, its elements
+  // 4(L & 1) .. +3), so lane order is still expert order and every lane has
+  // half the candidates to scan in each selection round.
+  const uint32_t kept = __ballot_sync(0xffffffffu, keep && (lane & 3) == 0);   // bit 4g per kept group
+  const int cg = static_cast<int>(__fns(kept, 0u, (lane >> 3) + 1)) >> 2;
+  const int src = 4 * cg + ((lane & 7) >> 1);
+  const bool upper = lane & 1;
+  float cand[4], cs[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float vl = __shfl_sync(0xffffffffu, sb[i], src);
+    const float vh = __shfl_sync(0xffffffffu, sb[4 + i], src);
+    const float sl = __shfl_sync(0xffffffffu, s[i], src);
+    const float sh = __shfl_sync(0xffffffffu, s[4 + i], src);
+    cand[i] = upper ? vh : vl;
+    cs[i] = upper ? sh : sl;
+  }
+  const int cand0 = 32 * cg + 4 * (lane & 7);   // expert of cand[0]
+
   // ---- top-8 experts among the kept groups --------------------------------
   // Each round takes the largest remaining candidate: every lane offers its
   // best untaken one (lowest index on equal values), one warp max over an
   // order-preserving integer key finds the value, and the lowest lane
-  // offering it wins -- lanes own increasing expert ranges, so that is the
+  // offering it wins -- lanes hold increasing expert ranges, so that is the
   // lowest expert index among equal values, the same total order as
   // ranks_before.
-  float cand[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) cand[j] = keep ? sb[j] : -INFINITY;
   uint32_t taken = 0;
   int sel_idx[kTopK];
   float sel_s[kTopK];
@@ -114,18 +132,18 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
     int bj = -1;
     float bs = 0.f;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < 4; ++j) {
       if (!((taken >> j) & 1u) && (bj < 0 || cand[j] > bv)) {
         bv = cand[j];
         bj = j;
-        bs = s[j];
+        bs = cs[j];
       }
     }
     const uint32_t key = bj >= 0 ? order_key(bv) : 0u;
     const uint32_t best = __reduce_max_sync(0xffffffffu, key);
     const int wl = __ffs(__ballot_sync(0xffffffffu, key == best)) - 1;
     if (lane == wl) taken |= 1u << bj;
-    sel_idx[k] = __shfl_sync(0xffffffffu, 8 * lane + bj, wl);
+    sel_idx[k] = __shfl_sync(0xffffffffu, cand0 + bj, wl);
     sel_s[k] = __shfl_sync(0xffffffffu, bs, wl);
   }
 
