@@ -67,6 +67,7 @@ constexpr int kTmSplitRows = 1664;
 
 __device__ __forceinline__ int tm_gemm1_splits(int units) {
   if (units <= 0 || units >= kTmSplitUnits) return 1;
+  if (4 * units < kTmSplitUnits) return 8;   // 7 of the 56 K blocks per unit
   return 2 * units < kTmSplitUnits ? 4 : 2;
 }
 
