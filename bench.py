@@ -337,8 +337,13 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
             starts[i].record()
             plain.replay()
             ends[i].record()
-            if sampler is not None:
-                sampler.sample_now()   # the GPU is still running the queued calls
+        if sampler is not None:
+            # every timed call is queued: sample while the GPU runs them (not
+            # between enqueues, which would delay this rank's calls and, with
+            # the NVLink combine, make the other ranks wait inside their steps)
+            while not ends[-1].query():
+                sampler.sample_now()
+                time.sleep(0.0002)
         torch.cuda.synchronize()
         if sampler is not None:
             sampler.disarm()
