@@ -157,7 +157,7 @@ class ClockSampler:
 
     def sample_now(self):
         """One sample from the calling thread (the timing loop calls this
-        after each step's end event, outside the [start, end] event pair)."""
+        once all timed calls are queued, while the GPU still runs them)."""
         if self.nvml is None:
             return
         try:
