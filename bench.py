@@ -95,10 +95,12 @@ def load_peaks() -> dict:
 class ClockSampler:
     """SM clock and throttle reasons of this rank's GPU during the timed region.
 
-    With NVML (nvidia-ml-py) a background thread polls every 0.25 ms and keeps
-    only the samples taken while the sampler is armed, which `time_layer` does
-    around its timed loops (a few milliseconds). Without NVML, nvidia-smi
-    samples every 200 ms for the whole block instead."""
+    With NVML (nvidia-ml-py) samples are kept only while the sampler is armed,
+    which `time_layer` does around its timed loop (a few milliseconds): a
+    background thread polls every 0.25 ms when it gets the interpreter, and
+    the timing loop itself samples once all timed calls are queued, until
+    the last one ends. Without NVML, nvidia-smi samples every 200 ms for the
+    whole block instead."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
