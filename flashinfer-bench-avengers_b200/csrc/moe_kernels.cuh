@@ -24,7 +24,7 @@ struct PermuteParams {
   const int32_t* topk_idx;  // [T, 8]
   const float* topk_w;      // [T, 8]
   int* counts;              // [32] assignments per local expert (written)
-  int* chunk_counts;        // [ceil(T/1024), 33] per-chunk expert counts + touched tokens (multi-CTA path)
+  int* chunk_counts;        // [ceil(T/kPermChunk), 33] per-chunk expert counts + touched tokens (multi-CTA path)
   uint32_t* status;         // device status word (cleared)
   int* sched;               // [4] GEMM unit counters (cleared)
   int num_tokens;
