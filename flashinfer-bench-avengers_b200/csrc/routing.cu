@@ -798,8 +798,18 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
     if (tok < 0) continue;
     uint4* dst = reinterpret_cast<uint4*>(p.a_perm + static_cast<int64_t>(r) * kHidden);
     const uint4* src = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(tok) * kHidden);
+    // loads first, then stores (two halves of the row): the stores may alias
+    // the loads as far as the compiler knows, so interleaving them would keep
+    // one load in flight at a time
+    constexpr int kHalf = kHidden / 16 / 32 / 2;
 #pragma unroll
-    for (int i = 0; i < kHidden / 16 / 32; ++i) dst[lane + 32 * i] = src[lane + 32 * i];
+    for (int h = 0; h < 2; ++h) {
+      uint4 v[kHalf];
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) v[i] = src[lane + 32 * (h * kHalf + i)];
+#pragma unroll
+      for (int i = 0; i < kHalf; ++i) dst[lane + 32 * (h * kHalf + i)] = v[i];
+    }
     for (int kb = lane; kb < kHiddenBlocks; kb += 32)
       p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = p.hidden_scale[static_cast<int64_t>(kb) * p.num_tokens + tok];
   }
