@@ -208,7 +208,7 @@ int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, i
     p.area[q] = area;
     p.y[q] = reinterpret_cast<const float*>(ws + l.y_acc);
     // decode-size calls keep one combine row per token
-    p.slot[q] = l.g1_acc != 0 ? nullptr : reinterpret_cast<const int32_t*>(ws + l.tok_slot);
+    p.slot[q] = num_tokens <= kDecodeMaxTokens ? nullptr : reinterpret_cast<const int32_t*>(ws + l.tok_slot);
   }
   p.out = static_cast<uint16_t*>(output);
   p.status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_workspaces[rank]) + l.status);

@@ -11,28 +11,27 @@
 
 namespace moe {
 
-// Output row t comes from combine row tok_slot[t] (zeros when -1: the token
-// has no local pick), or from row t when tok_slot is null. A CTA step covers
-// one 2048-column segment of a row (4 per row); a thread converts 8 columns
-// (two float4 loads, one 16-byte store).
-__global__ void __launch_bounds__(256) finalize_kernel(const float* y_acc, const int32_t* tok_slot,
-                                                       uint16_t* out, int num_tokens) {
+// Combine row r becomes output row slot_tok[r], for the *n_touched rows in
+// use; with slot_tok null, all num_tokens rows are converted (row r =
+// token r). Output rows of tokens without a combine row (no local
+// pick) are not touched here: route_kernel has written their zeros. A CTA
+// step covers one 2048-column segment of a row (4 per row); a thread
+// converts 8 columns (two float4 loads, one 16-byte store).
+__global__ void __launch_bounds__(256) finalize_kernel(const float* y_acc, const int32_t* slot_tok,
+                                                       const int* n_touched, uint16_t* out, int num_tokens) {
   pdl_launch_next();
   pdl_wait();
   constexpr int kOcts = kHidden / 8;   // 896 groups of 8 columns per row
   constexpr int kSegs = 4;             // ceil(896 / 256)
-  const int items = num_tokens * kSegs;
+  const int rows = slot_tok != nullptr ? min(*n_touched, num_tokens) : num_tokens;
+  const int items = rows * kSegs;
   for (int it = blockIdx.x; it < items; it += gridDim.x) {
-    const int t = it / kSegs;
+    const int r = it / kSegs;
     const int j = (it % kSegs) * 256 + threadIdx.x;
     if (j >= kOcts) continue;
-    const int slot = tok_slot != nullptr ? __ldg(tok_slot + t) : t;
+    const int t = slot_tok != nullptr ? __ldg(slot_tok + r) : r;
     uint4* orow = reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * kHidden);
-    if (slot < 0) {
-      orow[j] = make_uint4(0u, 0u, 0u, 0u);
-      continue;
-    }
-    const float4* yrow = reinterpret_cast<const float4*>(y_acc + static_cast<int64_t>(slot) * kHidden);
+    const float4* yrow = reinterpret_cast<const float4*>(y_acc + static_cast<int64_t>(r) * kHidden);
     {
       const float4 a = yrow[2 * j];
       const float4 b = yrow[2 * j + 1];

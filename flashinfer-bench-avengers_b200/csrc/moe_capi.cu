@@ -116,6 +116,8 @@ moe_b200_workspace_layout make_layout(int64_t T) {
     l.g1_acc = off;
     off = align_up(off + static_cast<size_t>(kTmSplitRows) * kGemm1Out * sizeof(float));
   }
+  l.slot_tok = off;
+  off = align_up(off + static_cast<size_t>(T) * sizeof(int32_t));
   l.total_bytes = off;
   l.cap_rows = static_cast<int64_t>(cap);
   return l;
@@ -201,7 +203,7 @@ int grid_for(int64_t T, int bn, int row_blocks, int splits, int sm_count) {
 }
 
 int launch_route(const float* logits, const void* bias, int bias_dtype, int T, float rsf,
-                 int local_off, int32_t* topk_idx, float* topk_w, cudaStream_t s) {
+                 int local_off, int32_t* topk_idx, float* topk_w, uint16_t* out, cudaStream_t s) {
   RouteParams rp;
   rp.logits = logits;
   rp.bias = bias;
@@ -211,6 +213,7 @@ int launch_route(const float* logits, const void* bias, int bias_dtype, int T, f
   rp.local_expert_offset = local_off;
   rp.topk_idx = topk_idx;
   rp.topk_w = topk_w;
+  rp.out = out;
   // The first kernel of a call is launched without the dependent-launch
   // attribute, so it starts only after all earlier work on the stream.
   route_kernel<<<static_cast<unsigned>(div_up(T, 8)), 256, 0, s>>>(rp);
@@ -287,6 +290,7 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   rp.local_expert_offset = local_off;
   rp.topk_idx = reinterpret_cast<int32_t*>(ws + l.topk_idx);
   rp.topk_w = reinterpret_cast<float*>(ws + l.topk_w);
+  rp.out = nullptr;
   DecodeFrontParams dp;
   dp.counts = counts;
   dp.seg_off = seg_off;
@@ -349,7 +353,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
   if (output != nullptr &&
       launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
-                    static_cast<const int32_t*>(nullptr), static_cast<uint16_t*>(output), T) != cudaSuccess)
+                    static_cast<const int32_t*>(nullptr), static_cast<const int*>(nullptr),
+                    static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;
@@ -419,7 +424,7 @@ int moe_b200_route(const float* routing_logits, const void* routing_bias, int ro
   int st = current_device_info(&di);
   if (st != MOE_B200_OK) return st;
   return launch_route(routing_logits, routing_bias, routing_bias_dtype, static_cast<int>(num_tokens),
-                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w,
+                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w, nullptr,
                       static_cast<cudaStream_t>(stream));
 }
 
@@ -487,6 +492,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   int32_t* perm_row = reinterpret_cast<int32_t*>(ws + l.perm_row);
   int32_t* tok_slot = reinterpret_cast<int32_t*>(ws + l.tok_slot);
   int* n_touched = reinterpret_cast<int*>(ws + l.n_touched);
+  int32_t* slot_tok = reinterpret_cast<int32_t*>(ws + l.slot_tok);
 
   if (plan.decode)
     return run_decode(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale,
@@ -513,7 +519,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   mark_stage(0, s);
   mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
-                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w, s);
+                    static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w,
+                    static_cast<uint16_t*>(output), s);
   if (st != MOE_B200_OK) return st;
   mark_stage(2, s);
 
@@ -532,6 +539,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   pp.perm_row = perm_row;
   pp.tok_slot = tok_slot;
   pp.n_touched = n_touched;
+  pp.slot_tok = slot_tok;
   if (T <= 1024) {
     if (launch_kernel(permute_kernel, 1, 1024, 0, s, true, pp) != cudaSuccess) return MOE_B200_ERR_CUDA;
   } else {
@@ -612,7 +620,8 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   const int fgrid = 4 * T < di.sm_count * 8 ? 4 * T : di.sm_count * 8;   // 4 row segments
   if (output != nullptr &&
       launch_kernel(finalize_kernel, fgrid, 256, 0, s, true, static_cast<const float*>(y_acc),
-                    static_cast<const int32_t*>(tok_slot), static_cast<uint16_t*>(output), T) != cudaSuccess)
+                    static_cast<const int32_t*>(slot_tok), static_cast<const int*>(n_touched),
+                    static_cast<uint16_t*>(output), T) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;

@@ -18,6 +18,7 @@ struct RouteParams {
   int local_expert_offset;
   int32_t* topk_idx;        // [T, 8] global expert ids, best first
   float* topk_w;            // [T, 8]
+  uint16_t* out;            // [T, 7168] bf16 output: rows of tokens with no local pick are zeroed (or null)
 };
 
 struct PermuteParams {
@@ -37,6 +38,7 @@ struct PermuteParams {
   int32_t* tok_slot;        // [T] combine row of each token, -1 if untouched
   int32_t* perm_row;        // [cap] combine row of each permuted row, -1 for padding
   int* n_touched;           // [1] number of touched tokens
+  int32_t* slot_tok;        // [T] token of each combine row (first n_touched entries)
 };
 
 struct GatherParams {
@@ -150,7 +152,8 @@ __global__ void permute_kernel(PermuteParams p);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
-__global__ void finalize_kernel(const float* y_acc, const int32_t* tok_slot, uint16_t* out, int num_tokens);
+__global__ void finalize_kernel(const float* y_acc, const int32_t* slot_tok, const int* n_touched, uint16_t* out,
+                                int num_tokens);
 __global__ void route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp);
 
 }  // namespace moe

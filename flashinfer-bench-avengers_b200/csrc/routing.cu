@@ -170,9 +170,20 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
 __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   pdl_launch_next();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
   int idx;
   float w;
-  if (t < p.num_tokens) route_token(p, t, threadIdx.x & 31, idx, w);
+  if (t >= p.num_tokens) return;
+  route_token(p, t, lane, idx, w);
+  // A token with no pick among the local experts gets no combine row, so its
+  // output row is zero: written here, where the stores overlap the routing
+  // arithmetic of the other warps, and skipped by finalize_kernel.
+  const bool local = lane < kTopK && static_cast<unsigned>(idx - p.local_expert_offset) < kExpertsLocal;
+  if (p.out != nullptr && !__any_sync(0xffffffffu, local)) {
+    uint4* orow = reinterpret_cast<uint4*>(p.out + static_cast<int64_t>(t) * kHidden);
+#pragma unroll
+    for (int i = 0; i < kHidden / 8 / 32; ++i) orow[lane + 32 * i] = make_uint4(0u, 0u, 0u, 0u);
+  }
 }
 
 namespace {
@@ -308,6 +319,7 @@ __device__ __forceinline__ void permute_body(const PermuteParams& p) {
       }
       if (mask != 0u) slot = trun + before + __popc(tbal & lt_mask);
       if (t < p.num_tokens) p.tok_slot[t] = slot;
+      if (slot >= 0) p.slot_tok[slot] = t;
       trun += total;
     }
 
@@ -740,6 +752,7 @@ __global__ void __launch_bounds__(kPermChunk) permute_place_kernel(PermuteParams
     for (int off = 16; off >= 1; off >>= 1) before += __shfl_xor_sync(0xffffffffu, before, off);
     if (mask != 0u) slot = s_tbase + before + __popc(tbal & lt_mask);
     if (t < p.num_tokens) p.tok_slot[t] = slot;
+    if (slot >= 0) p.slot_tok[slot] = t;
   }
   __syncthreads();
   uint32_t m = mask;

@@ -66,6 +66,7 @@ class WorkspaceLayout(ctypes.Structure):
         ("perm_row", ctypes.c_size_t),
         ("tok_slot", ctypes.c_size_t),
         ("n_touched", ctypes.c_size_t),
+        ("slot_tok", ctypes.c_size_t),
     ]
 
 

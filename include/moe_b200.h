@@ -129,11 +129,12 @@ typedef struct moe_b200_workspace_layout {
   size_t g1_acc;      /* fp32 K-split GEMM1 sums: [cap_rows, 4096] for T <= 64, [1664, 4096] for
                          T >= 512 (used when a batch has few token tiles); 0 for 64 < T < 512 */
   int64_t cap_rows;   /* round_up(8T, 16) + 32 * 16 + 128 */
-  size_t chunk_counts; /* int32[ceil(T/1024), 33] per-chunk expert counts + touched tokens */
+  size_t chunk_counts; /* int32[ceil(T/256), 33] per-chunk expert counts + touched tokens */
   size_t sched;       /* int32[4] work-unit counters of the GEMM kernels */
   size_t perm_row;    /* int32[cap_rows] combine row of each permuted row, -1 in padding (not decode) */
   size_t tok_slot;    /* int32[T] combine row of each token, -1 without a local pick (not decode) */
   size_t n_touched;   /* int32 number of tokens with a local pick (not decode) */
+  size_t slot_tok;    /* int32[T] token of each combine row, the first n_touched in use (not decode) */
 } moe_b200_workspace_layout;
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);

@@ -68,16 +68,17 @@ def test_workspace_size_and_layout(lib):
         token_major = T >= moe_host.TOKEN_MAJOR_MIN_TOKENS
         if decode or token_major:
             offs += [lay.g1_acc]
+        offs += [lay.slot_tok]   # appended last, so the other offsets did not move
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
-        assert offs[-1] < n
+        assert n - lay.slot_tok >= 4 * T
         assert lay.c_lo - lay.c_hi >= lay.cap_rows * 2048
         if decode:
             assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
-            assert n - lay.g1_acc >= lay.cap_rows * 4096 * 4
+            assert lay.slot_tok - lay.g1_acc >= lay.cap_rows * 4096 * 4
         elif token_major:
             # K-split GEMM1 sums of batches with few token tiles: 1,664 rows
             assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
-            assert n - lay.g1_acc >= 1664 * 4096 * 4
+            assert lay.slot_tok - lay.g1_acc >= 1664 * 4096 * 4
         else:
             assert lay.g1_acc == 0
         if T > 65:  # plans without the decode scratch grow with T

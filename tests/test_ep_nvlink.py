@@ -58,7 +58,7 @@ def _worker(rank: int, world: int, port: int, cases, results):
             lay = moe_host.workspace_layout(T)
             ws = comb.workspace
             y = ws[lay.y_acc: lay.y_acc + 4 * T * 7168].view(torch.float32).view(T, 7168)
-            if lay.g1_acc != 0:   # decode plan: one row per token
+            if T <= 64:   # decode plan: one row per token
                 full = y.clone()
             else:
                 slot = ws[lay.tok_slot: lay.tok_slot + 4 * T].view(torch.int32).long()
@@ -94,7 +94,8 @@ def test_nvlink_combine_ranks():
 
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    cases = [(16, "uniform"), (200, "uniform")]   # decode plan; compact combine rows
+    # decode plan; compact combine rows; token-major GEMMs (K split, compact rows)
+    cases = [(16, "uniform"), (200, "uniform"), (600, "uniform")]
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, cases, results)) for r in range(world)]
     for p in procs:

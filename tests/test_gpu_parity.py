@@ -79,8 +79,8 @@ def test_routing_fp32_bias(host):
 
 
 # -------------------------------------------------------------- permutation
-@pytest.mark.parametrize("T,offset,variant", [(1, 0, "uniform"), (64, 0, "uniform"), (3000, 32, "uniform"),
-                                              (2500, 0, "hot")])
+@pytest.mark.parametrize("T,offset,variant", [(1, 0, "uniform"), (64, 0, "uniform"), (700, 32, "uniform"),
+                                              (3000, 32, "uniform"), (2500, 0, "hot")])
 def test_permutation_bit_exact(host, T, offset, variant):
     inp = _gpu_inputs(T, 5, variant, offset)
     out = host.run(*workloads.as_args(inp))
@@ -120,6 +120,9 @@ def test_permutation_bit_exact(host, T, offset, variant):
         assert torch.equal(tok_slot, expect_slot)
         n_touched = int(ws[lay.n_touched: lay.n_touched + 4].view(torch.int32).cpu()[0])
         assert n_touched == int(touched.sum())
+        # and the inverse map: token of each combine row in use
+        slot_tok = ws[lay.slot_tok: lay.slot_tok + 4 * n_touched].view(torch.int32).cpu().long()
+        assert torch.equal(slot_tok, touched.nonzero().flatten())
         perm_row = ws[lay.perm_row: lay.perm_row + 4 * n].view(torch.int32).cpu().long()
         assert torch.equal(perm_row[valid], expect_slot[perm_tok[valid]])
         assert bool((perm_row[~valid] == -1).all())
@@ -172,6 +175,27 @@ def test_no_local_experts_gives_zeros(host):
     out = host.run(*workloads.as_args(inp))
     torch.cuda.synchronize()
     assert torch.count_nonzero(out.float()) == 0
+
+
+@pytest.mark.parametrize("T,variant,offset", [(200, "uniform", 256), (300, "zipf", 0), (3000, "uniform", 32)])
+def test_untouched_rows_written_over_nan(host, T, variant, offset):
+    """Rows of tokens with no local pick are written by the routing kernel and
+    skipped by the final conversion: an output buffer full of NaNs must come
+    back with those rows zero and the others finite (and, where the oracle is
+    cheap, equal to it)."""
+    inp = _gpu_inputs(T, 11, variant, offset)
+    out = torch.full((T, workloads.H), float("nan"), dtype=torch.bfloat16, device="cuda")
+    host.run_dps(*workloads.as_args(inp), out)
+    torch.cuda.synchronize()
+    assert not bool(torch.isnan(out.float()).any())
+    idx, _ = host.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    touched = ((idx >= offset) & (idx < offset + 32)).any(dim=1)
+    assert int(touched.sum()) < T
+    assert torch.count_nonzero(out[~touched].float()) == 0
+    if variant != "uniform" or offset >= 256:
+        ref = moe_oracle.moe_forward(*workloads.as_args(inp))
+        _check_output(out, ref, f"T={T} {variant} offset={offset} (NaN-filled output)")
+    assert host.read_status(host.get_workspace(T, out.device)) == 0
 
 
 def test_zero_tokens(host):
