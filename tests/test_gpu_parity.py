@@ -228,6 +228,22 @@ def test_large_batches_row_subset(host, T, variant, seed):
     assert host.read_status(host.get_workspace(T, out.device)) == 0
 
 
+def test_maximum_token_count(host):
+    """T = MAX_TOKENS (262,144): the permuted buffers hold 2.1 M rows (a_perm
+    alone is 15 GB, beyond 32-bit byte offsets; the workspace is about 34 GB).
+    The first, the last and 30 random rows are checked against the oracle run
+    on those tokens."""
+    T = host.MAX_TOKENS
+    inp = _gpu_inputs(T, 51, "uniform")
+    out = host.run(*workloads.as_args(inp))
+    torch.cuda.synchronize()
+    g = torch.Generator().manual_seed(51)
+    sub = torch.cat([torch.tensor([0, T - 1]), torch.randperm(T - 2, generator=g)[:30] + 1]).sort().values
+    ref = moe_oracle.moe_forward(*workloads.as_args(dict(inp)), token_subset=sub)
+    _check_output(out[sub.cuda()].cpu(), ref, f"T={T} uniform subset")
+    assert host.read_status(host.get_workspace(T, out.device)) == 0
+
+
 def test_repeatability(host):
     inp = _gpu_inputs(512, 31, "hot")
     a = host.run(*workloads.as_args(inp)).float()
