@@ -269,11 +269,26 @@ def weights_exceed_l2(st: dict) -> bool:
     return st["E_act"] * (W13_BYTES + W2_BYTES) > 2 * L2_BYTES
 
 
+# --bf16-hidden: the calls take bf16 hidden states (inp["hidden_bf16"]) and
+# quantise them inside the layer (moe_b200_run_bf16_hidden), one GPU only.
+BF16_HIDDEN = False
+
+
+def token_keys() -> tuple:
+    """The per-call activation tensors of a step."""
+    return ("routing_logits", "hidden_bf16") if BF16_HIDDEN else ("routing_logits", "hidden_states",
+                                                                     "hidden_states_scale")
+
+
 def layer_call(inp: dict, combiner=None):
     """One call of the layer on inp's tokens into `out`: the library entry
     point at N=1, this rank's shard plus the NVLink combine at N>1."""
     import moe_host
 
+    if BF16_HIDDEN:
+        args = workloads.as_args(inp)
+        return lambda tokens, out: moe_host.run_bf16_hidden(tokens["routing_logits"], inp["routing_bias"],
+                                                            tokens["hidden_bf16"], *args[4:], output=out)
     if combiner is None:
         args = workloads.as_args(inp)
         return lambda tokens, out: moe_host.run_dps(tokens["routing_logits"], inp["routing_bias"],
@@ -301,7 +316,7 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
     import torch.distributed as dist
 
     call = layer_call(inp, combiner)
-    tokens = {k: inp[k] for k in ("routing_logits", "hidden_states", "hidden_states_scale")}
+    tokens = {k: inp[k] for k in token_keys()}
     T = inp["routing_logits"].shape[0]
     dev = inp["routing_logits"].device
     out = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
@@ -378,7 +393,7 @@ def time_e2e(inp: dict, steps: int, warmup: int, group=None, combiner=None) -> d
     call = layer_call(inp, combiner)
     dev = inp["routing_logits"].device
     T = inp["routing_logits"].shape[0]
-    keys = ("routing_logits", "hidden_states", "hidden_states_scale")
+    keys = token_keys()
     host_in = {k: inp[k].cpu().pin_memory() for k in keys}
     dev_in = [{k: torch.empty_like(v, device=dev) for k, v in host_in.items()} for _ in range(2)]
     out = [torch.empty(T, 7168, dtype=torch.bfloat16, device=dev) for _ in range(2)]
@@ -508,6 +523,8 @@ def main() -> None:
     ap.add_argument("--no-extras", action="store_true", help="skip the sweep/prefill/stress points")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
                     help="headline configuration (default: config 1 decode, T=64)")
+    ap.add_argument("--bf16-hidden", action="store_true",
+                    help="bf16 hidden states quantised inside the layer (one GPU; the extras are skipped)")
     args = ap.parse_args()
     warmup = max(args.warmup, 3)
 
@@ -536,6 +553,13 @@ def main() -> None:
     HEADLINE_T, variant, desc = WORKLOADS[args.workload]
     offset = (32 * rank) % 256
     inp = workloads.make_inputs(HEADLINE_T, SEED, device, variant, offset, 2.5, weight_seed=SEED + 1 + rank)
+    if args.bf16_hidden:
+        if world > 1:
+            raise SystemExit("--bf16-hidden runs on one GPU")
+        global BF16_HIDDEN
+        BF16_HIDDEN = True
+        # the bf16 source of inp's e4m3 hidden states: the same tokens and routing
+        inp["hidden_bf16"] = workloads.make_hidden_bf16(HEADLINE_T, SEED, device)
     st = routing_stats(inp)
 
     # every rank must take the same timing path (the all-reduces inside it)
@@ -609,6 +633,8 @@ def main() -> None:
                    "T": HEADLINE_T, "local_expert_offset": offset, "E_act": st["E_act"],
                    "sum_Tk": st["sum_Tk"],
                    "parallelism": f"ep{world}" + (" + NVLink combine (peer loads/stores, one kernel)" if world > 1 else ""),
+                   **({"hidden": "bf16, quantised per 1x128 block inside the row copy (moe_b200_run_bf16_hidden)"}
+                      if BF16_HIDDEN else {}),
                    "l2": ("back to back: each call streams the active experts' weights "
                           f"({st['E_act'] * (W13_BYTES + W2_BYTES) / 1e6:.0f} MB > 2 x 126 MB L2), so no "
                           "weight byte is L2-resident from the previous call; value_l2_write_flushed is the "
@@ -624,7 +650,7 @@ def main() -> None:
         "clocks": clocks.summary(),
     }
 
-    if world == 1 and not args.no_extras and args.workload == "decode":
+    if world == 1 and not args.no_extras and args.workload == "decode" and not BF16_HIDDEN:
         n_extra = max(5, args.steps // 2)
         line["sweep"] = [point(T, "uniform", n_extra, warmup, flush, peaks, device) for T in (1, 4, 16, 64)]
         line["prefill"] = point(4096, "hot", n_extra, warmup, flush, peaks, device)

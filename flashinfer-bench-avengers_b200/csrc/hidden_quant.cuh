@@ -1,0 +1,134 @@
+// Per-token 1x128 block quantiser of bf16 hidden states: the step that
+// produces this operator's e4m3 hidden states and their [56, T] fp32 block
+// scales. The reference takes both pre-quantised (main.py:31-42); the
+// benchmark inputs it is measured on follow this convention, which is
+// restated here: per 128-column block of a token row,
+//   scale = amax / 448 (IEEE fp32 division; 1 for an all-zero block),
+//   value = e4m3(x / scale), x / scale by IEEE fp32 division, rounded to
+//           the nearest e4m3 value (ties to even, saturating at 448).
+// Inputs are finite bf16.
+//
+// No division is executed in the common case:
+// * scale: s0 = amax * c with c = fp32(1/448), then one FMA correction
+//   s = fma(fma(-s0, 448, amax), c, s0). For every positive finite bf16
+//   amax whose quotient is a normal fp32 number this equals the IEEE
+//   quotient (checked exhaustively, all 31,392 such values); smaller amax
+//   take the division.
+// * values: inv = 1/scale from the hardware reciprocal estimate refined by
+//   one Newton step (error below 1 ulp), so |x| * inv is within 4 ulp of the
+//   fp32 quotient. e4m3 rounding is monotonic: when the values 6 ulp below
+//   and above |x| * inv round to the same e4m3 value, that is the rounding
+//   of the quotient. Otherwise (a value within 6 ulp of an e4m3 rounding
+//   midpoint, about 1 in 10^5) the lane's 8 values and the scale are formed
+//   again by IEEE division.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+
+#include <cstdint>
+
+#include "moe_shapes.cuh"
+
+namespace moe {
+
+struct Quant8 {
+  uint2 q;      // 8 e4m3 bytes, element j in byte j
+  float scale;  // the block's scale
+};
+
+// The lane's 8 values and the scale by IEEE division (rare path).
+static __device__ __noinline__ Quant8 quantize8_by_division(uint4 v, float amax) {
+  Quant8 r;
+  r.scale = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t q[2] = {0u, 0u};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t h = j & 1 ? (w[j >> 1] >> 16) : (w[j >> 1] & 0xffffu);
+    const float x = __uint_as_float(h << 16);
+    const uint32_t m = __nv_cvt_float_to_fp8(__fdiv_rn(fabsf(x), r.scale), __NV_SATFINITE, __NV_E4M3);
+    q[j >> 2] |= (m | ((h >> 8) & 0x80u)) << (8 * (j & 3));
+  }
+  r.q = make_uint2(q[0], q[1]);
+  return r;
+}
+
+// Lane l of a half-warp holds 8 consecutive bf16 values of one 128-column
+// block in v; returns their e4m3 bytes and the block scale (the same in all
+// 16 lanes of the half-warp). Called by all 32 lanes.
+__device__ __forceinline__ Quant8 quantize8(const uint4& v) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+  uint32_t mw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) mw[j] = w[j] & 0x7fff7fffu;   // magnitudes
+  // non-negative bf16 values order like their bit patterns
+  const __nv_bfloat162 m01 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&mw[0]),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&mw[1]));
+  const __nv_bfloat162 m23 = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&mw[2]),
+                                     *reinterpret_cast<const __nv_bfloat162*>(&mw[3]));
+  const __nv_bfloat162 mm = __hmax2(m01, m23);
+  const uint32_t mb = *reinterpret_cast<const uint32_t*>(&mm);
+  float amax = fmaxf(__uint_as_float(mb << 16), __uint_as_float(mb & 0xffff0000u));
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+
+  constexpr float kInv448 = 1.0f / 448.0f;
+  const float s0 = amax * kInv448;
+  float scale = fmaf(fmaf(-s0, 448.0f, amax), kInv448, s0);
+  scale = amax > 0.f ? scale : 1.0f;
+  float inv;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(scale));
+  inv = fmaf(fmaf(-scale, inv, 1.0f), inv, inv);
+
+  uint32_t lo[4], hi[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t y0 = __float_as_uint(__uint_as_float(mw[j] << 16) * inv);
+    const uint32_t y1 = __float_as_uint(__uint_as_float(mw[j] & 0xffff0000u) * inv);
+    lo[j] = __nv_cvt_float2_to_fp8x2(make_float2(__uint_as_float(max(y0, 6u) - 6u),
+                                                 __uint_as_float(max(y1, 6u) - 6u)),
+                                     __NV_SATFINITE, __NV_E4M3);
+    hi[j] = __nv_cvt_float2_to_fp8x2(make_float2(__uint_as_float(y0 + 6u), __uint_as_float(y1 + 6u)),
+                                     __NV_SATFINITE, __NV_E4M3);
+  }
+  const uint32_t l0 = lo[0] | (lo[1] << 16), l1 = lo[2] | (lo[3] << 16);
+  const uint32_t h0 = hi[0] | (hi[1] << 16), h1 = hi[2] | (hi[3] << 16);
+  const bool divide = (l0 != h0) | (l1 != h1) | (amax > 0.f && amax < 448.0f * 1.17549435e-38f);
+  if (divide) return quantize8_by_division(v, amax);
+  // sign of element j (bit 15 of its bf16) into bit 7 of byte j
+  Quant8 r;
+  r.q = make_uint2(l0 | (__byte_perm(w[0], w[1], 0x7531) & 0x80808080u),
+                   l1 | (__byte_perm(w[2], w[3], 0x7531) & 0x80808080u));
+  r.scale = scale;
+  return r;
+}
+
+// One warp quantises one 7168-column row in 28 passes of 256 columns. In a
+// pass lane l holds columns 8l .. 8l+7, so lanes 0-15 form one 128-column
+// block and lanes 16-31 the next. The 7 loads of a quarter row are issued
+// before any of its stores (the destination may alias the source as far as
+// the compiler knows). scale_out(kb, scale) is called by lanes 0 and 16 for
+// block kb. src and dst must be 16- and 8-byte aligned.
+template <typename ScaleOut>
+__device__ __forceinline__ void quantize_row_1x128(const uint16_t* src, uint8_t* dst, int lane,
+                                                   ScaleOut scale_out) {
+  constexpr int kPasses = kHidden / 256;
+  constexpr int kChunk = kPasses / 4;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint2* d2 = reinterpret_cast<uint2*>(dst);
+#pragma unroll 1
+  for (int h = 0; h < kPasses / kChunk; ++h) {
+    uint4 v[kChunk];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) v[i] = s4[(h * kChunk + i) * 32 + lane];
+#pragma unroll
+    for (int i = 0; i < kChunk; ++i) {
+      const Quant8 r = quantize8(v[i]);
+      d2[(h * kChunk + i) * 32 + lane] = r.q;
+      if ((lane & 15) == 0) scale_out(2 * (h * kChunk + i) + (lane >> 4), r.scale);
+    }
+  }
+}
+
+}  // namespace moe

@@ -118,6 +118,13 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   }
   l.slot_tok = off;
   off = align_up(off + static_cast<size_t>(T) * sizeof(int32_t));
+  if (!plan.decode) {
+    // e4m3 copy of bf16 hidden states (moe_b200_run_bf16_hidden), one row per token
+    l.hidden_q = off;
+    off = align_up(off + static_cast<size_t>(T) * kHidden);
+    l.hidden_qs = off;
+    off = align_up(off + static_cast<size_t>(T) * kHiddenBlocks * sizeof(float));
+  }
   l.total_bytes = off;
   l.cap_rows = static_cast<int64_t>(cap);
   return l;
@@ -245,7 +252,8 @@ void mark_stage(int i, cudaStream_t s) {
 //      split 2 ways, red.add into y_acc
 //   -> finalize (bf16).
 int run_decode(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
-               const void* hidden_states, const float* hidden_states_scale, const void* gemm1_weights,
+               const void* hidden_states, const float* hidden_states_scale, bool hidden_bf16,
+               const void* gemm1_weights,
                const float* gemm1_weights_scale, const void* gemm2_weights,
                const float* gemm2_weights_scale, int local_off, float rsf, int T, void* output,
                uint8_t* ws, const moe_b200_workspace_layout& l, const DeviceInfo& di, cudaStream_t s) {
@@ -299,15 +307,19 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   dp.status = status;
   dp.sched = sched;
   dp.g1_acc = g1_acc;
-  dp.hidden = static_cast<const uint8_t*>(hidden_states);
-  dp.hidden_scale = hidden_states_scale;
+  dp.hidden = hidden_bf16 ? nullptr : static_cast<const uint8_t*>(hidden_states);
+  dp.hidden_scale = hidden_bf16 ? nullptr : hidden_states_scale;
+  dp.hidden_bf16 = hidden_bf16 ? static_cast<const uint16_t*>(hidden_states) : nullptr;
   dp.a_perm = a_perm;
   dp.sa_perm = sa_perm;
   dp.cap = cap;
   dp.local_expert_offset = local_off;
   // First kernel of the call: no dependent-launch attribute. The cluster
   // shape is compiled into the kernel.
-  route_permute_decode_kernel<<<kDecodeClusterCtas, 256, 0, s>>>(rp, dp);
+  if (hidden_bf16)
+    route_permute_decode_kernel<true><<<kDecodeClusterCtas, 256, 0, s>>>(rp, dp);
+  else
+    route_permute_decode_kernel<false><<<kDecodeClusterCtas, 256, 0, s>>>(rp, dp);
   if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
   mark_stage(2, s);
   mark_stage(3, s);
@@ -441,18 +453,21 @@ int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream) 
   return v == 0 ? MOE_B200_OK : MOE_B200_ERR_DEVICE_TIMEOUT;
 }
 
-int moe_b200_run(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
-                 const void* hidden_states, const float* hidden_states_scale,
-                 const void* gemm1_weights, const float* gemm1_weights_scale,
-                 const void* gemm2_weights, const float* gemm2_weights_scale,
-                 int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
-                 void* output, void* workspace, size_t workspace_bytes, void* stream) {
+// The layer on e4m3 hidden states with their block scales, or (hidden_bf16)
+// on bf16 hidden states that the row copy into the permuted buffers
+// quantises (hidden_states_scale unused).
+static int run_layer(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                     const void* hidden_states, const float* hidden_states_scale, bool hidden_bf16,
+                     const void* gemm1_weights, const float* gemm1_weights_scale,
+                     const void* gemm2_weights, const float* gemm2_weights_scale,
+                     int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
+                     void* output, void* workspace, size_t workspace_bytes, void* stream) {
   // ---- argument checks (no device work before they pass) -----------------
   if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
-  if (!routing_logits || !routing_bias || !hidden_states || !hidden_states_scale ||
+  if (!routing_logits || !routing_bias || !hidden_states || (!hidden_bf16 && !hidden_states_scale) ||
       !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !workspace)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
@@ -496,7 +511,7 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
 
   if (plan.decode)
     return run_decode(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale,
-                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
+                      hidden_bf16, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
                       static_cast<float>(routed_scaling_factor), T, output, ws, l, di, s);
 
   // ---- tensor maps ---------------------------------------------------------
@@ -517,6 +532,19 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
   // clears the status word, the gather kernel clears the accumulation
   // buffers, so the workspace may hold anything when the call starts.
   mark_stage(0, s);
+  if (hidden_bf16) {
+    // bf16 hidden states: each token row is quantised once into the
+    // workspace, and the rest of the call reads that e4m3 copy (a row is
+    // copied once per local pick, 4.4 times per token in the prefill
+    // workload, so quantising inside the row copy repeats the work)
+    uint8_t* hq = ws + l.hidden_q;
+    float* hqs = reinterpret_cast<float*>(ws + l.hidden_qs);
+    quantize_hidden_kernel<<<static_cast<unsigned>(div_up(T, 8)), 256, 0, s>>>(
+        static_cast<const uint16_t*>(hidden_states), T, hq, hqs);
+    if (cudaGetLastError() != cudaSuccess) return MOE_B200_ERR_CUDA;
+    hidden_states = hq;
+    hidden_states_scale = hqs;
+  }
   mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
                     static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w,
@@ -625,6 +653,44 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
     return MOE_B200_ERR_CUDA;
   mark_stage(6, s);
   return MOE_B200_OK;
+}
+
+int moe_b200_run(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                 const void* hidden_states, const float* hidden_states_scale,
+                 const void* gemm1_weights, const float* gemm1_weights_scale,
+                 const void* gemm2_weights, const float* gemm2_weights_scale,
+                 int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
+                 void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  return run_layer(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale, false,
+                   gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                   routed_scaling_factor, num_tokens, output, workspace, workspace_bytes, stream);
+}
+
+int moe_b200_run_bf16_hidden(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                             const void* hidden_states, const void* gemm1_weights,
+                             const float* gemm1_weights_scale, const void* gemm2_weights,
+                             const float* gemm2_weights_scale, int64_t local_expert_offset,
+                             double routed_scaling_factor, int64_t num_tokens, void* output, void* workspace,
+                             size_t workspace_bytes, void* stream) {
+  return run_layer(routing_logits, routing_bias, routing_bias_dtype, hidden_states, nullptr, true, gemm1_weights,
+                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                   routed_scaling_factor, num_tokens, output, workspace, workspace_bytes, stream);
+}
+
+int moe_b200_quantize_hidden(const void* hidden_states, int64_t num_tokens, void* hidden_fp8, float* hidden_scale,
+                             void* stream) {
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (num_tokens == 0) return MOE_B200_OK;
+  if (!hidden_states || !hidden_fp8 || !hidden_scale) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!aligned(hidden_states, 16) || !aligned(hidden_fp8, 16) || !aligned(hidden_scale, 4))
+    return MOE_B200_ERR_MISALIGNED;
+  DeviceInfo di;
+  const int st = current_device_info(&di);
+  if (st != MOE_B200_OK) return st;
+  quantize_hidden_kernel<<<static_cast<unsigned>(div_up(num_tokens, 8)), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(hidden_states), static_cast<int>(num_tokens), static_cast<uint8_t*>(hidden_fp8),
+      hidden_scale);
+  return cudaGetLastError() == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -89,6 +89,7 @@ struct DecodeFrontParams {
   float* g1_acc;            // [cap, 4096] rows of valid (token, expert) pairs cleared
   const uint8_t* hidden;    // [T, 7168] e4m3
   const float* hidden_scale;  // [56, T]
+  const uint16_t* hidden_bf16;  // [T, 7168] bf16 when set: rows are quantised while copied (hidden unused)
   uint8_t* a_perm;          // [cap, 7168] valid rows copied from hidden
   float* sa_perm;           // [56, cap] their block scales
   int cap;
@@ -152,8 +153,12 @@ __global__ void permute_kernel(PermuteParams p);
 __global__ void permute_count_kernel(PermuteParams p);
 __global__ void permute_place_kernel(PermuteParams p);
 __global__ void gather_rows_kernel(GatherParams p);
+__global__ void quantize_hidden_kernel(const uint16_t* hidden_bf16, int num_tokens, uint8_t* hidden_fp8,
+                                       float* hidden_scale);
 __global__ void finalize_kernel(const float* y_acc, const int32_t* slot_tok, const int* n_touched, uint16_t* out,
                                 int num_tokens);
+// kBf16: dp.hidden_bf16 rows are quantised while copied; otherwise e4m3 rows copied.
+template <bool kBf16>
 __global__ void route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp);
 
 }  // namespace moe

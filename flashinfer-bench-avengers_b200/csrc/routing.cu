@@ -10,6 +10,7 @@
 #include <cuda_bf16.h>
 #include <cstdint>
 
+#include "hidden_quant.cuh"
 #include "moe_kernels.cuh"
 #include "moe_ptx.cuh"
 #include "moe_shapes.cuh"
@@ -409,6 +410,7 @@ __device__ __forceinline__ void st_cluster_u32(const void* local, uint32_t rank,
 // Routing runs on eight SMs rather than one: a warp issues about a thousand
 // instructions per token, which on a single SM would serialise 64 tokens.
 constexpr int kDecodeMaxRows = kDecodeMaxTokens * kTopK + kExpertsLocal * (kSegAlign - 1);
+template <bool kBf16>
 __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256)
     route_permute_decode_kernel(RouteParams rp, DecodeFrontParams dp) {
   __shared__ int s_idx[kDecodeMaxTokens * kTopK];   // every CTA holds all selections
@@ -442,7 +444,14 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
       // A token with a local pick has its row copied in step 3: start
       // pulling its 7 KB row and 56 block scales into L2 now.
       const int le = idx - dp.local_expert_offset;
-      if (__ballot_sync(0xffffffffu, lane < kTopK && le >= 0 && le < kExpertsLocal)) {
+      if constexpr (kBf16) {
+        if (__ballot_sync(0xffffffffu, lane < kTopK && le >= 0 && le < kExpertsLocal)) {
+          const uint8_t* row = reinterpret_cast<const uint8_t*>(dp.hidden_bf16 + static_cast<int64_t>(t) * kHidden);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if ((lane + 32 * k) * 128 < kHidden * 2) prefetch_l2(row + (lane + 32 * k) * 128);
+        }
+      } else if (__ballot_sync(0xffffffffu, lane < kTopK && le >= 0 && le < kExpertsLocal)) {
         const uint8_t* row = dp.hidden + static_cast<int64_t>(t) * kHidden;
         prefetch_l2(row + lane * 128);
         prefetch_l2(row + (lane + 32) * 128);
@@ -571,6 +580,15 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
       const int e = __popc(__ballot_sync(0xffffffffu, incl <= v));
       const int row = s_start[e] + v - s_cpre[e];
       const int tok = s_ptok[row];
+      if constexpr (kBf16) {
+        float4* g = reinterpret_cast<float4*>(dp.g1_acc + static_cast<int64_t>(row) * kGemm1Out);
+#pragma unroll 8
+        for (int i = lane; i < kGemm1Out / 4; i += 32) g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+        quantize_row_1x128(dp.hidden_bf16 + static_cast<int64_t>(tok) * kHidden,
+                           dp.a_perm + static_cast<int64_t>(row) * kHidden, lane,
+                           [&](int kb, float sc) { dp.sa_perm[static_cast<int64_t>(kb) * dp.cap + row] = sc; });
+        continue;
+      }
       // every load first, then the stores (the clears do not wait for them)
       const uint4* src = reinterpret_cast<const uint4*>(dp.hidden + static_cast<int64_t>(tok) * kHidden);
       uint4 rowv[kHidden / 16 / 32];
@@ -827,5 +845,8 @@ __global__ void __launch_bounds__(256) gather_rows_kernel(GatherParams p) {
       p.sa_perm[static_cast<int64_t>(kb) * p.cap + r] = p.hidden_scale[static_cast<int64_t>(kb) * p.num_tokens + tok];
   }
 }
+
+template __global__ void route_permute_decode_kernel<false>(RouteParams, DecodeFrontParams);
+template __global__ void route_permute_decode_kernel<true>(RouteParams, DecodeFrontParams);
 
 }  // namespace moe

@@ -67,6 +67,8 @@ class WorkspaceLayout(ctypes.Structure):
         ("tok_slot", ctypes.c_size_t),
         ("n_touched", ctypes.c_size_t),
         ("slot_tok", ctypes.c_size_t),
+        ("hidden_q", ctypes.c_size_t),
+        ("hidden_qs", ctypes.c_size_t),
     ]
 
 
@@ -86,6 +88,11 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_run.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64,
                                      ctypes.c_double, _I64, _P, _P, ctypes.c_size_t, _P]
         lib.moe_b200_run.restype = ctypes.c_int
+        lib.moe_b200_run_bf16_hidden.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _I64,
+                                                 ctypes.c_double, _I64, _P, _P, ctypes.c_size_t, _P]
+        lib.moe_b200_run_bf16_hidden.restype = ctypes.c_int
+        lib.moe_b200_quantize_hidden.argtypes = [_P, _I64, _P, _P, _P]
+        lib.moe_b200_quantize_hidden.restype = ctypes.c_int
         lib.moe_b200_route.argtypes = [_P, _P, ctypes.c_int, _I64, ctypes.c_double, _P, _P, _P]
         lib.moe_b200_route.restype = ctypes.c_int
         lib.moe_b200_read_status.argtypes = [_P, ctypes.POINTER(ctypes.c_uint32), _P]
@@ -151,6 +158,9 @@ def _check(cond: bool, msg: str) -> None:
 
 def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale) -> int:
+    """Checks the layer inputs; hidden_states_scale None means bf16 hidden
+    states (run_bf16_hidden) instead of e4m3 ones with their scales."""
+    bf16_hidden = hidden_states_scale is None
     tensors = {
         "routing_logits": routing_logits,
         "routing_bias": routing_bias,
@@ -161,6 +171,8 @@ def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_sca
         "gemm2_weights": gemm2_weights,
         "gemm2_weights_scale": gemm2_weights_scale,
     }
+    if bf16_hidden:
+        del tensors["hidden_states_scale"]
     for name, t in tensors.items():
         _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
         _check(t.is_cuda, f"{name} must be CUDA")
@@ -174,10 +186,13 @@ def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_sca
     _check(routing_logits.dtype == torch.float32, "routing_logits must be float32")
     _check(routing_bias.numel() == E_GLOBAL, f"routing_bias must have {E_GLOBAL} elements")
     _check(tuple(hidden_states.shape) == (T, H), f"hidden_states must be [T, {H}]")
-    _check(hidden_states.dtype == torch.float8_e4m3fn, "hidden_states must be float8_e4m3fn")
-    _check(tuple(hidden_states_scale.shape) == (HIDDEN_BLOCKS, T),
-           f"hidden_states_scale must be [{HIDDEN_BLOCKS}, T]")
-    _check(hidden_states_scale.dtype == torch.float32, "hidden_states_scale must be float32")
+    if bf16_hidden:
+        _check(hidden_states.dtype == torch.bfloat16, "hidden_states must be bfloat16")
+    else:
+        _check(hidden_states.dtype == torch.float8_e4m3fn, "hidden_states must be float8_e4m3fn")
+        _check(tuple(hidden_states_scale.shape) == (HIDDEN_BLOCKS, T),
+               f"hidden_states_scale must be [{HIDDEN_BLOCKS}, T]")
+        _check(hidden_states_scale.dtype == torch.float32, "hidden_states_scale must be float32")
     _check(tuple(gemm1_weights.shape) == (E_LOCAL, 2 * I, H), f"gemm1_weights must be [{E_LOCAL}, {2 * I}, {H}]")
     _check(gemm1_weights.dtype == torch.float8_e4m3fn, "gemm1_weights must be float8_e4m3fn")
     _check(tuple(gemm1_weights_scale.shape) == (E_LOCAL, GEMM1_OUT_BLOCKS, HIDDEN_BLOCKS),
@@ -235,6 +250,61 @@ def run_dps(routing_logits, routing_bias, hidden_states, hidden_states_scale, ge
             output.data_ptr() if output is not None else None, ws.data_ptr(), ws.numel(), stream)
     _raise_on(code, "moe_b200_run")
     return output
+
+
+def run_bf16_hidden(routing_logits, routing_bias, hidden_states, gemm1_weights, gemm1_weights_scale,
+                    gemm2_weights, gemm2_weights_scale, local_expert_offset, routed_scaling_factor,
+                    output: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The layer on bf16 hidden states [T, 7168]: each (token, expert) row is
+    quantised (quantize_hidden's convention) while it is copied into the
+    permuted buffers (moe_b200_run_bf16_hidden). Returns ``output`` (allocated
+    when None)."""
+    T = _check_inputs(routing_logits, routing_bias, hidden_states, None,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    dev = routing_logits.device
+    if output is None:
+        output = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    _check(isinstance(output, torch.Tensor) and output.device == dev and tuple(output.shape) == (T, H)
+           and output.dtype == torch.bfloat16 and output.is_contiguous(),
+           f"output must be a contiguous bf16 [T, {H}] tensor on the inputs' device")
+    if T == 0:
+        return output
+    lib = load_library()
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias)
+        s13 = gemm1_weights_scale.contiguous()
+        s2 = gemm2_weights_scale.contiguous()
+        ws = workspace if workspace is not None else get_workspace(T, dev)
+        code = lib.moe_b200_run_bf16_hidden(
+            logits.data_ptr(), bias.data_ptr(), bias_dtype, hidden_states.data_ptr(), gemm1_weights.data_ptr(),
+            s13.data_ptr(), gemm2_weights.data_ptr(), s2.data_ptr(), int(local_expert_offset),
+            float(routed_scaling_factor), T, output.data_ptr(), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_run_bf16_hidden")
+    return output
+
+
+def quantize_hidden(hidden_states: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """bf16 [T, 7168] -> (e4m3 [T, 7168], fp32 block scales [56, T]): per
+    128-column block scale = amax / 448 (1 for an all-zero block), value =
+    e4m3(x / scale) (moe_b200_quantize_hidden)."""
+    _check(isinstance(hidden_states, torch.Tensor) and hidden_states.is_cuda
+           and hidden_states.dtype == torch.bfloat16 and hidden_states.dim() == 2
+           and hidden_states.size(1) == H, f"hidden_states must be a CUDA bf16 [T, {H}] tensor")
+    T = hidden_states.size(0)
+    _check(T <= MAX_TOKENS, f"at most {MAX_TOKENS} tokens per call")
+    dev = hidden_states.device
+    q = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+    s = torch.empty((HIDDEN_BLOCKS, T), dtype=torch.float32, device=dev)
+    if T == 0:
+        return q, s
+    with torch.cuda.device(dev):
+        x = hidden_states.contiguous()
+        code = load_library().moe_b200_quantize_hidden(x.data_ptr(), T, q.data_ptr(), s.data_ptr(),
+                                                        torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_quantize_hidden")
+    return q, s
 
 
 def ep_area_bytes(num_tokens: int) -> int:

@@ -87,9 +87,13 @@ def make_routing_inputs(T: int, seed: int = 0, device="cpu", variant: str = "uni
     return {"routing_logits": logits.contiguous(), "routing_bias": bias.to(torch.bfloat16)}
 
 
+def make_hidden_bf16(T: int, seed: int = 0, device="cpu") -> torch.Tensor:
+    """The bf16 [T, 7168] hidden states that make_hidden quantises."""
+    return torch.randn(T, H, generator=_gen(seed, _PIECE_HIDDEN, device), device=device).to(torch.bfloat16)
+
+
 def make_hidden(T: int, seed: int = 0, device="cpu") -> tuple[torch.Tensor, torch.Tensor]:
-    x = torch.randn(T, H, generator=_gen(seed, _PIECE_HIDDEN, device), device=device).to(torch.bfloat16)
-    return quantize_rows_1x128(x)
+    return quantize_rows_1x128(make_hidden_bf16(T, seed, device))
 
 
 def make_expert_weights(seed: int, le: int, device="cpu"):

@@ -83,6 +83,37 @@ MOE_B200_API int moe_b200_run(const float* routing_logits, const void* routing_b
                  void* output, void* workspace, size_t workspace_bytes, void* stream);
 
 /*
+ * The upstream quantiser of this operator's hidden states: bf16 [T, 7168]
+ * -> e4m3 [T, 7168] and fp32 scales [56, T] (block-major, as moe_b200_run
+ * reads them). Per 128-column block of a token row: scale = amax / 448
+ * (1 for an all-zero block) and value = e4m3(x / scale), both divisions
+ * IEEE fp32, rounded to nearest even and saturating. This is the
+ * convention of the inputs the reference is benchmarked on; the reference
+ * itself takes them pre-quantised (solution/cuda/main.py:31-42), so it has
+ * no counterpart. Inputs must be finite. Alignment: hidden_states and
+ * hidden_fp8 16 bytes, hidden_scale 4.
+ */
+MOE_B200_API int moe_b200_quantize_hidden(const void* hidden_states, int64_t num_tokens, void* hidden_fp8,
+                                          float* hidden_scale, void* stream);
+
+/*
+ * moe_b200_run on bf16 hidden states [T, 7168] (no scale argument), with
+ * the quantiser above inside the call: for T <= 64 it runs inside the copy
+ * of each (token, expert) row into the permuted buffers (no e4m3 copy of
+ * the hidden states is written); above, each token row is quantised once
+ * into the workspace (hidden_q / hidden_qs of the layout) before routing.
+ * Same result as moe_b200_quantize_hidden followed by moe_b200_run, and the
+ * same workspace size. No reference counterpart (see above).
+ */
+MOE_B200_API int moe_b200_run_bf16_hidden(const float* routing_logits, const void* routing_bias,
+                                          int routing_bias_dtype, const void* hidden_states,
+                                          const void* gemm1_weights, const float* gemm1_weights_scale,
+                                          const void* gemm2_weights, const float* gemm2_weights_scale,
+                                          int64_t local_expert_offset, double routed_scaling_factor,
+                                          int64_t num_tokens, void* output, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
+/*
  * Routing only: DeepSeek-V3 no-aux top-8 selection and weights.
  * Replaces the reference launcher launch_noaux_routing_topk8
  * (solution/cuda/kernel.h:37-44, kernel.cu:2527-2537). Experts are listed
@@ -135,6 +166,8 @@ typedef struct moe_b200_workspace_layout {
   size_t tok_slot;    /* int32[T] combine row of each token, -1 without a local pick (not decode) */
   size_t n_touched;   /* int32 number of tokens with a local pick (not decode) */
   size_t slot_tok;    /* int32[T] token of each combine row, the first n_touched in use (not decode) */
+  size_t hidden_q;    /* e4m3[T, 7168] quantised bf16 hidden states (moe_b200_run_bf16_hidden, not decode) */
+  size_t hidden_qs;   /* fp32[56, T] their block scales (not decode) */
 } moe_b200_workspace_layout;
 
 MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout* out);
@@ -143,7 +176,9 @@ MOE_B200_API int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_work
  * Profiling hook. When `events` is non-null, later moe_b200_run calls made
  * by the calling thread record events[i] (cudaEvent_t values created on the
  * current device) on their stream at the stage boundaries:
- *   0 start, 1 after the scratch clears, 2 after routing, 3 after the
+ *   0 start, 1 after the quantiser of bf16 hidden states (only
+ *   moe_b200_run_bf16_hidden with more than 64 tokens runs one; otherwise
+ *   nothing runs between 0 and 1), 2 after routing, 3 after the
  *   permutation, 4 after GEMM1 (+SwiGLU), 5 after GEMM2, 6 after the final
  *   bf16 conversion.
  * num_events must be 7. Pass NULL to switch the hook off. No reference

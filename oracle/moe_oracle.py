@@ -19,6 +19,8 @@ solution for moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048:
 * GEMM2 + combine    W2 scale [e, h/128, i/128] (kernel.cu:1466 with
                      S_cols = 16 from main.cpp:130), out[t] += w * O
 * final cast         main.cpp:141 (fp32 -> bf16)
+* hidden quantiser   no reference code (the reference takes e4m3 inputs):
+                     the 1x128 amax/448 convention of its benchmark inputs
 
 Tie-breaking is made explicit: every top-k orders by value descending and,
 on equal values, by the smaller index (the reference kernel's __ffs / strict
@@ -105,6 +107,23 @@ def dequant_hidden(hidden_states: torch.Tensor, hidden_states_scale: torch.Tenso
     sc = hidden_states_scale.to("cpu", torch.float32).t()           # [T, 56]
     T = a.shape[0]
     return (a.view(T, H // BLOCK, BLOCK) * sc.unsqueeze(2)).view(T, H)
+
+
+def quantize_hidden(hidden_bf16: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """The upstream quantiser of the layer's hidden states, bf16 [T, 7168] ->
+    (e4m3 [T, 7168], fp32 scales [56, T] block-major). Per 128-column block:
+    scale = amax / 448 (1 for an all-zero block), value = e4m3(x / scale),
+    both divisions in fp32, rounded to nearest even. The reference takes its
+    inputs pre-quantised (solution/cuda/main.py:31-42); this is the
+    convention of the inputs it is benchmarked on (1x128 blocks, amax/448,
+    scales [56, T]), pinned by tests against the committed fixtures."""
+    x = hidden_bf16.detach().to("cpu").float()
+    T = x.shape[0]
+    xb = x.view(T, H // 128, 128)
+    amax = xb.abs().amax(dim=2)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    q = (xb / scale.unsqueeze(2)).to(torch.float8_e4m3fn).view(T, H)
+    return q, scale.t().contiguous()
 
 
 def dequant_block(w: torch.Tensor, scale: torch.Tensor) -> torch.Tensor:

@@ -68,9 +68,15 @@ def test_workspace_size_and_layout(lib):
         token_major = T >= moe_host.TOKEN_MAJOR_MIN_TOKENS
         if decode or token_major:
             offs += [lay.g1_acc]
-        offs += [lay.slot_tok]   # appended last, so the other offsets did not move
+        offs += [lay.slot_tok]   # appended after the others, so their offsets did not move
+        if not decode:
+            offs += [lay.hidden_q, lay.hidden_qs]
+            assert lay.hidden_qs - lay.hidden_q >= T * 7168 and n - lay.hidden_qs >= 56 * 4 * T
+            assert lay.hidden_q - lay.slot_tok >= 4 * T
+        else:
+            assert lay.hidden_q == 0 and lay.hidden_qs == 0
+            assert n - lay.slot_tok >= 4 * T
         assert offs == sorted(offs) and all(o % 256 == 0 for o in offs)
-        assert n - lay.slot_tok >= 4 * T
         assert lay.c_lo - lay.c_hi >= lay.cap_rows * 2048
         if decode:
             assert lay.g1_acc - lay.y_acc >= T * 7168 * 4
