@@ -70,7 +70,8 @@ LAYER_BYTES_PER_TOKEN = 22_752
 FLOP_PER_ASSIGNMENT_G1 = 2 * 7168 * 4096
 FLOP_PER_ASSIGNMENT_G2 = 2 * 2048 * 7168
 
-# Published reference latencies (Modal B200, reference kernel).
+# Published reference latencies: the reference kernel on a Modal B200, from
+# the summary of its scripts/run_modal.py in the reference's Trace_Summary.png.
 PUBLISHED_US = {1: 551.0, 7: 1034.0, 14: 1609.0, 15: 850.0, 16: 1727.0, 32: 2803.0, 80: 3620.0,
                 901: 4545.0, 11948: 11731.0, 14107: 15650.0}
 
