@@ -3,7 +3,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (the single-B200 decode path): one call of the
+Workload (config 1 of the benchmark, the single-B200 decode path): one call of the
 layer on T=64 tokens, 32 local experts, seeded synthetic inputs with the
 benchmark distributions (flashinfer-bench-avengers_b200/workloads.py). With
 N>1 GPUs (torchrun) every rank owns a different 32-expert shard of the
@@ -616,7 +616,10 @@ def main() -> None:
     # decode (T <= 64): front end, GEMM1, GEMM2, finalize; larger T: route,
     # permute (two kernels above 1024 tokens), gather, GEMM1, GEMM2, finalize,
     # and with bf16 hidden states the per-token quantiser first
-    launches_per_call = 4 if HEADLINE_T <= 64 else (6 if HEADLINE_T <= 1024 else 7) + (1 if BF16_HIDDEN else 0)
+    if HEADLINE_T <= 64:
+        launches_per_call = 4
+    else:
+        launches_per_call = (6 if HEADLINE_T <= 1024 else 7) + (1 if BF16_HIDDEN else 0)
     line = {
         "metric": METRIC,
         "value": round(mean_ms * 1e3, 2),
