@@ -210,7 +210,8 @@ int grid_for(int64_t T, int bn, int row_blocks, int splits, int sm_count) {
 }
 
 int launch_route(const float* logits, const void* bias, int bias_dtype, int T, float rsf,
-                 int local_off, int32_t* topk_idx, float* topk_w, uint16_t* out, cudaStream_t s) {
+                 int local_off, int32_t* topk_idx, float* topk_w, uint16_t* out, int method, int top_k,
+                 cudaStream_t s) {
   RouteParams rp;
   rp.logits = logits;
   rp.bias = bias;
@@ -221,6 +222,8 @@ int launch_route(const float* logits, const void* bias, int bias_dtype, int T, f
   rp.topk_idx = topk_idx;
   rp.topk_w = topk_w;
   rp.out = out;
+  rp.method = method;
+  rp.top_k = top_k;
   // The first kernel of a call is launched without the dependent-launch
   // attribute, so it starts only after all earlier work on the stream.
   route_kernel<<<static_cast<unsigned>(div_up(T, 8)), 256, 0, s>>>(rp);
@@ -251,8 +254,8 @@ void mark_stage(int i, cudaStream_t s) {
 //      loaded; W2 tiles stream meanwhile), then two W2 blocks per tile, K
 //      split 2 ways, red.add into y_acc
 //   -> finalize (bf16).
-int run_decode(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
-               const void* hidden_states, const float* hidden_states_scale, bool hidden_bf16,
+int run_decode(const float* routing_logits, const void* routing_bias, int routing_bias_dtype, int method,
+               int top_k, const void* hidden_states, const float* hidden_states_scale, bool hidden_bf16,
                const void* gemm1_weights,
                const float* gemm1_weights_scale, const void* gemm2_weights,
                const float* gemm2_weights_scale, int local_off, float rsf, int T, void* output,
@@ -299,6 +302,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   rp.topk_idx = reinterpret_cast<int32_t*>(ws + l.topk_idx);
   rp.topk_w = reinterpret_cast<float*>(ws + l.topk_w);
   rp.out = nullptr;
+  rp.method = method;
+  rp.top_k = top_k;
   DecodeFrontParams dp;
   dp.counts = counts;
   dp.seg_off = seg_off;
@@ -377,6 +382,20 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
 
 using namespace moe;
 
+// A routing method and top_k the routing kernels support: DeepSeek-V3 with
+// its 8 picks, Llama4 with 1, the others with 1 to 8.
+static bool valid_routing(int method, int top_k) {
+  switch (method) {
+    case MOE_B200_ROUTING_DEEPSEEK_V3: return top_k == kTopK;
+    case MOE_B200_ROUTING_LLAMA4: return top_k == 1;
+    case MOE_B200_ROUTING_DEFAULT:
+    case MOE_B200_ROUTING_RENORMALIZE:
+    case MOE_B200_ROUTING_RENORMALIZE_NAIVE:
+    case MOE_B200_ROUTING_TOPK: return top_k >= 1 && top_k <= kTopK;
+    default: return false;
+  }
+}
+
 extern "C" {
 
 int moe_b200_abi_version(void) { return 5; }
@@ -424,11 +443,21 @@ const char* moe_b200_status_string(int status) {
 int moe_b200_route(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
                    int64_t num_tokens, double routed_scaling_factor, int32_t* topk_idx,
                    float* topk_w, void* stream) {
+  return moe_b200_route_method(MOE_B200_ROUTING_DEEPSEEK_V3, kTopK, routing_logits, routing_bias,
+                               routing_bias_dtype, num_tokens, routed_scaling_factor, topk_idx, topk_w, stream);
+}
+
+int moe_b200_route_method(int routing_method, int top_k, const float* routing_logits, const void* routing_bias,
+                          int routing_bias_dtype, int64_t num_tokens, double routed_scaling_factor,
+                          int32_t* topk_idx, float* topk_w, void* stream) {
   if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
     return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!valid_routing(routing_method, top_k)) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
-  if (!routing_logits || !routing_bias || !topk_idx || !topk_w) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!routing_logits || (!routing_bias && routing_method == MOE_B200_ROUTING_DEEPSEEK_V3) || !topk_idx ||
+      !topk_w)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(topk_idx, 16) ||
       !aligned(topk_w, 16))
     return MOE_B200_ERR_MISALIGNED;
@@ -436,8 +465,8 @@ int moe_b200_route(const float* routing_logits, const void* routing_bias, int ro
   int st = current_device_info(&di);
   if (st != MOE_B200_OK) return st;
   return launch_route(routing_logits, routing_bias, routing_bias_dtype, static_cast<int>(num_tokens),
-                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w, nullptr,
-                      static_cast<cudaStream_t>(stream));
+                      static_cast<float>(routed_scaling_factor), 0, topk_idx, topk_w, nullptr, routing_method,
+                      top_k, static_cast<cudaStream_t>(stream));
 }
 
 int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream) {
@@ -457,6 +486,7 @@ int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream) 
 // on bf16 hidden states that the row copy into the permuted buffers
 // quantises (hidden_states_scale unused).
 static int run_layer(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
+                     int routing_method, int top_k,
                      const void* hidden_states, const float* hidden_states_scale, bool hidden_bf16,
                      const void* gemm1_weights, const float* gemm1_weights_scale,
                      const void* gemm2_weights, const float* gemm2_weights_scale,
@@ -466,8 +496,10 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
   if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
     return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!valid_routing(routing_method, top_k)) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
-  if (!routing_logits || !routing_bias || !hidden_states || (!hidden_bf16 && !hidden_states_scale) ||
+  if (!routing_logits || (!routing_bias && routing_method == MOE_B200_ROUTING_DEEPSEEK_V3) || !hidden_states ||
+      (!hidden_bf16 && !hidden_states_scale) ||
       !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !workspace)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (!aligned(routing_logits, 16) || !aligned(routing_bias, 16) || !aligned(hidden_states, 16) ||
@@ -510,8 +542,8 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
   int32_t* slot_tok = reinterpret_cast<int32_t*>(ws + l.slot_tok);
 
   if (plan.decode)
-    return run_decode(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale,
-                      hidden_bf16, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
+    return run_decode(routing_logits, routing_bias, routing_bias_dtype, routing_method, top_k, hidden_states,
+                      hidden_states_scale, hidden_bf16, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
                       static_cast<float>(routed_scaling_factor), T, output, ws, l, di, s);
 
   // ---- tensor maps ---------------------------------------------------------
@@ -548,7 +580,7 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
   mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
                     static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w,
-                    static_cast<uint16_t*>(output), s);
+                    static_cast<uint16_t*>(output), routing_method, top_k, s);
   if (st != MOE_B200_OK) return st;
   mark_stage(2, s);
 
@@ -661,9 +693,22 @@ int moe_b200_run(const float* routing_logits, const void* routing_bias, int rout
                  const void* gemm2_weights, const float* gemm2_weights_scale,
                  int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
                  void* output, void* workspace, size_t workspace_bytes, void* stream) {
-  return run_layer(routing_logits, routing_bias, routing_bias_dtype, hidden_states, hidden_states_scale, false,
-                   gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
-                   routed_scaling_factor, num_tokens, output, workspace, workspace_bytes, stream);
+  return run_layer(routing_logits, routing_bias, routing_bias_dtype, MOE_B200_ROUTING_DEEPSEEK_V3, kTopK,
+                   hidden_states, hidden_states_scale, false, gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                   gemm2_weights_scale, local_expert_offset, routed_scaling_factor, num_tokens, output, workspace,
+                   workspace_bytes, stream);
+}
+
+int moe_b200_run_routing(int routing_method, int top_k, const float* routing_logits, const void* routing_bias,
+                         int routing_bias_dtype, const void* hidden_states, const float* hidden_states_scale,
+                         const void* gemm1_weights, const float* gemm1_weights_scale, const void* gemm2_weights,
+                         const float* gemm2_weights_scale, int64_t local_expert_offset,
+                         double routed_scaling_factor, int64_t num_tokens, void* output, void* workspace,
+                         size_t workspace_bytes, void* stream) {
+  return run_layer(routing_logits, routing_bias, routing_bias_dtype, routing_method, top_k, hidden_states,
+                   hidden_states_scale, false, gemm1_weights, gemm1_weights_scale, gemm2_weights,
+                   gemm2_weights_scale, local_expert_offset, routed_scaling_factor, num_tokens, output, workspace,
+                   workspace_bytes, stream);
 }
 
 int moe_b200_run_bf16_hidden(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,
@@ -672,7 +717,8 @@ int moe_b200_run_bf16_hidden(const float* routing_logits, const void* routing_bi
                              const float* gemm2_weights_scale, int64_t local_expert_offset,
                              double routed_scaling_factor, int64_t num_tokens, void* output, void* workspace,
                              size_t workspace_bytes, void* stream) {
-  return run_layer(routing_logits, routing_bias, routing_bias_dtype, hidden_states, nullptr, true, gemm1_weights,
+  return run_layer(routing_logits, routing_bias, routing_bias_dtype, MOE_B200_ROUTING_DEEPSEEK_V3, kTopK,
+                   hidden_states, nullptr, true, gemm1_weights,
                    gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
                    routed_scaling_factor, num_tokens, output, workspace, workspace_bytes, stream);
 }

@@ -9,9 +9,22 @@
 
 namespace moe {
 
+// Routing methods, in the numbering of flashinfer's RoutingMethodType; this
+// operator's own is kRouteDeepSeekV3 (route_token).
+enum RouteMethod : int {
+  kRouteDefault = 0,            // softmax -> top-k
+  kRouteRenormalize = 1,        // top-k -> softmax over the picks
+  kRouteDeepSeekV3 = 2,         // sigmoid + bias, group-limited top-8 (this operator)
+  kRouteLlama4 = 3,             // top-1 -> sigmoid
+  kRouteRenormalizeNaive = 4,   // softmax -> top-k -> renormalise
+  kRouteTopK = 5,               // top-k, uniform weights
+};
+// Expert id of the unused selection slots (k >= top_k): never a local expert.
+constexpr int kNoExpert = -(1 << 30);
+
 struct RouteParams {
   const float* logits;      // [T, 256] fp32
-  const void* bias;         // [256] bf16 or fp32
+  const void* bias;         // [256] bf16 or fp32 (may be null for methods other than DeepSeek-V3)
   int bias_is_fp32;
   int num_tokens;           // T
   float routed_scaling_factor;
@@ -19,6 +32,8 @@ struct RouteParams {
   int32_t* topk_idx;        // [T, 8] global expert ids, best first
   float* topk_w;            // [T, 8]
   uint16_t* out;            // [T, 7168] bf16 output: rows of tokens with no local pick are zeroed (or null)
+  int method;               // RouteMethod
+  int top_k;                // selections per token, 1..8 (8 for DeepSeek-V3, 1 for Llama4)
 };
 
 struct PermuteParams {

@@ -167,6 +167,149 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
   }
 }
 
+// The other routing methods of this operator family, restated from the
+// published reference functions of flashinfer's MoE trace templates
+// (flashinfer/trace/templates/moe.py: default 187-225, renormalize 227-266,
+// llama4 268-307, renormalize_naive 309-349, topk 351-390). With
+// l = logit + bias (no bias: l = logit):
+//   Default           top-k of softmax(l)   w = softmax(l)[e]
+//   Renormalize       top-k of l            w = softmax of l over the picks
+//   Llama4            top-1 of l            w = sigmoid(l[e])
+//   RenormalizeNaive  top-k of softmax(l)   w = softmax(l)[e] / (sum over picks + 1e-20)
+//   TopK              top-k of l            w = 1 / k
+// each weight times routed_scaling_factor (TopK: routed_scaling_factor / k).
+// Softmax is monotonic, so every method selects by l, in the total order of
+// all routing here (larger first, smaller expert id on equal values; -0.0
+// counts as 0.0). Lane l owns experts 8l .. 8l+7 as in route_token; lanes
+// 0..7 return and store selection k, with kNoExpert and weight 0 in the
+// slots k >= top_k.
+__device__ __forceinline__ void route_token_simple(const RouteParams& p, int t, int lane, int& out_idx,
+                                                   float& out_w) {
+  const float4* lrow = reinterpret_cast<const float4*>(p.logits + static_cast<int64_t>(t) * kExpertsGlobal);
+  const float4 l0 = lrow[2 * lane];
+  const float4 l1 = lrow[2 * lane + 1];
+  float l[8] = {l0.x, l0.y, l0.z, l0.w, l1.x, l1.y, l1.z, l1.w};
+  if (p.bias != nullptr) {
+    if (p.bias_is_fp32) {
+      const float4* brow = reinterpret_cast<const float4*>(p.bias);
+      const float4 b0 = brow[2 * lane];
+      const float4 b1 = brow[2 * lane + 1];
+      const float b[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) l[j] += b[j];
+    } else {
+      const uint4 raw = reinterpret_cast<const uint4*>(p.bias)[lane];
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        l[2 * j] += __uint_as_float(w[j] << 16);
+        l[2 * j + 1] += __uint_as_float(w[j] & 0xFFFF0000u);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) l[j] += 0.0f;   // -0.0 -> +0.0: equal values, one key
+
+  // ---- top-k: per round the lane's best untaken expert, then the warp's --
+  const int K = p.top_k;
+  uint32_t taken = 0;
+  int sel_idx[kTopK];
+  float sel_l[kTopK];
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    sel_idx[k] = kNoExpert;
+    sel_l[k] = 0.f;
+    if (k < K) {
+      uint32_t bk = 0;
+      int bj = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t key = ((taken >> j) & 1u) ? 0u : order_key(l[j]);
+        if (key > bk) {
+          bk = key;
+          bj = j;
+        }
+      }
+      const uint32_t wk = __reduce_max_sync(0xffffffffu, bk);
+      const int wl = __ffs(__ballot_sync(0xffffffffu, bk == wk)) - 1;
+      const int wj = __shfl_sync(0xffffffffu, bj, wl);
+      float lv = l[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) lv = (j == bj) ? l[j] : lv;
+      sel_l[k] = __shfl_sync(0xffffffffu, lv, wl);
+      sel_idx[k] = 8 * wl + wj;
+      if (lane == wl) taken |= 1u << wj;
+    }
+  }
+
+  // ---- weights --------------------------------------------------------------
+  float wsel[kTopK];
+  const int m = p.method;
+  if (m == kRouteDefault || m == kRouteRenormalizeNaive) {
+    float mx = l[0];
+#pragma unroll
+    for (int j = 1; j < 8; ++j) mx = fmaxf(mx, l[j]);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float z = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) z += expf(l[j] - mx);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) z += __shfl_xor_sync(0xffffffffu, z, off);
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      wsel[k] = k < K ? expf(sel_l[k] - mx) / z : 0.f;
+      sum += wsel[k];
+    }
+    if (m == kRouteRenormalizeNaive) {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) wsel[k] = wsel[k] / (sum + 1e-20f);
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wsel[k] *= p.routed_scaling_factor;
+  } else if (m == kRouteRenormalize) {
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) {
+      wsel[k] = k < K ? expf(sel_l[k] - sel_l[0]) : 0.f;
+      sum += wsel[k];
+    }
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wsel[k] = wsel[k] / sum * p.routed_scaling_factor;
+  } else if (m == kRouteLlama4) {
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k)
+      wsel[k] = k == 0 ? 1.0f / (1.0f + expf(-sel_l[0])) * p.routed_scaling_factor : 0.f;
+  } else {   // kRouteTopK
+#pragma unroll
+    for (int k = 0; k < kTopK; ++k) wsel[k] = k < K ? p.routed_scaling_factor / static_cast<float>(K) : 0.f;
+  }
+
+  int my_idx = kNoExpert;
+  float my_w = 0.f;
+#pragma unroll
+  for (int k = 0; k < kTopK; ++k) {
+    if (lane == k) {
+      my_idx = sel_idx[k];
+      my_w = wsel[k];
+    }
+  }
+  out_idx = my_idx;
+  out_w = my_w;
+  if (lane < kTopK) {
+    p.topk_idx[t * kTopK + lane] = my_idx;
+    p.topk_w[t * kTopK + lane] = my_w;
+  }
+}
+
+__device__ __forceinline__ void route_token_any(const RouteParams& p, int t, int lane, int& out_idx, float& out_w) {
+  if (p.method == kRouteDeepSeekV3)
+    route_token(p, t, lane, out_idx, out_w);
+  else
+    route_token_simple(p, t, lane, out_idx, out_w);
+}
+
 // One warp per token, 8 tokens per CTA.
 __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   pdl_launch_next();
@@ -175,7 +318,7 @@ __global__ void __launch_bounds__(256) route_kernel(RouteParams p) {
   int idx;
   float w;
   if (t >= p.num_tokens) return;
-  route_token(p, t, lane, idx, w);
+  route_token_any(p, t, lane, idx, w);
   // A token with no pick among the local experts gets no combine row, so its
   // output row is zero: written here, where the stores overlap the routing
   // arithmetic of the other warps, and skipped by finalize_kernel.
@@ -433,7 +576,7 @@ __global__ void __cluster_dims__(kDecodeClusterCtas, 1, 1) __launch_bounds__(256
     if (t < T) {
       int idx;
       float w;
-      route_token(rp, t, lane, idx, w);
+      route_token_any(rp, t, lane, idx, w);
       if (lane < kTopK) {
 #pragma unroll
         for (uint32_t q = 0; q < kDecodeClusterCtas; ++q) {

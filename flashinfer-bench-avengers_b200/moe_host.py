@@ -93,6 +93,12 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_run_bf16_hidden.restype = ctypes.c_int
         lib.moe_b200_quantize_hidden.argtypes = [_P, _I64, _P, _P, _P]
         lib.moe_b200_quantize_hidden.restype = ctypes.c_int
+        lib.moe_b200_run_routing.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, _P, _P, _P, _P, _P,
+                                             _P, _I64, ctypes.c_double, _I64, _P, _P, ctypes.c_size_t, _P]
+        lib.moe_b200_run_routing.restype = ctypes.c_int
+        lib.moe_b200_route_method.argtypes = [ctypes.c_int, ctypes.c_int, _P, _P, ctypes.c_int, _I64,
+                                              ctypes.c_double, _P, _P, _P]
+        lib.moe_b200_route_method.restype = ctypes.c_int
         lib.moe_b200_route.argtypes = [_P, _P, ctypes.c_int, _I64, ctypes.c_double, _P, _P, _P]
         lib.moe_b200_route.restype = ctypes.c_int
         lib.moe_b200_read_status.argtypes = [_P, ctypes.POINTER(ctypes.c_uint32), _P]
@@ -173,6 +179,8 @@ def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_sca
     }
     if bf16_hidden:
         del tensors["hidden_states_scale"]
+    if routing_bias is None:   # other routing methods may run without a bias
+        del tensors["routing_bias"]
     for name, t in tensors.items():
         _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
         _check(t.is_cuda, f"{name} must be CUDA")
@@ -184,7 +192,7 @@ def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_sca
     T = routing_logits.size(0)
     _check(T <= MAX_TOKENS, f"at most {MAX_TOKENS} tokens per call")
     _check(routing_logits.dtype == torch.float32, "routing_logits must be float32")
-    _check(routing_bias.numel() == E_GLOBAL, f"routing_bias must have {E_GLOBAL} elements")
+    _check(routing_bias is None or routing_bias.numel() == E_GLOBAL, f"routing_bias must have {E_GLOBAL} elements")
     _check(tuple(hidden_states.shape) == (T, H), f"hidden_states must be [T, {H}]")
     if bf16_hidden:
         _check(hidden_states.dtype == torch.bfloat16, "hidden_states must be bfloat16")
@@ -208,7 +216,9 @@ def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_sca
     return T
 
 
-def _bias_arg(routing_bias: torch.Tensor) -> tuple[torch.Tensor, int]:
+def _bias_arg(routing_bias: torch.Tensor | None) -> tuple[torch.Tensor | None, int]:
+    if routing_bias is None:
+        return None, BIAS_BF16
     b = routing_bias.reshape(-1)
     if b.dtype == torch.bfloat16:
         return b.contiguous(), BIAS_BF16
@@ -283,6 +293,70 @@ def run_bf16_hidden(routing_logits, routing_bias, hidden_states, gemm1_weights, 
             torch.cuda.current_stream(dev).cuda_stream)
     _raise_on(code, "moe_b200_run_bf16_hidden")
     return output
+
+
+# Routing methods, numbered as flashinfer's RoutingMethodType (moe_b200.h).
+ROUTING_DEFAULT, ROUTING_RENORMALIZE, ROUTING_DEEPSEEK_V3 = 0, 1, 2
+ROUTING_LLAMA4, ROUTING_RENORMALIZE_NAIVE, ROUTING_TOPK = 3, 4, 5
+
+
+def run_routing(routing_method: int, top_k: int, routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                routed_scaling_factor, output: torch.Tensor | None = None,
+                workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The layer with another routing method of the family ahead of the same
+    permutation and GEMMs (moe_b200_run_routing); routing_bias may be None
+    except for ROUTING_DEEPSEEK_V3. Returns ``output`` (allocated when None)."""
+    T = _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    dev = routing_logits.device
+    if output is None:
+        output = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    _check(isinstance(output, torch.Tensor) and output.device == dev and tuple(output.shape) == (T, H)
+           and output.dtype == torch.bfloat16 and output.is_contiguous(),
+           f"output must be a contiguous bf16 [T, {H}] tensor on the inputs' device")
+    if T == 0:
+        return output
+    lib = load_library()
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias)
+        hs_scale = hidden_states_scale.contiguous()
+        s13 = gemm1_weights_scale.contiguous()
+        s2 = gemm2_weights_scale.contiguous()
+        ws = workspace if workspace is not None else get_workspace(T, dev)
+        code = lib.moe_b200_run_routing(
+            int(routing_method), int(top_k), logits.data_ptr(), bias.data_ptr() if bias is not None else None,
+            bias_dtype, hidden_states.data_ptr(), hs_scale.data_ptr(), gemm1_weights.data_ptr(), s13.data_ptr(),
+            gemm2_weights.data_ptr(), s2.data_ptr(), int(local_expert_offset), float(routed_scaling_factor), T,
+            output.data_ptr(), ws.data_ptr(), ws.numel(), torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_run_routing")
+    return output
+
+
+def route_method(routing_method: int, top_k: int, routing_logits, routing_bias,
+                 routed_scaling_factor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Routing only, any method of the family: (topk_idx int32 [T, 8] best
+    first, -(1 << 30) after top_k; topk_w fp32 [T, 8], 0 after top_k)."""
+    _check(routing_logits.is_cuda and routing_logits.dtype == torch.float32
+           and routing_logits.dim() == 2 and routing_logits.size(1) == E_GLOBAL,
+           f"routing_logits must be a CUDA float32 [T, {E_GLOBAL}] tensor")
+    T = routing_logits.size(0)
+    dev = routing_logits.device
+    idx = torch.empty((T, TOP_K), dtype=torch.int32, device=dev)
+    w = torch.empty((T, TOP_K), dtype=torch.float32, device=dev)
+    if T == 0:
+        return idx, w
+    lib = load_library()
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias.to(dev) if routing_bias is not None else None)
+        code = lib.moe_b200_route_method(int(routing_method), int(top_k), logits.data_ptr(),
+                                         bias.data_ptr() if bias is not None else None, bias_dtype, T,
+                                         float(routed_scaling_factor), idx.data_ptr(), w.data_ptr(),
+                                         torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_route_method")
+    return idx, w
 
 
 def quantize_hidden(hidden_states: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:

@@ -114,6 +114,52 @@ MOE_B200_API int moe_b200_run_bf16_hidden(const float* routing_logits, const voi
                                           size_t workspace_bytes, void* stream);
 
 /*
+ * Routing methods of this operator family, numbered as flashinfer's
+ * RoutingMethodType. With l = logit + bias (bias optional except for
+ * DeepSeek-V3) and k = top_k:
+ *   DEFAULT            top-k of softmax(l), weight softmax(l)[e]
+ *   RENORMALIZE        top-k of l, weights softmax of l over the k picks
+ *   DEEPSEEK_V3        this operator's routing (moe_b200_run), k = 8
+ *   LLAMA4             top-1 of l, weight sigmoid(l[e]); k = 1
+ *   RENORMALIZE_NAIVE  top-k of softmax(l), weights renormalised over the picks
+ *   TOPK               top-k of l, weights 1/k
+ * every weight times routed_scaling_factor; ties go to the lower expert id.
+ */
+#define MOE_B200_ROUTING_DEFAULT 0
+#define MOE_B200_ROUTING_RENORMALIZE 1
+#define MOE_B200_ROUTING_DEEPSEEK_V3 2
+#define MOE_B200_ROUTING_LLAMA4 3
+#define MOE_B200_ROUTING_RENORMALIZE_NAIVE 4
+#define MOE_B200_ROUTING_TOPK 5
+
+/*
+ * moe_b200_run with another routing method ahead of the same permutation,
+ * GEMMs and combine (top_k 1..8; 8 for DEEPSEEK_V3, 1 for LLAMA4;
+ * routing_bias may be NULL except for DEEPSEEK_V3). These are the sibling
+ * definitions of the operator in flashinfer's MoE trace templates
+ * (flashinfer/trace/templates/moe.py:187-390); the reference implements
+ * only DeepSeek-V3 routing, so they have no reference counterpart.
+ */
+MOE_B200_API int moe_b200_run_routing(int routing_method, int top_k, const float* routing_logits,
+                                      const void* routing_bias, int routing_bias_dtype,
+                                      const void* hidden_states, const float* hidden_states_scale,
+                                      const void* gemm1_weights, const float* gemm1_weights_scale,
+                                      const void* gemm2_weights, const float* gemm2_weights_scale,
+                                      int64_t local_expert_offset, double routed_scaling_factor,
+                                      int64_t num_tokens, void* output, void* workspace,
+                                      size_t workspace_bytes, void* stream);
+
+/*
+ * Routing only, any method above: topk_idx [T, 8] int32 global expert ids
+ * best first, topk_w [T, 8] fp32; slots k >= top_k hold expert id
+ * -(1 << 30) and weight 0.
+ */
+MOE_B200_API int moe_b200_route_method(int routing_method, int top_k, const float* routing_logits,
+                                       const void* routing_bias, int routing_bias_dtype, int64_t num_tokens,
+                                       double routed_scaling_factor, int32_t* topk_idx, float* topk_w,
+                                       void* stream);
+
+/*
  * Routing only: DeepSeek-V3 no-aux top-8 selection and weights.
  * Replaces the reference launcher launch_noaux_routing_topk8
  * (solution/cuda/kernel.h:37-44, kernel.cu:2527-2537). Experts are listed

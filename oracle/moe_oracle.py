@@ -81,6 +81,63 @@ def route(routing_logits: torch.Tensor, routing_bias: torch.Tensor, routed_scali
     return topk_idx, topk_w.to(torch.float32)
 
 
+# Routing methods, numbered as flashinfer's RoutingMethodType.
+ROUTING_DEFAULT, ROUTING_RENORMALIZE, ROUTING_DEEPSEEK_V3 = 0, 1, 2
+ROUTING_LLAMA4, ROUTING_RENORMALIZE_NAIVE, ROUTING_TOPK = 3, 4, 5
+NO_EXPERT = -(1 << 30)   # expert id of the unused selection slots
+
+
+@torch.no_grad()
+def route_method(routing_logits: torch.Tensor, routing_bias, routed_scaling_factor: float, method: int,
+                 top_k: int):
+    """The routing methods of the operator family other than DeepSeek-V3,
+    restated from the reference functions of the installed flashinfer
+    package (flashinfer/trace/templates/moe.py: default 187-225,
+    renormalize 227-266, llama4 268-307, renormalize_naive 309-349, topk
+    351-390). l = logit + bias (bias may be None). Every method selects the
+    top_k largest l (softmax is monotonic; equal values: smaller expert id
+    first, -0.0 equal to 0.0); weights:
+      Default           softmax(l)[e]
+      Renormalize       softmax of l over the picks
+      Llama4            1 / (1 + exp(-l[e]))            (top_k = 1)
+      RenormalizeNaive  softmax(l)[e] / (sum over the picks + 1e-20)
+      TopK              routed_scaling_factor / top_k   (no further scaling)
+    times routed_scaling_factor. DeepSeek-V3 is route().
+
+    Returns (topk_idx int64 [T, 8] best first, NO_EXPERT after top_k;
+    topk_w fp32 [T, 8], 0 after top_k).
+    """
+    if method == ROUTING_DEEPSEEK_V3:
+        return route(routing_logits, routing_bias, routed_scaling_factor)
+    l = routing_logits.detach().to("cpu", torch.float32)
+    if routing_bias is not None:
+        l = l + routing_bias.detach().to("cpu").to(torch.float32).reshape(-1)
+    l = l + 0.0
+    T = l.shape[0]
+    k = int(top_k)
+    sel = _sort_desc_stable(l, 1)[:, :k]
+    sl = l.gather(1, sel)
+    rsf = float(routed_scaling_factor)
+    if method in (ROUTING_DEFAULT, ROUTING_RENORMALIZE_NAIVE):
+        w = torch.softmax(l, dim=1).gather(1, sel)
+        if method == ROUTING_RENORMALIZE_NAIVE:
+            w = w / (w.sum(dim=1, keepdim=True) + 1e-20)
+        w = w * rsf
+    elif method == ROUTING_RENORMALIZE:
+        w = torch.softmax(sl, dim=1) * rsf
+    elif method == ROUTING_LLAMA4:
+        w = (1.0 / (1.0 + torch.exp(-sl))) * rsf
+    elif method == ROUTING_TOPK:
+        w = torch.full_like(sl, rsf / k)
+    else:
+        raise ValueError(f"unknown routing method {method}")
+    idx = torch.full((T, TOP_K), NO_EXPERT, dtype=torch.int64)
+    wt = torch.zeros(T, TOP_K, dtype=torch.float32)
+    idx[:, :k] = sel
+    wt[:, :k] = w.to(torch.float32)
+    return idx, wt
+
+
 @torch.no_grad()
 def permute(topk_idx: torch.Tensor, topk_w: torch.Tensor, local_expert_offset: int):
     """Per-local-expert segments of (token, weight), tokens ascending.
@@ -146,15 +203,17 @@ def expert_forward(a_rows: torch.Tensor, w13_e, s13_e, w2_e, s2_e, return_c: boo
 @torch.no_grad()
 def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
-                routed_scaling_factor, token_subset=None, experts=None, return_fp32=False):
+                routed_scaling_factor, token_subset=None, experts=None, return_fp32=False,
+                routing_method=ROUTING_DEEPSEEK_V3, top_k=TOP_K):
     """Full layer on the CPU. Returns bf16 [T, 7168] (or fp32 with return_fp32).
 
     token_subset: optional 1-D index tensor; only those rows are computed
     (each output row depends only on its own token), rows in subset order.
     experts: optional iterable of local expert ids to include (the others
     are skipped), used for bounded CPU-baseline samples.
+    routing_method / top_k: another routing method of the family (route_method).
     """
-    topk_idx, topk_w = route(routing_logits, routing_bias, routed_scaling_factor)
+    topk_idx, topk_w = route_method(routing_logits, routing_bias, routed_scaling_factor, routing_method, top_k)
     hs, hs_scale = hidden_states, hidden_states_scale
     if token_subset is not None:
         sub = torch.as_tensor(token_subset, dtype=torch.int64)
@@ -177,9 +236,10 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     return out if return_fp32 else out.to(torch.bfloat16)
 
 
-def active_local_experts(routing_logits, routing_bias, routed_scaling_factor, local_expert_offset):
+def active_local_experts(routing_logits, routing_bias, routed_scaling_factor, local_expert_offset,
+                         routing_method=ROUTING_DEEPSEEK_V3, top_k=TOP_K):
     """Sorted local expert ids selected by at least one token."""
-    idx, _ = route(routing_logits, routing_bias, routed_scaling_factor)
+    idx, _ = route_method(routing_logits, routing_bias, routed_scaling_factor, routing_method, top_k)
     le = idx - int(local_expert_offset)
     le = le[(le >= 0) & (le < E_LOCAL)]
     return sorted(set(le.tolist()))

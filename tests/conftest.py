@@ -43,6 +43,10 @@ def load_golden(path: str) -> dict:
         "variant": str(d["variant"]),
         "local_expert_offset": int(d["local_expert_offset"]),
         "routed_scaling_factor": float(d["routed_scaling_factor"]),
+        # routing method (flashinfer's RoutingMethodType numbering) and top_k;
+        # fixtures without them use this operator's DeepSeek-V3 routing
+        "routing_method": int(d["routing_method"]) if "routing_method" in d else 2,
+        "top_k": int(d["top_k"]) if "top_k" in d else 8,
         "output": torch.from_numpy(d["output_bf16_bits"]).view(torch.bfloat16),
         "digests": dict(zip([str(k) for k in d["digest_keys"]], [str(v) for v in d["digest_values"]])),
     }
@@ -64,7 +68,8 @@ def golden_inputs(g: dict, device="cpu"):
 
     r = workloads.make_routing_inputs(g["T"], g["seed"], "cpu", g["variant"], g["local_expert_offset"])
     active = moe_oracle.active_local_experts(r["routing_logits"], r["routing_bias"],
-                                             g["routed_scaling_factor"], g["local_expert_offset"])
+                                             g["routed_scaling_factor"], g["local_expert_offset"],
+                                             g["routing_method"], g["top_k"])
     inp = workloads.make_inputs(g["T"], g["seed"], "cpu", g["variant"], g["local_expert_offset"],
                                 g["routed_scaling_factor"], experts=active)
     dig = g["digests"]

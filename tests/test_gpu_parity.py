@@ -208,7 +208,10 @@ def test_zero_tokens(host):
 def test_golden_on_gpu(host, path):
     g = load_golden(path)
     inp, _ = golden_inputs(g, device="cuda")
-    out = host.run(*workloads.as_args(inp))
+    if g["routing_method"] == 2:
+        out = host.run(*workloads.as_args(inp))
+    else:
+        out = host.run_routing(g["routing_method"], g["top_k"], *workloads.as_args(inp))
     torch.cuda.synchronize()
     _check_output(out, g["output"], g["name"])
 

@@ -15,7 +15,7 @@ import workloads
 def test_oracle_matches_golden(path):
     g = load_golden(path)
     inp, active = golden_inputs(g)
-    out = moe_oracle.moe_forward(*workloads.as_args(inp))
+    out = moe_oracle.moe_forward(*workloads.as_args(inp), routing_method=g["routing_method"], top_k=g["top_k"])
     ref = g["output"]
     assert out.shape == ref.shape == (g["T"], workloads.H)
     # Same fp32 math in a different operation order: the bf16 results agree
@@ -30,9 +30,14 @@ def test_oracle_matches_golden(path):
 
 
 def test_golden_cases_cover_offsets_and_variants():
-    cases = [load_golden(p) for p in golden_files()]
+    cases = [load_golden(p) for p in golden_files() if load_golden(p)["routing_method"] == 2]
     assert len(cases) >= 5
     assert {c["variant"] for c in cases} >= {"uniform", "hot", "zipf"}
     assert {c["local_expert_offset"] for c in cases} >= {0, 32, 224}
     assert any(c["T"] == 1 for c in cases)
     assert any(c["T"] == 16 and c["seed"] == 0 for c in cases)
+
+
+def test_golden_cases_cover_routing_methods():
+    methods = {load_golden(p)["routing_method"] for p in golden_files()}
+    assert methods == {0, 1, 2, 3, 4, 5}

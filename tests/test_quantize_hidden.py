@@ -142,6 +142,8 @@ def test_golden_from_bf16_hidden(host, path):
     """The fixtures' outputs, reached from the bf16 hidden states their e4m3
     inputs were quantised from."""
     g = load_golden(path)
+    if g["routing_method"] != 2:
+        pytest.skip("the bf16-hidden entry point routes with DeepSeek-V3 only")
     inp, _ = golden_inputs(g, device="cuda")
     x = workloads.make_hidden_bf16(g["T"], g["seed"], "cpu").cuda()
     args = workloads.as_args(inp)
