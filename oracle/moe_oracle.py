@@ -21,6 +21,9 @@ solution for moe_fp8_block_scale_ds_routing_topk8_ng8_kg4_e32_h7168_i2048:
 * final cast         main.cpp:141 (fp32 -> bf16)
 * hidden quantiser   no reference code (the reference takes e4m3 inputs):
                      the 1x128 amax/448 convention of its benchmark inputs
+* other routing      the sibling routing methods of the operator family
+  methods            (route_method), restated from flashinfer's reference
+                     functions and pinned by tests/golden/routing_*.npz
 
 Tie-breaking is made explicit: every top-k orders by value descending and,
 on equal values, by the smaller index (the reference kernel's __ffs / strict
