@@ -208,7 +208,8 @@ __device__ __forceinline__ void route_token_simple(const RouteParams& p, int t, 
     }
   }
 #pragma unroll
-  for (int j = 0; j < 8; ++j) l[j] += 0.0f;   // -0.0 -> +0.0: equal values, one key
+  for (int j = 0; j < 8; ++j)   // -0.0 -> +0.0: equal values, one key
+    if (__float_as_uint(l[j]) == 0x80000000u) l[j] = 0.0f;
 
   // ---- top-k: per round the lane's best untaken expert, then the warp's --
   const int K = p.top_k;

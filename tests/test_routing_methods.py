@@ -51,6 +51,9 @@ def test_routing_method_ties_go_to_lower_index(host):
     logits = (torch.randint(-2, 3, (256, 256), generator=g).float() * 0.5)
     logits[0, 7] = -0.0
     logits[0, 9] = 0.0
+    logits[1] = -1.0            # -0.0 and +0.0 compete for the first slot: equal, so 100 first
+    logits[1, 100] = -0.0
+    logits[1, 200] = 0.0
     for method, top_k in METHODS:
         idx, _ = host.route_method(method, top_k, logits.cuda(), None, 1.0)
         ref_idx, _ = moe_oracle.route_method(logits, None, 1.0, method, top_k)
