@@ -297,7 +297,7 @@ MOE_B200_API size_t moe_b200_ep_area_bytes(int64_t num_tokens);
 MOE_B200_API int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
                                      int64_t num_tokens, void* output, void* stream);
 
-/* ABI version of this header (bumped on any signature change). */
+/* ABI version of this header (bumped on any signature or struct layout change). */
 MOE_B200_API int moe_b200_abi_version(void);
 
 #ifdef __cplusplus

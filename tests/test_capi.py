@@ -32,7 +32,9 @@ def test_header_declares_the_entry_points():
     names = declared_functions()
     for n in ("moe_b200_run", "moe_b200_route", "moe_b200_workspace_bytes", "moe_b200_read_status",
               "moe_b200_status_string", "moe_b200_get_workspace_layout", "moe_b200_set_stage_events",
-              "moe_b200_abi_version", "moe_b200_ep_area_bytes", "moe_b200_ep_combine"):
+              "moe_b200_abi_version", "moe_b200_ep_area_bytes", "moe_b200_ep_combine", "moe_b200_run_noalloc",
+              "moe_b200_quantize_hidden", "moe_b200_run_bf16_hidden", "moe_b200_run_routing",
+              "moe_b200_route_method"):
         assert n in names
 
 
@@ -128,4 +130,33 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 5
+    assert lib.moe_b200_abi_version() == 6
+
+
+def test_widened_entry_points_reject_bad_arguments_without_a_device(lib):
+    """The routing-method, quantiser and bf16-hidden entry points check their
+    arguments before any CUDA call."""
+    P = ctypes.c_void_p
+    buf = ctypes.create_string_buffer(4096 + 256)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    p = P(base)
+    big = 1 << 40
+    # unknown method, top_k outside 1..8, DeepSeek-V3 needs 8 picks, Llama4 one
+    for method, top_k in [(6, 8), (-1, 8), (2, 4), (3, 2), (1, 0), (1, 9)]:
+        assert lib.moe_b200_route_method(method, top_k, p, p, 0, 4, 1.0, p, p, None) == 1
+        assert lib.moe_b200_run_routing(method, top_k, p, p, 0, p, p, p, p, p, p, 0, 1.0, 4, p, p, big, None) == 1
+    assert lib.moe_b200_route_method(2, 8, p, None, 0, 4, 1.0, p, p, None) == 1    # DeepSeek-V3 needs its bias
+    assert lib.moe_b200_route_method(1, 8, p, None, 0, 0, 1.0, p, p, None) == 0    # T = 0, bias optional
+    assert lib.moe_b200_run_routing(1, 8, p, None, 0, p, p, p, p, p, p, 0, 1.0, 0, p, p, big, None) == 0
+    assert lib.moe_b200_run_routing(3, 1, p, None, 0, P(base + 1), p, p, p, p, p, 0, 1.0, 4, p, p, big,
+                                    None) == 2                                      # misaligned hidden_states
+    assert lib.moe_b200_run_routing(5, 4, p, None, 0, p, p, p, p, p, p, 0, 1.0, 4, p, p, 16, None) == 3
+    # the quantiser
+    assert lib.moe_b200_quantize_hidden(None, 4, None, None, None) == 1
+    assert lib.moe_b200_quantize_hidden(p, -1, p, p, None) == 1
+    assert lib.moe_b200_quantize_hidden(P(base + 8), 4, p, p, None) == 2
+    assert lib.moe_b200_quantize_hidden(p, 0, p, p, None) == 0
+    # the layer on bf16 hidden states takes no scale argument
+    assert lib.moe_b200_run_bf16_hidden(p, p, 0, None, p, p, p, p, 0, 2.5, 4, p, p, big, None) == 1
+    assert lib.moe_b200_run_bf16_hidden(p, p, 0, p, p, p, p, p, 0, 2.5, 4, p, p, 16, None) == 3
+    assert lib.moe_b200_run_bf16_hidden(p, p, 0, p, p, p, p, p, 0, 2.5, 0, p, p, 16, None) == 0
