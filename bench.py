@@ -3,14 +3,17 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 
-Workload (config 1 of the benchmark, the single-B200 decode path): one call of the
-layer on T=64 tokens, 32 local experts, seeded synthetic inputs with the
-benchmark distributions (flashinfer-bench-avengers_b200/workloads.py). With
-N>1 GPUs (torchrun) every rank owns a different 32-expert shard of the
-256 experts (local_expert_offset = 32*rank) over the same tokens; the
-library's NVLink combine (moe_b200_ep_combine, workspaces in symmetric
-memory) forms the summed bf16 output on every rank: expert parallelism with
-fixed work per GPU ("weak" scaling).
+Headline workload (config 1 of the benchmark, the single-B200 decode path):
+one call of the layer on T=64 tokens, 32 local experts, seeded synthetic
+inputs with the benchmark distributions
+(flashinfer-bench-avengers_b200/workloads.py). With N>1 GPUs (torchrun)
+every rank owns a different 32-expert shard of the 256 experts
+(local_expert_offset = 32*rank) over the same tokens; the library's NVLink
+combine (moe_b200_ep_combine_shards, buffers shared through CUDA IPC) forms
+the summed bf16 output on every rank: expert parallelism with fixed work
+per GPU ("weak" scaling). At N>1 the line carries `ep_check`: every rank's
+status word, and the fused output against the fp32 sum of independent
+runs of every rank's shard (operator tolerance), identical on all ranks.
 
 A step is one layer call. Timing: W untimed warm-up steps, then K steps
 bracketed by a barrier and device synchronisation; the reported time is the
@@ -19,12 +22,19 @@ experts' weights exceed twice the 126 MB L2 (705 MB at T=64) cannot find
 any weight byte in L2 from the previous call, so those calls run back to
 back ("inputs larger than L2"); smaller calls get a 256 MB write flush
 before each timed call. The headline line also reports the same call after
-a 256 MB write flush (`value_l2_write_flushed`): the write-back of the
-dirty flush lines then shares HBM with the weight stream.
+a 256 MB write flush (`value_l2_write_flushed`).
 
-At N=1 the line also carries the decode sweep T in {1,4,16,64} (config 1),
-the prefill point (config 2, T=4096 with 4 hot experts) and the stress
-point (config 4, T=16384 Zipf), each with its roofline figures.
+Extra points:
+* every N: `ep_t8192` (config 3: T=8192, all 256 experts as 8 shards of 32
+  spread over the N ranks, 8/N shards per rank, NVLink combine; fixed total
+  work, "strong" scaling) and `stress` (config 4: T=16384 with Zipf(1.2)
+  expert popularity, the same 8-shard layout; per-shard and per-rank times,
+  the per-rank maximum is the figure). Both carry their own ep_check.
+* N=1 only: the decode sweep T in {1,4,16,64} (config 1; T=1 uses the first
+  seed >= 1234 whose token picks a local expert, stated in the point), the
+  prefill point (config 2, T=4096 with 4 hot experts) and the CPU baselines
+  (the oracle over all active experts, median of 3 runs, for the headline
+  and for config 0).
 
 `--impl reference` times the reference algorithm on the host CPU (the
 reference solution has no CPU implementation, so its CPU restatement in
@@ -57,8 +67,10 @@ SEED = 1234
 WORKLOADS = {
     "decode": (64, "uniform", "config1 decode: one MoE layer call, T=64"),
     "prefill": (4096, "hot", "config2 prefill: one MoE layer call, T=4096, 4 hot local experts"),
-    "stress": (16384, "zipf", "config4 stress: one MoE layer call, T=16384, Zipf(1.2) expert popularity"),
 }
+NUM_SHARDS = 8
+REL_TOL = 1e-2
+MATCH_FRAC = 0.999
 
 # Algorithmic sizes (bytes, FLOPs) of the operator.
 W13_BYTES = 2 * 2048 * 7168 + 32 * 56 * 4          # per active expert, weights + scales
@@ -97,7 +109,7 @@ class ClockSampler:
     """SM clock and throttle reasons of this rank's GPU during the timed region.
 
     With NVML (nvidia-ml-py) samples are kept only while the sampler is armed,
-    which `time_layer` does around its timed loop (a few milliseconds): a
+    which `time_step` does around its timed loop (a few milliseconds): a
     background thread polls every 0.25 ms when it gets the interpreter, and
     the timing loop itself samples once all timed calls are queued, until
     the last one ends. Without NVML, nvidia-smi samples every 200 ms for the
@@ -262,6 +274,10 @@ def layer_bytes(st: dict) -> int:
     return st["E_act"] * LAYER_BYTES_PER_EXPERT + st["T"] * LAYER_BYTES_PER_TOKEN + 512
 
 
+def layer_flops(sum_tk: int) -> int:
+    return sum_tk * (FLOP_PER_ASSIGNMENT_G1 + FLOP_PER_ASSIGNMENT_G2)
+
+
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -281,11 +297,19 @@ def token_keys() -> tuple:
                                                                      "hidden_states_scale")
 
 
-def layer_call(inp: dict, combiner=None):
-    """One call of the layer on inp's tokens into `out`: the library entry
-    point at N=1, this rank's shard plus the NVLink combine at N>1."""
+def shard_list(inps: list) -> list:
+    return [(i["gemm1_weights"], i["gemm1_weights_scale"], i["gemm2_weights"], i["gemm2_weights_scale"],
+             i["local_expert_offset"]) for i in inps]
+
+
+def make_step(inps: list, combiner=None, marks=None):
+    """One layer call on a step's tokens into `out`: the library entry point
+    (one shard, no combiner), or this rank's shards one after another and the
+    NVLink combine. `marks` (external CUDA events, shards + 2 of them) are
+    recorded before each shard, before the combine and after it."""
     import moe_host
 
+    inp = inps[0]
     if BF16_HIDDEN:
         args = workloads.as_args(inp)
         return lambda tokens, out: moe_host.run_bf16_hidden(tokens["routing_logits"], inp["routing_bias"],
@@ -295,35 +319,51 @@ def layer_call(inp: dict, combiner=None):
         return lambda tokens, out: moe_host.run_dps(tokens["routing_logits"], inp["routing_bias"],
                                                     tokens["hidden_states"], tokens["hidden_states_scale"],
                                                     *args[4:], out)
-    return lambda tokens, out: combiner.forward(
-        {"routing_logits": tokens["routing_logits"], "routing_bias": inp["routing_bias"],
-         "hidden_states": tokens["hidden_states"], "hidden_states_scale": tokens["hidden_states_scale"],
-         "routed_scaling_factor": inp["routed_scaling_factor"]},
-        inp["gemm1_weights"], inp["gemm1_weights_scale"], inp["gemm2_weights"], inp["gemm2_weights_scale"],
-        inp["local_expert_offset"], out)
+    shards = shard_list(inps)
+
+    def step(tokens, out):
+        tok = {"routing_logits": tokens["routing_logits"], "routing_bias": inp["routing_bias"],
+               "hidden_states": tokens["hidden_states"], "hidden_states_scale": tokens["hidden_states_scale"],
+               "routed_scaling_factor": inp["routed_scaling_factor"]}
+        for s, (w13, s13, w2, s2, off) in enumerate(shards):
+            if marks is not None:
+                marks[s].record()
+            combiner.run_shard(s, tok, w13, s13, w2, s2, off)
+        if marks is not None:
+            marks[len(shards)].record()
+        combiner.combine(tok["routing_logits"].shape[0], out)
+        if marks is not None:
+            marks[len(shards) + 1].record()
+        return out
+    return step
 
 
-def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=None,
-               do_flush: bool = True, combiner=None, clocks=None) -> dict:
-    """Device time of `steps` layer calls replayed from a CUDA graph, each
-    after a 256 MB write flush when `do_flush` (otherwise back to back; the
+def time_step(inps: list, steps: int, warmup: int, flush: torch.Tensor, group=None,
+              do_flush: bool = True, combiner=None, clocks=None, flushed_too: bool = True) -> dict:
+    """Device time of `steps` calls replayed from a CUDA graph, each after a
+    256 MB write flush when `do_flush` (otherwise back to back, and the
     flushed timing is then taken as well, as `call_ms_flushed`). A second
-    graph of the same call records the library's stage events and gives the
-    per-stage breakdown (its event nodes add a little latency, so the
-    headline time comes from the graph without them). With a combiner (N>1)
-    each call is this rank's shard plus the NVLink combine, both in the
-    graph."""
+    graph of the same call gives the breakdown: with one shard the library's
+    stage events, with a combiner external events around every shard and the
+    combine (their nodes add a little latency, so the headline time comes
+    from the graph without them)."""
     import moe_host
     import torch.distributed as dist
 
-    call = layer_call(inp, combiner)
+    inp = inps[0]
     tokens = {k: inp[k] for k in token_keys()}
     T = inp["routing_logits"].shape[0]
     dev = inp["routing_logits"].device
     out = torch.empty(T, 7168, dtype=torch.bfloat16, device=dev)
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(moe_host.NUM_STAGE_EVENTS)]
-    for e in ev:
-        e.record()
+    call = make_step(inps, combiner)
+    if combiner is None:
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(moe_host.NUM_STAGE_EVENTS)]
+        for e in ev:
+            e.record()
+        staged_call = call
+    else:
+        ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(inps) + 2)]
+        staged_call = make_step(inps, combiner, marks=ev)
     for _ in range(warmup):
         call(tokens, out)
     torch.cuda.synchronize()
@@ -332,18 +372,21 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
     with torch.cuda.stream(cap_stream):
         with torch.cuda.graph(plain, stream=cap_stream):
             call(tokens, out)
-        moe_host.set_stage_events(ev)
+        if combiner is None:
+            moe_host.set_stage_events(ev)
         try:
             with torch.cuda.graph(staged, stream=cap_stream):
-                call(tokens, out)
+                staged_call(tokens, out)
         finally:
-            moe_host.set_stage_events(None)
+            if combiner is None:
+                moe_host.set_stage_events(None)
     for _ in range(warmup):
         plain.replay()
     torch.cuda.synchronize()
     if group is not None:
         dist.barrier(group=group)
     torch.cuda.synchronize()
+
     def timed(flushed: bool, sampler=None) -> list:
         starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
         ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
@@ -370,28 +413,38 @@ def time_layer(inp: dict, steps: int, warmup: int, flush: torch.Tensor, group=No
         return [a.elapsed_time(b) for a, b in zip(starts, ends)]
 
     call_ms = timed(do_flush, clocks)
-    call_ms_flushed = call_ms if do_flush else timed(True)
-    stage_ms = {n: [] for n in moe_host.STAGE_NAMES}
+    call_ms_flushed = call_ms if (do_flush or not flushed_too) else timed(True)
+    # the same calls once more, replaying the graph with the breakdown events
+    parts: dict[str, list] = {}
     for _ in range(max(3, steps // 4)):
         if do_flush:
             flush.zero_()
         staged.replay()
-        torch.cuda.synchronize()  # the stage events are reused every replay
-        for j, name in enumerate(moe_host.STAGE_NAMES):
-            stage_ms[name].append(ev[j].elapsed_time(ev[j + 1]))
+        torch.cuda.synchronize()  # the events are reused every replay
+        if combiner is None:
+            names = moe_host.STAGE_NAMES
+        else:
+            names = [f"shard{s}" for s in range(len(inps))] + ["combine"]
+        for j, name in enumerate(names):
+            parts.setdefault(name, []).append(ev[j].elapsed_time(ev[j + 1]))
+    torch.cuda.synchronize()
+    if group is not None:
+        dist.barrier(group=group)
     del plain, staged
     return {"call_ms": call_ms, "call_ms_flushed": call_ms_flushed,
-            "stage_ms": {k: statistics.mean(v) for k, v in stage_ms.items()}, "out": out}
+            "stage_ms": {k: statistics.mean(v) for k, v in parts.items()}, "out": out}
 
 
-def time_e2e(inp: dict, steps: int, warmup: int, group=None, combiner=None) -> dict:
+def time_e2e(inps: list, steps: int, warmup: int, group=None, combiner=None) -> dict:
     """The public API call with host buffers: every step copies its
     activations host->device from pinned memory, runs the layer through
-    moe_host.run_dps and copies the bf16 result device->host. Copies run on
-    their own streams with two buffer sets, so step i+1's upload and step
-    i-1's download overlap step i's compute; the timed region spans the first
+    moe_host.run_dps (with a combiner: this rank's shards and the NVLink
+    combine) and copies the bf16 result device->host. Copies run on their
+    own streams with two buffer sets, so step i+1's upload and step i-1's
+    download overlap step i's compute; the timed region spans the first
     upload to the last download."""
-    call = layer_call(inp, combiner)
+    inp = inps[0]
+    call = make_step(inps, combiner)
     dev = inp["routing_logits"].device
     T = inp["routing_logits"].shape[0]
     keys = token_keys()
@@ -439,42 +492,76 @@ def time_e2e(inp: dict, steps: int, warmup: int, group=None, combiner=None) -> d
     return {"ms": s.elapsed_time(e) / steps, "h2d": h2d, "d2h": d2h}
 
 
-def cpu_baseline(inp: dict, max_experts: int = 4) -> dict:
-    """The CPU restatement of the reference algorithm (oracle/) timed on the
-    host cores over a bounded sample: routing of all tokens plus up to
-    `max_experts` active experts, scaled to all active experts."""
+def ep_check(combiner, inps: list, fused: torch.Tensor, group) -> dict:
+    """Correctness of the combined output of the last timed call: every
+    rank's status words, the output against the fp32 sum over every shard of
+    every rank of independent layer runs (moe_host.run, the regular entry
+    point), within the operator tolerance, and identical on all ranks."""
+    import moe_host
+    import torch.distributed as dist
+
+    status = combiner.status()
+    ref = None
+    for inp in inps:
+        part = moe_host.run(*workloads.as_args(inp)).float()
+        ref = part if ref is None else ref + part
+    world = 1 if group is None else dist.get_world_size(group)
+    if world > 1:
+        dist.all_reduce(ref, group=group)
+    err = (fused.float() - ref).abs()
+    amax = float(ref.abs().max())
+    matched = float((err <= REL_TOL * amax).float().mean())
+    other = fused.clone()
+    if world > 1:
+        dist.broadcast(other, src=0, group=group)
+    mine = torch.tensor([float(status), matched, float(err.max()), 1.0 if torch.equal(fused, other) else 0.0],
+                        dtype=torch.float64, device=fused.device)
+    allr = [torch.zeros_like(mine) for _ in range(world)]
+    if world > 1:
+        dist.all_gather(allr, mine, group=group)
+    else:
+        allr = [mine]
+    st = 0
+    for v in allr:
+        st |= int(v[0])
+    return {"status": st, "matched": round(min(float(v[1]) for v in allr), 6),
+            "max_err": max(float(v[2]) for v in allr), "max_abs_ref": amax,
+            "identical": all(float(v[3]) == 1.0 for v in allr),
+            "reference": "fp32 sum of independent moe_b200_run outputs of every shard",
+            "tolerance": f"|err| <= {REL_TOL} * max|ref| on >= {MATCH_FRAC} of elements"}
+
+
+def cpu_oracle_time(inp: dict, runs: int = 3) -> dict:
+    """The CPU restatement of the reference algorithm (oracle/) over the
+    whole workload (every active expert) on the host cores: one warm-up run,
+    then the median of `runs` runs. The inputs are copied to host memory
+    first, outside the timing (only the active experts' weights)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import moe_oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
-    args = workloads.as_args(inp)
-    active = moe_oracle.active_local_experts(inp["routing_logits"], inp["routing_bias"],
+    small = ("routing_logits", "routing_bias", "hidden_states", "hidden_states_scale")
+    cpu_inp = {k: (v.cpu() if isinstance(v, torch.Tensor) and k in small else v) for k, v in inp.items()}
+    active = moe_oracle.active_local_experts(cpu_inp["routing_logits"], cpu_inp["routing_bias"],
                                              inp["routed_scaling_factor"], inp["local_expert_offset"])
-    sample = active[:max_experts]
-    # the sample's weights are copied to host memory once, outside the timing
-    cpu_inp = {k: (v.cpu() if isinstance(v, torch.Tensor) and k in ("routing_logits", "routing_bias",
-                                                                      "hidden_states", "hidden_states_scale")
-                   else v) for k, v in inp.items()}
     for k in ("gemm1_weights", "gemm1_weights_scale", "gemm2_weights", "gemm2_weights_scale"):
         full = inp[k]
         host = torch.zeros(full.shape, dtype=full.dtype)
-        for e in sample:
+        for e in active:
             host[e].copy_(full[e].cpu())
         cpu_inp[k] = host
     cargs = workloads.as_args(cpu_inp)
-    t0 = time.perf_counter()
-    moe_oracle.route(cpu_inp["routing_logits"], cpu_inp["routing_bias"], inp["routed_scaling_factor"])
-    t_route = time.perf_counter() - t0
-    moe_oracle.moe_forward(*cargs, experts=sample)  # warm-up
-    t0 = time.perf_counter()
-    moe_oracle.moe_forward(*cargs, experts=sample)
-    t_sample = time.perf_counter() - t0
-    n = max(len(sample), 1)
-    est = t_route + (t_sample - t_route) * len(active) / n if active else t_sample
-    return {"value": est * 1e6, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
-            "sample": f"T={inp['routing_logits'].shape[0]}: routing of all tokens + {len(sample)} of "
-                      f"{len(active)} active experts, scaled to all active experts "
-                      f"(sample took {t_sample:.2f} s)"}
+    moe_oracle.moe_forward(*cargs)   # warm-up
+    times = []
+    for _ in range(runs):
+        t0 = time.perf_counter()
+        moe_oracle.moe_forward(*cargs)
+        times.append(time.perf_counter() - t0)
+    T = inp["routing_logits"].shape[0]
+    return {"value": round(statistics.median(times) * 1e6, 1), "unit": UNIT, "cores": torch.get_num_threads(),
+            "kind": "port", "runs_s": [round(t, 3) for t in times],
+            "sample": f"T={T}, all {len(active)} active experts (the whole call), median of {runs} runs "
+                      f"after one warm-up"}
 
 
 def roofline_entry(ms: float, nbytes: int, flops: int, peaks: dict, bound: str) -> dict:
@@ -490,27 +577,97 @@ def roofline_entry(ms: float, nbytes: int, flops: int, peaks: dict, bound: str) 
             "frac": round(achieved / peak, 4)}
 
 
+def roofline_point(us: float, lb: int, lf: int, peaks: dict, n_gpus: int = 1) -> dict:
+    t_hbm = lb / (n_gpus * peaks["hbm_gbs"] * 1e9)
+    t_tc = lf / (n_gpus * 2.0 * peaks["bf16_tflops"] * 1e12)
+    r = max(t_hbm, t_tc) * 1e6
+    return {"roofline_us": round(r, 2), "roofline_bound": "hbm" if t_hbm >= t_tc else "tensor",
+            "frac_of_roofline": round(r / us, 4) if us > 0 else None}
+
+
+def first_seed_with_local_pick(T: int, device, seed: int = SEED) -> int:
+    """The first seed >= `seed` whose tokens pick at least one of the 32
+    local experts at offset 0 (with offset 0 a token reaches them only when
+    routing group 0 is among its 4 kept groups, about half the time)."""
+    import moe_host
+
+    for s in range(seed, seed + 1000):
+        r = workloads.make_routing_inputs(T, s, device)
+        idx, _ = moe_host.route(r["routing_logits"], r["routing_bias"], 2.5)
+        if bool(((idx >= 0) & (idx < 32)).any()):
+            return s
+    raise RuntimeError("no seed with a local pick")
+
+
 def point(T: int, variant: str, steps: int, warmup: int, flush, peaks, device, seed=SEED) -> dict:
     inp = workloads.make_inputs(T, seed, device, variant)
     st = routing_stats(inp)
-    r = time_layer(inp, steps, warmup, flush, do_flush=not weights_exceed_l2(st))
+    r = time_step([inp], steps, warmup, flush, do_flush=not weights_exceed_l2(st))
     us = statistics.mean(r["call_ms"]) * 1e3
-    kb, kf = kernel_bytes(st), kernel_flops(st)
     lb = layer_bytes(st)
-    lf = kf["gemm1"] + kf["gemm2"]
-    res = {"T": T, "variant": variant, "us_per_call": round(us, 2), **st,
+    lf = layer_flops(st["sum_Tk"])
+    res = {"T": T, "variant": variant, "seed": seed, "us_per_call": round(us, 2), **st,
            "layer_GBps": round(lb / (us * 1e-6) / 1e9, 1), "layer_TFLOPs": round(lf / (us * 1e-6) / 1e12, 2),
            "stages_us": {k: round(v * 1e3, 2) for k, v in r["stage_ms"].items()},
            "l2": "back to back (weights > 2x L2)" if weights_exceed_l2(st) else "256 MB write flush",
            "us_per_call_l2_write_flushed": round(statistics.mean(r["call_ms_flushed"]) * 1e3, 2)}
-    t_hbm = lb / (peaks["hbm_gbs"] * 1e9)
-    t_tc = lf / (2.0 * peaks["bf16_tflops"] * 1e12)
-    res["roofline_us"] = round(max(t_hbm, t_tc) * 1e6, 2)
-    res["roofline_bound"] = "hbm" if t_hbm >= t_tc else "tensor"
-    res["frac_of_roofline"] = round(res["roofline_us"] / us, 4)
-    if T in PUBLISHED_US:
+    res.update(roofline_point(us, lb, lf, peaks))
+    if T in PUBLISHED_US and st["sum_Tk"] > 0:
         res["published_reference_us"] = PUBLISHED_US[T]
     del r["out"]
+    return res
+
+
+def all_shard_point(T: int, variant: str, desc: str, steps: int, warmup: int, flush, peaks, device, group,
+                    world: int, rank: int) -> dict:
+    """Configs 3 and 4: the whole layer over all 256 experts as 8 shards of
+    32, 8/N shards per rank (offsets 32 * (rank * 8/N + s)), each shard its
+    own layer call with its combine rows kept, then one NVLink combine.
+    Total work is fixed ("strong" scaling); the time is the max over ranks.
+    Reports every shard's routing statistics and time, each rank's shard and
+    combine times, the whole-layer roofline over N GPUs and an ep_check."""
+    import expert_parallel
+    import torch.distributed as dist
+
+    spr = NUM_SHARDS // world
+    offsets = [32 * (rank * spr + s) for s in range(spr)]
+    inps = [workloads.make_inputs(T, SEED, device, variant, off, 2.5, weight_seed=SEED + 1 + off // 32)
+            for off in offsets]
+    stats = [routing_stats(i) for i in inps]
+    combiner = expert_parallel.NvlinkCombiner(T, device, group, shards_per_rank=spr)
+    try:
+        r = time_step(inps, steps, warmup, flush, group, do_flush=False, combiner=combiner, flushed_too=False)
+        check = ep_check(combiner, inps, r["out"], group)
+    finally:
+        combiner.close()
+    step_us = statistics.mean(r["call_ms"]) * 1e3
+    shard_us = [r["stage_ms"][f"shard{s}"] * 1e3 for s in range(spr)]
+    comb_us = r["stage_ms"]["combine"] * 1e3
+    mine = torch.tensor([step_us, sum(shard_us), comb_us], dtype=torch.float64, device=device)
+    rows = torch.tensor([[offsets[s], st["E_act"], st["sum_Tk"], st["max_Tk"], st["tokens_touched"], shard_us[s]]
+                         for s, st in enumerate(stats)], dtype=torch.float64, device=device)
+    if world > 1:
+        allm = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allm, mine, group=group)
+        allrows = [torch.zeros_like(rows) for _ in range(world)]
+        dist.all_gather(allrows, rows, group=group)
+    else:
+        allm, allrows = [mine], [rows]
+    per_rank = [{"rank": q, "us_per_call": round(float(v[0]), 2), "shards_us": round(float(v[1]), 2),
+                 "combine_us": round(float(v[2]), 2)} for q, v in enumerate(allm)]
+    shards = [{"local_expert_offset": int(x[0]), "E_act": int(x[1]), "sum_Tk": int(x[2]), "max_Tk": int(x[3]),
+               "tokens_touched": int(x[4]), "us": round(float(x[5]), 2)} for rr in allrows for x in rr]
+    us = max(p["us_per_call"] for p in per_rank)
+    e_act = sum(s["E_act"] for s in shards)
+    sum_tk = sum(s["sum_Tk"] for s in shards)
+    lb = e_act * LAYER_BYTES_PER_EXPERT + T * LAYER_BYTES_PER_TOKEN + 512
+    lf = layer_flops(sum_tk)
+    res = {"T": T, "variant": variant, "workload": desc, "n_gpus": world, "shards_per_rank": spr,
+           "scaling": "strong (all 256 experts at every N)", "us_per_call": round(us, 2),
+           "E_act": e_act, "sum_Tk": sum_tk, "layer_TFLOPs": round(lf / (us * 1e-6) / 1e12, 2),
+           "max_shard_us": max(s["us"] for s in shards), "per_rank": per_rank, "shards": shards,
+           "l2": "back to back (weights > 2x L2)", "ep_check": check}
+    res.update(roofline_point(us, lb, lf, peaks, world))
     return res
 
 
@@ -521,7 +678,7 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--no-extras", action="store_true", help="skip the sweep/prefill/stress points")
+    ap.add_argument("--no-extras", action="store_true", help="skip the sweep/prefill/stress/EP points")
     ap.add_argument("--workload", choices=tuple(WORKLOADS), default="decode",
                     help="headline configuration (default: config 1 decode, T=64)")
     ap.add_argument("--bf16-hidden", action="store_true",
@@ -545,6 +702,8 @@ def main() -> None:
     device = torch.device("cuda", local_rank)
     group = None
     if world > 1:
+        if NUM_SHARDS % world != 0:
+            raise SystemExit(f"--gpus {world} must divide the {NUM_SHARDS} expert shards")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
         group = dist.group.WORLD
     moe_host.load_library()
@@ -573,31 +732,43 @@ def main() -> None:
         import expert_parallel
         combiner = expert_parallel.NvlinkCombiner(HEADLINE_T, device, group)
     with ClockSampler(device) as clocks:
-        r = time_layer(inp, args.steps, warmup, flush, group, do_flush=not back_to_back, combiner=combiner,
-                       clocks=clocks)
+        r = time_step([inp], args.steps, warmup, flush, group, do_flush=not back_to_back, combiner=combiner,
+                      clocks=clocks)
+    check = ep_check(combiner, [inp], r["out"], group) if combiner is not None else None
     call_ms = torch.tensor(r["call_ms"], dtype=torch.float64, device=device)
     mean_ms = call_ms.mean()
     if group is not None:
         dist.all_reduce(mean_ms, op=dist.ReduceOp.MAX, group=group)
     per_rank = None
     if group is not None:
-        mine = torch.tensor([float(statistics.mean(r["call_ms"])) * 1e3, float(st["E_act"]), float(st["sum_Tk"])],
+        mine = torch.tensor([float(statistics.mean(r["call_ms"])) * 1e3, float(st["E_act"]), float(st["sum_Tk"]),
+                             r["stage_ms"]["shard0"] * 1e3, r["stage_ms"]["combine"] * 1e3],
                             dtype=torch.float64, device=device)
         allr = [torch.zeros_like(mine) for _ in range(world)]
         dist.all_gather(allr, mine, group=group)
-        per_rank = [{"rank": q, "us_per_call": round(float(v[0]), 2), "E_act": int(v[1]), "sum_Tk": int(v[2])}
+        per_rank = [{"rank": q, "us_per_call": round(float(v[0]), 2), "E_act": int(v[1]), "sum_Tk": int(v[2]),
+                     "layer_us": round(float(v[3]), 2), "combine_us": round(float(v[4]), 2)}
                     for q, v in enumerate(allr)]
     mean_ms = float(mean_ms)
     flushed_ms = torch.tensor(r["call_ms_flushed"], dtype=torch.float64, device=device).mean()
     if group is not None:
         dist.all_reduce(flushed_ms, op=dist.ReduceOp.MAX, group=group)
 
-    e2e = time_e2e(inp, args.steps, warmup, group, combiner)
+    e2e = time_e2e([inp], args.steps, warmup, group, combiner)
     e2e_ms = torch.tensor(e2e["ms"], dtype=torch.float64, device=device)
     if group is not None:
         dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX, group=group)
+    if combiner is not None:
+        combiner.close()
+        combiner = None
 
-    stage = r["stage_ms"]
+    # the kernel breakdown of the headline: the library's stage events at
+    # N=1; at N>1 the same call on one GPU without the combine
+    if group is None:
+        stage = r["stage_ms"]
+    else:
+        stage = time_step([inp], max(5, args.steps // 2), warmup, flush, None, do_flush=not back_to_back,
+                          flushed_too=False)["stage_ms"]
     kb, kf = kernel_bytes(st), kernel_flops(st)
     dominant = "gemm1" if stage["gemm1"] >= stage["gemm2"] else "gemm2"
     # a kernel is tensor-bound when its FLOPs at the dense e4m3 peak take
@@ -615,7 +786,9 @@ def main() -> None:
 
     # decode (T <= 64): front end, GEMM1, GEMM2, finalize; larger T: route,
     # permute (two kernels above 1024 tokens), gather, GEMM1, GEMM2, finalize,
-    # and with bf16 hidden states the per-token quantiser first
+    # and with bf16 hidden states the per-token quantiser first. At N>1 the
+    # layer writes no output (no finalize) and the combine kernel follows,
+    # so the count per call is the same.
     if HEADLINE_T <= 64:
         launches_per_call = 4
     else:
@@ -652,47 +825,78 @@ def main() -> None:
                 "d2h_bytes_per_step": e2e["d2h"]},
         "gpu_launches": launches_per_call * args.steps,
         **({"per_rank": per_rank} if per_rank is not None else {}),
+        **({"ep_check": check} if check is not None else {}),
         "clocks": clocks.summary(),
     }
 
-    if world == 1 and not args.no_extras and args.workload == "decode" and not BF16_HIDDEN:
-        n_extra = max(5, args.steps // 2)
-        line["sweep"] = [point(T, "uniform", n_extra, warmup, flush, peaks, device) for T in (1, 4, 16, 64)]
+    extras = not args.no_extras and args.workload == "decode" and not BF16_HIDDEN
+    n_extra = max(5, args.steps // 2)
+    if extras and world == 1:
+        sweep = []
+        for T in (1, 4, 16, 64):
+            seed = first_seed_with_local_pick(T, device) if T == 1 else SEED
+            p = point(T, "uniform", n_extra, warmup, flush, peaks, device, seed=seed)
+            if T == 1:
+                p["seed_rule"] = f"first seed >= {SEED} whose token picks a local expert"
+            sweep.append(p)
+        line["sweep"] = sweep
         line["prefill"] = point(4096, "hot", n_extra, warmup, flush, peaks, device)
-        line["stress"] = point(16384, "zipf", max(3, n_extra // 2), warmup, flush, peaks, device)
-        line["cpu_baseline"] = cpu_baseline(inp)
+    if extras:
+        line["ep_t8192"] = all_shard_point(
+            8192, "uniform", "config3: T=8192, all 256 experts in 8 shards, NVLink combine", n_extra, warmup,
+            flush, peaks, device, group, world, rank)
+        line["stress"] = all_shard_point(
+            16384, "zipf", "config4 stress: T=16384, Zipf(1.2) expert popularity, all 256 experts in 8 shards",
+            max(3, n_extra // 2), warmup, flush, peaks, device, group, world, rank)
+    if extras and world == 1:
+        line["cpu_baseline"] = cpu_oracle_time(inp)
+        c0 = workloads.make_inputs(16, 0, device)
+        line["cpu_baseline_config0"] = cpu_oracle_time(c0)
+        del c0
 
     if group is not None:
         dist.barrier(group=group)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if group is not None:
-        del combiner   # release the symmetric workspace before the group goes
         torch.cuda.synchronize()
         dist.barrier(group=group)
         dist.destroy_process_group()
 
 
 def run_reference(args, world: int, rank: int, warmup: int) -> None:
-    """The reference algorithm on the host cores (rank 0 only)."""
+    """The reference algorithm on the host cores (rank 0 only): every step
+    is one whole call of the CPU restatement (all active experts)."""
     if rank != 0:
         return
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import moe_oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
-    device = "cuda" if torch.cuda.is_available() else "cpu"
     HEADLINE_T, variant, desc = WORKLOADS[args.workload]
-    inp = workloads.make_inputs(HEADLINE_T, SEED, device, variant, 0, 2.5, weight_seed=SEED + 1)
+    # the inputs come from the same seeded generators on the same device as
+    # our arm's (CPU and CUDA generators differ), so the tokens, routing and
+    # weights are the same; only the active experts' weights are drawn, then
+    # everything is copied to host memory outside the timing
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    r = workloads.make_routing_inputs(HEADLINE_T, SEED, dev, variant, 0)
+    active = moe_oracle.active_local_experts(r["routing_logits"].cpu(), r["routing_bias"].cpu(), 2.5, 0)
+    inp = workloads.make_inputs(HEADLINE_T, SEED, dev, variant, 0, 2.5, experts=active, weight_seed=SEED + 1)
+    inp = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    if dev == "cuda":
+        torch.cuda.empty_cache()
+    cargs = workloads.as_args(inp)
     times = []
-    base = None
     for i in range(warmup + args.steps):
-        b = cpu_baseline(inp, max_experts=2)
-        base = b
+        t0 = time.perf_counter()
+        moe_oracle.moe_forward(*cargs)
+        dt = time.perf_counter() - t0
         if i >= warmup:
-            times.append(b["value"])
+            times.append(dt * 1e6)
     v = statistics.mean(times)
-    base["value"] = round(v, 1)
+    base = {"value": round(v, 1), "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"T={HEADLINE_T}: every step one whole call (routing + all {len(active)} active experts)",
+            "median_us": round(statistics.median(times), 1)}
     line = {
         "metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(v / 1e3, 3), "higher_is_better": False, "scaling": "weak",

@@ -1,18 +1,20 @@
 // Expert-parallel combine over NVLink peer memory.
 //
 // With expert parallelism every rank runs the layer on the same tokens for
-// its own 32-expert shard and leaves the fp32 combine rows in its workspace
-// (moe_b200_run with a null output). This kernel then forms the bf16 output
-// of the whole layer on every rank in one launch:
+// its own expert shards (one moe_b200_run per 32-expert shard, each with its
+// own workspace) and leaves the fp32 combine rows in those workspaces
+// (output = NULL). This kernel then forms the bf16 output of the whole layer
+// on every rank in one launch:
 //   1. announce "my combine rows are final" to every peer (a release store at
 //      system scope of a call counter into the peer's flag array) and wait
 //      (bounded) until every peer has announced;
 //   2. reduce this rank's 1/W slice of the token rows: for each row, the fp32
-//      rows of all ranks are read over NVLink (plain loads of peer memory),
-//      summed in fp32 in rank order and rounded once to bf16; the result is
-//      stored into the output staging area of every rank (plain stores to
-//      peer memory) -- reduce-scatter and all-gather in one pass, with the
-//      sum formed before the single bf16 rounding;
+//      rows of every shard of every rank are read (plain loads of peer memory
+//      over NVLink for the other ranks' shards), summed in fp32 in shard order
+//      (rank-major) and rounded once to bf16; the result is stored into the
+//      output staging area of every rank (plain stores to peer memory) --
+//      reduce-scatter and all-gather in one pass, with the sum formed before
+//      the single bf16 rounding;
 //   3. count this CTA's slice as written on every rank (release reduction at
 //      system scope), wait (bounded) until every CTA of every rank has
 //      written into this rank's staging area, and copy it to the caller's
@@ -20,11 +22,15 @@
 // Counters only grow (the call number is kept in the EP area), so nothing
 // has to be cleared between calls and the sequence can be captured in a CUDA
 // graph. No multicast and no library kernel touches peer memory; every wait
-// gives up after one second with a status bit instead of hanging.
+// gives up after one second with a status bit instead of hanging. A wait that
+// gives up leaves the ranks' counters out of step, so it also marks every
+// rank's area as poisoned: every later combine on those areas returns at once
+// with a status bit, until every rank has zeroed its area's counter block.
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 
 #include "../../include/moe_b200.h"
 #include "moe_kernels.cuh"
@@ -36,27 +42,31 @@ namespace moe {
 namespace {
 
 constexpr uint32_t kStatusTimeoutPeer = 1u << 7;   // a peer never announced / wrote its slice
+constexpr uint32_t kStatusPoisoned = 1u << 8;      // an earlier combine on these areas gave up a wait
 constexpr int kEpMaxRanks = 8;
+constexpr int kEpMaxSources = 8;                   // shards summed by one combine, over all ranks
 constexpr int kEpThreads = 256;
 
 // Layout of a rank's expert-parallel area (moe_b200_ep_area_bytes): the
 // counters sit at fixed offsets, so calls with different token counts find
-// them in the same place.
+// them in the same place. Bytes [0, kStage) are the counter block.
 struct EpArea {
   static constexpr size_t kFlags = 0;       // int32[kEpMaxRanks]: call number announced by each rank
   static constexpr size_t kDone = 64;       // int32: CTAs (of all ranks) that wrote into this staging
   static constexpr size_t kFinished = 68;   // int32: CTAs of this rank that finished a call
   static constexpr size_t kCalls = 72;      // int32: completed calls of this rank
+  static constexpr size_t kPoison = 76;     // int32: nonzero once a combine on these areas gave up a wait
   static constexpr size_t kStage = 256;     // bf16[T, 7168] output staging
 };
+static_assert(EpArea::kStage == MOE_B200_EP_COUNTER_BYTES, "counter block size in the header");
 
 struct EpParams {
   uint8_t* area[kEpMaxRanks];          // each rank's EP area (this process's mapping)
-  const float* y[kEpMaxRanks];         // each rank's fp32 combine rows
-  const int32_t* slot[kEpMaxRanks];    // each rank's token -> combine row map, null: row = token
+  const float* y[kEpMaxSources];       // each shard's fp32 combine rows, rank-major
+  const int32_t* slot[kEpMaxSources];  // each shard's token -> combine row map, null: row = token
   uint16_t* out;                       // this rank's output, bf16 [T, 7168]
   uint32_t* status;                    // this rank's status word
-  int rank, world, num_tokens;
+  int rank, world, sources, num_tokens;
 };
 
 __device__ __forceinline__ int ld_acquire_sys(const int* p) {
@@ -83,14 +93,25 @@ __device__ __forceinline__ bool wait_at_least(const int* p, int target) {
   return true;
 }
 
+// A wait gave up: record it and poison every rank's area, so that no later
+// combine runs on counters that are out of step.
+__device__ __forceinline__ void give_up(const EpParams& p) {
+  atomicOr(p.status, kStatusTimeoutPeer);
+  for (int q = 0; q < p.world; ++q) st_release_sys(reinterpret_cast<int*>(p.area[q] + EpArea::kPoison), 1);
+}
+
 }  // namespace
 
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
   __shared__ int s_ok;
-  pdl_wait();   // this rank's layer (its GEMM2 reductions) has completed
+  pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
   const int W = p.world;
   const int T = p.num_tokens;
   uint8_t* mine = p.area[p.rank];
+  if (*reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0) {
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusPoisoned);
+    return;
+  }
   const int call = *reinterpret_cast<volatile int*>(mine + EpArea::kCalls) + 1;
 
   // ---- 1. announce and wait for every rank -------------------------------
@@ -100,7 +121,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
     st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, call);
   if (threadIdx.x < W &&
       !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kFlags) + threadIdx.x, call)) {
-    atomicOr(p.status, kStatusTimeoutPeer);
+    give_up(p);
     s_ok = 0;
   }
   __syncthreads();
@@ -116,7 +137,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
     const int t = r0 + static_cast<int>(it / kOcts);
     const int j = static_cast<int>(it % kOcts);
     float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < W; ++q) {
+    for (int q = 0; q < p.sources; ++q) {
       const int row = p.slot[q] != nullptr ? p.slot[q][t] : t;
       if (row < 0) continue;
       const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row) * kHidden) + 2 * j;
@@ -142,7 +163,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
   }
   if (threadIdx.x == 0 &&
       !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone), call * W * static_cast<int>(gridDim.x))) {
-    atomicOr(p.status, kStatusTimeoutPeer);
+    give_up(p);
     s_ok = 0;
   }
   __syncthreads();
@@ -184,41 +205,108 @@ size_t moe_b200_ep_area_bytes(int64_t num_tokens) {
   return EpArea::kStage + (static_cast<size_t>(num_tokens) * kHidden * 2 + 255) / 256 * 256;
 }
 
-int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
-                        int64_t num_tokens, void* output, void* stream) {
-  if (rank_workspaces == nullptr || rank_areas == nullptr || output == nullptr || world < 1 ||
-      world > kEpMaxRanks || rank < 0 || rank >= world || num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS)
+int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_rank, void* const* rank_areas,
+                               int rank, int world, int64_t num_tokens, void* output, void* stream) {
+  if (shard_workspaces == nullptr || rank_areas == nullptr || output == nullptr || world < 1 ||
+      world > kEpMaxRanks || shards_per_rank < 1 || world * shards_per_rank > kEpMaxSources || rank < 0 ||
+      rank >= world || num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
   moe_b200_workspace_layout l;
   if (moe_b200_get_workspace_layout(num_tokens, &l) != MOE_B200_OK) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(output) % 16 != 0) return MOE_B200_ERR_MISALIGNED;
+  const int sources = world * shards_per_rank;
   EpParams p;
-  for (int q = 0; q < kEpMaxRanks; ++q) {
-    p.area[q] = nullptr;
+  for (int q = 0; q < kEpMaxRanks; ++q) p.area[q] = nullptr;
+  for (int q = 0; q < kEpMaxSources; ++q) {
     p.y[q] = nullptr;
     p.slot[q] = nullptr;
   }
   for (int q = 0; q < world; ++q) {
-    uint8_t* ws = static_cast<uint8_t*>(rank_workspaces[q]);
     uint8_t* area = static_cast<uint8_t*>(rank_areas[q]);
-    if (ws == nullptr || area == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
-    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0 || reinterpret_cast<uintptr_t>(area) % 256 != 0)
-      return MOE_B200_ERR_MISALIGNED;
+    if (area == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(area) % 256 != 0) return MOE_B200_ERR_MISALIGNED;
     p.area[q] = area;
+  }
+  for (int q = 0; q < sources; ++q) {
+    uint8_t* ws = static_cast<uint8_t*>(shard_workspaces[q]);
+    if (ws == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+    if (reinterpret_cast<uintptr_t>(ws) % 256 != 0) return MOE_B200_ERR_MISALIGNED;
     p.y[q] = reinterpret_cast<const float*>(ws + l.y_acc);
     // decode-size calls keep one combine row per token
     p.slot[q] = num_tokens <= kDecodeMaxTokens ? nullptr : reinterpret_cast<const int32_t*>(ws + l.tok_slot);
   }
   p.out = static_cast<uint16_t*>(output);
-  p.status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(rank_workspaces[rank]) + l.status);
+  // this rank's first shard workspace holds the status word the caller reads
+  p.status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(shard_workspaces[rank * shards_per_rank]) +
+                                         l.status);
   p.rank = rank;
   p.world = world;
+  p.sources = sources;
   p.num_tokens = static_cast<int>(num_tokens);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (launch_kernel(ep_combine_kernel, kEpGrid, kEpThreads, 0, s, true, p) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   return MOE_B200_OK;
+}
+
+int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
+                        int64_t num_tokens, void* output, void* stream) {
+  return moe_b200_ep_combine_shards(rank_workspaces, 1, rank_areas, rank, world, num_tokens, output, stream);
+}
+
+// ---- device buffers shared between processes (CUDA IPC) -------------------
+
+int moe_b200_ep_buffer_alloc(size_t bytes, void** ptr) {
+  if (ptr == nullptr || bytes == 0) return MOE_B200_ERR_INVALID_ARGUMENT;
+  *ptr = nullptr;
+  void* p = nullptr;
+  if (cudaMalloc(&p, bytes) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_B200_ERR_CUDA;
+  }
+  if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    cudaFree(p);
+    return MOE_B200_ERR_CUDA;
+  }
+  *ptr = p;
+  return MOE_B200_OK;
+}
+
+int moe_b200_ep_buffer_free(void* ptr) {
+  if (ptr == nullptr) return MOE_B200_OK;
+  return cudaFree(ptr) == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
+}
+
+int moe_b200_ipc_get_handle(const void* buffer, void* handle) {
+  if (buffer == nullptr || handle == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+  static_assert(sizeof(cudaIpcMemHandle_t) == MOE_B200_IPC_HANDLE_BYTES, "IPC handle size in the header");
+  cudaIpcMemHandle_t h;
+  if (cudaIpcGetMemHandle(&h, const_cast<void*>(buffer)) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_B200_ERR_CUDA;
+  }
+  memcpy(handle, &h, sizeof(h));
+  return MOE_B200_OK;
+}
+
+int moe_b200_ipc_open_handle(const void* handle, void** buffer) {
+  if (handle == nullptr || buffer == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+  *buffer = nullptr;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  void* p = nullptr;
+  if (cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+    cudaGetLastError();
+    return MOE_B200_ERR_CUDA;
+  }
+  *buffer = p;
+  return MOE_B200_OK;
+}
+
+int moe_b200_ipc_close_handle(void* buffer) {
+  if (buffer == nullptr) return MOE_B200_OK;
+  return cudaIpcCloseMemHandle(buffer) == cudaSuccess ? MOE_B200_OK : MOE_B200_ERR_CUDA;
 }
 
 }  // extern "C"

@@ -398,7 +398,7 @@ static bool valid_routing(int method, int top_k) {
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 6; }
+int moe_b200_abi_version(void) { return 7; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {

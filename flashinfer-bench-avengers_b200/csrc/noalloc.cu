@@ -74,3 +74,13 @@ extern "C" int moe_b200_run_noalloc(const float* routing_logits, const void* rou
                       gemm2_weights_scale, local_expert_offset, routed_scaling_factor, num_tokens,
                       output, scratch, moe::kNoAllocScratchBytes, stream);
 }
+
+// The status word of the allocation-free calls sits inside the fixed array,
+// at the same offset as in any workspace, so the regular reader applies once
+// the array's device address is known.
+extern "C" int moe_b200_noalloc_read_status(uint32_t* status, void* stream) {
+  if (status == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;
+  void* scratch = moe::scratch_for_current_device();
+  if (scratch == nullptr) return MOE_B200_ERR_CUDA;
+  return moe_b200_read_status(scratch, status, stream);
+}

@@ -140,7 +140,9 @@ __device__ __forceinline__ void route_token(const RouteParams& p, int t, int lan
         bs = cs[j];
       }
     }
-    const uint32_t key = bj >= 0 ? order_key(bv) : 0u;
+    // a candidate's key is at least 1, so it always beats a lane with none
+    // left (key 0), even when its value is the NaN whose order key is 0
+    const uint32_t key = bj >= 0 ? max(order_key(bv), 1u) : 0u;
     const uint32_t best = __reduce_max_sync(0xffffffffu, key);
     const int wl = __ffs(__ballot_sync(0xffffffffu, key == best)) - 1;
     if (lane == wl) taken |= 1u << bj;
@@ -225,7 +227,9 @@ __device__ __forceinline__ void route_token_simple(const RouteParams& p, int t, 
       int bj = 0;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const uint32_t key = ((taken >> j) & 1u) ? 0u : order_key(l[j]);
+        // untaken experts have keys >= 1 (the NaN whose order key is 0
+        // included), so a taken one (key 0) is never picked again
+        const uint32_t key = ((taken >> j) & 1u) ? 0u : max(order_key(l[j]), 1u);
         if (key > bk) {
           bk = key;
           bj = j;

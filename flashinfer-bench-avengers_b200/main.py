@@ -4,10 +4,12 @@ Same signature and meaning as the reference entry point
 (solution/cuda/main.py:31-54): returns a new bf16 [T, 7168] tensor.
 ``run_dps`` is the destination-passing variant that writes ``output``.
 
-Unlike the reference (solution/cuda/main.py:6-29), importing this module
-compiles nothing and deletes no cache: it loads the prebuilt sm_100a
-library libmoe_b200.so next to this file (built by build.py), and raises
-if that library is missing.
+Like the reference (solution/cuda/main.py:6-29), importing this module
+compiles the CUDA sources from source when needed: it loads the sm_100a
+library libmoe_b200.so next to this file, building it first with build.py
+(nvcc, a few seconds) when it is missing or was built from other sources.
+Unlike the reference it deletes no cache and recompiles nothing when the
+build is current. It raises if the library cannot be built.
 """
 from __future__ import annotations
 

@@ -72,16 +72,29 @@ class WorkspaceLayout(ctypes.Structure):
     ]
 
 
+def _build_module():
+    """This package's build.py, loaded by path (a top-level module named
+    ``build`` could be another package's)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("moe_b200_build", os.path.join(_HERE, "build.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
-    """Loads (once) the C-ABI library; raises if it has not been built."""
+    """Loads (once) the C-ABI library. The in-tree library is first compiled
+    from csrc/ when it is missing or older than its sources (nvcc needed);
+    a build failure raises, since the layer has no fallback implementation."""
     global _lib
     with _lib_lock:
         if _lib is not None:
             return _lib
+        if os.path.abspath(path) == os.path.abspath(LIB_PATH):
+            _build_module().build()
         if not os.path.exists(path):
-            raise RuntimeError(
-                f"{path} is missing: build it with `python build.py` in {_HERE} "
-                "(the MoE layer has no fallback implementation)")
+            raise RuntimeError(f"{path} is missing (the MoE layer has no fallback implementation)")
         lib = ctypes.CDLL(path)
         lib.moe_b200_workspace_bytes.argtypes = [_I64]
         lib.moe_b200_workspace_bytes.restype = ctypes.c_size_t
@@ -116,6 +129,25 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_ep_combine.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
                                             ctypes.c_int, ctypes.c_int, _I64, _P, _P]
         lib.moe_b200_ep_combine.restype = ctypes.c_int
+        lib.moe_b200_ep_combine_shards.argtypes = [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                                   ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                                   _I64, _P, _P]
+        lib.moe_b200_ep_combine_shards.restype = ctypes.c_int
+        lib.moe_b200_ep_buffer_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]
+        lib.moe_b200_ep_buffer_alloc.restype = ctypes.c_int
+        lib.moe_b200_ep_buffer_free.argtypes = [_P]
+        lib.moe_b200_ep_buffer_free.restype = ctypes.c_int
+        lib.moe_b200_ipc_get_handle.argtypes = [_P, _P]
+        lib.moe_b200_ipc_get_handle.restype = ctypes.c_int
+        lib.moe_b200_ipc_open_handle.argtypes = [_P, ctypes.POINTER(ctypes.c_void_p)]
+        lib.moe_b200_ipc_open_handle.restype = ctypes.c_int
+        lib.moe_b200_ipc_close_handle.argtypes = [_P]
+        lib.moe_b200_ipc_close_handle.restype = ctypes.c_int
+        lib.moe_b200_run_noalloc.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64,
+                                             ctypes.c_double, _I64, _P, _P]
+        lib.moe_b200_run_noalloc.restype = ctypes.c_int
+        lib.moe_b200_noalloc_read_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), _P]
+        lib.moe_b200_noalloc_read_status.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -401,6 +433,65 @@ def ep_combine(rank_workspace_ptrs: list[int], rank_area_ptrs: list[int], rank: 
     _raise_on(load_library().moe_b200_ep_combine(ws, areas, int(rank), world, int(num_tokens),
                                                    output.data_ptr(), stream), "moe_b200_ep_combine")
     return output
+
+
+def ep_combine_shards(shard_workspace_ptrs: list[int], shards_per_rank: int, rank_area_ptrs: list[int],
+                      rank: int, num_tokens: int, output: torch.Tensor) -> torch.Tensor:
+    """moe_b200_ep_combine_shards: bf16 sum over every shard of every rank
+    into ``output``; ``shard_workspace_ptrs`` lists world * shards_per_rank
+    workspace addresses rank-major, ``rank_area_ptrs`` one EP area per rank."""
+    _check(output.is_cuda and output.dtype == torch.bfloat16 and output.is_contiguous()
+           and tuple(output.shape) == (int(num_tokens), H), f"output must be a contiguous bf16 [T, {H}] tensor")
+    world = len(rank_area_ptrs)
+    _check(len(shard_workspace_ptrs) == world * int(shards_per_rank), "world * shards_per_rank workspaces")
+    n = len(shard_workspace_ptrs)
+    ws = (ctypes.c_void_p * n)(*[ctypes.c_void_p(int(p)) for p in shard_workspace_ptrs])
+    areas = (ctypes.c_void_p * world)(*[ctypes.c_void_p(int(p)) for p in rank_area_ptrs])
+    stream = torch.cuda.current_stream(output.device).cuda_stream
+    _raise_on(load_library().moe_b200_ep_combine_shards(ws, int(shards_per_rank), areas, int(rank), world,
+                                                          int(num_tokens), output.data_ptr(), stream),
+              "moe_b200_ep_combine_shards")
+    return output
+
+
+def run_noalloc(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
+                gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+                routed_scaling_factor, output: torch.Tensor) -> torch.Tensor:
+    """moe_b200_run_noalloc: the layer for at most 16 tokens with the
+    library's fixed scratch array instead of a workspace."""
+    T = _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale,
+                      gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale)
+    _check(isinstance(output, torch.Tensor) and output.device == routing_logits.device
+           and tuple(output.shape) == (T, H) and output.dtype == torch.bfloat16 and output.is_contiguous(),
+           f"output must be a contiguous bf16 [T, {H}] tensor on the inputs' device")
+    if T == 0:
+        return output
+    dev = routing_logits.device
+    with torch.cuda.device(dev):
+        logits = routing_logits.contiguous()
+        bias, bias_dtype = _bias_arg(routing_bias)
+        hs_scale = hidden_states_scale.contiguous()
+        s13 = gemm1_weights_scale.contiguous()
+        s2 = gemm2_weights_scale.contiguous()
+        code = load_library().moe_b200_run_noalloc(
+            logits.data_ptr(), bias.data_ptr(), bias_dtype, hidden_states.data_ptr(), hs_scale.data_ptr(),
+            gemm1_weights.data_ptr(), s13.data_ptr(), gemm2_weights.data_ptr(), s2.data_ptr(),
+            int(local_expert_offset), float(routed_scaling_factor), T, output.data_ptr(),
+            torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_run_noalloc")
+    return output
+
+
+def noalloc_read_status(device: torch.device | None = None) -> int:
+    """Status word of the last moe_b200_run_noalloc on ``device`` (0 = clean)."""
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    st = ctypes.c_uint32(0)
+    with torch.cuda.device(dev):
+        code = load_library().moe_b200_noalloc_read_status(ctypes.byref(st),
+                                                            torch.cuda.current_stream(dev).cuda_stream)
+    if code not in (0, 7):
+        _raise_on(code, "moe_b200_noalloc_read_status")
+    return int(st.value)
 
 
 def run(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,

@@ -70,6 +70,9 @@ MOE_B200_API size_t moe_b200_workspace_bytes(int64_t num_tokens);
  *                         the fp32 combine rows stay in the workspace (y_acc) for
  *                         moe_b200_ep_combine and no output is written
  *
+ * Logits and bias must be finite. With a NaN among them the selection is
+ * unspecified, but a token never selects the same expert twice.
+ *
  * Alignment: hidden_states, gemm1_weights, gemm2_weights, routing_logits,
  * routing_bias and output 16 bytes; workspace 256 bytes.
  * The call is asynchronous on `stream` (a cudaStream_t) and performs no
@@ -174,8 +177,13 @@ MOE_B200_API int moe_b200_route(const float* routing_logits, const void* routing
  * Reads the device status word of the last moe_b200_run that used this
  * workspace (synchronises `stream`). *status receives the raw bits (0 when
  * every bounded wait completed); returns MOE_B200_ERR_DEVICE_TIMEOUT when
- * any bit is set. No reference counterpart (the reference's waits are
- * unbounded, solution/cuda/kernel.cu:300-307).
+ * any bit is set. Bits: 1 << 0..3 a GEMM role (TMA producer, MMA issuer,
+ * epilogue, scale combiner) gave up a wait; 1 << 4 a routing pick out of
+ * range; 1 << 5 a work-unit hand-off timed out; 1 << 6 a grid-wide arrival
+ * count never completed; 1 << 7 an EP combine gave up waiting for a peer;
+ * 1 << 8 an EP combine found its areas poisoned by an earlier give-up. The
+ * word is cleared by each layer call. No reference counterpart (the
+ * reference's waits are unbounded, solution/cuda/kernel.cu:300-307).
  */
 MOE_B200_API int moe_b200_read_status(const void* workspace, uint32_t* status, void* stream);
 
@@ -268,13 +276,25 @@ MOE_B200_API int moe_b200_run_noalloc(const float* routing_logits, const void* r
                                       void* output, void* stream);
 
 /*
+ * moe_b200_read_status for moe_b200_run_noalloc: reads the device status
+ * word of the last allocation-free call on the current device (its status
+ * word lives in the library's fixed array, which the caller cannot
+ * address). Synchronises `stream`; same bits and return values as
+ * moe_b200_read_status. A nonzero word means a kernel gave up a bounded
+ * wait and the output of that call is not valid. Like the calls themselves,
+ * it must not overlap another allocation-free call on the same device.
+ */
+MOE_B200_API int moe_b200_noalloc_read_status(uint32_t* status, void* stream);
+
+/*
  * Expert-parallel combine over NVLink peer memory. No reference counterpart
  * (the reference is single-GPU).
  *
  * With expert parallelism every rank calls moe_b200_run on the same tokens
  * for its own expert shard (local_expert_offset) with output = NULL, on a
- * workspace that every rank can address (e.g. symmetric memory: the same
- * allocation mapped in every process). Each rank also owns an EP area of
+ * workspace that every rank can address (e.g. a moe_b200_ep_buffer_alloc
+ * buffer mapped in every process through its IPC handle, below). Each rank
+ * also owns an EP area of
  * moe_b200_ep_area_bytes(max tokens) bytes, equally addressable by all.
  * moe_b200_ep_combine then writes the bf16 sum over all ranks of the layer
  * output into `output` (this rank's, bf16 [T, 7168]): each rank reduces 1/W
@@ -290,12 +310,48 @@ MOE_B200_API int moe_b200_run_noalloc(const float* routing_logits, const void* r
  * Every rank must call it once per layer call, on the stream of its
  * moe_b200_run, with the same num_tokens. Each EP area must be zero before
  * the first call (its counters only grow, so later calls need no clearing).
- * Each wait on a peer gives up after one second and sets a bit of the
- * status word (moe_b200_read_status). Asynchronous, no host synchronisation.
+ * Each wait on a peer gives up after one second, sets status bit 1 << 7
+ * (moe_b200_read_status) and marks every rank's area as poisoned: from then
+ * on every combine on those areas returns at once with status bit 1 << 8 and
+ * writes no output. To recover, every rank synchronises its device, zeroes
+ * the first MOE_B200_EP_COUNTER_BYTES of its own area, and the ranks meet at
+ * a host barrier before any of them calls the combine again.
+ * Asynchronous, no host synchronisation.
  */
+#define MOE_B200_EP_COUNTER_BYTES 256
 MOE_B200_API size_t moe_b200_ep_area_bytes(int64_t num_tokens);
 MOE_B200_API int moe_b200_ep_combine(void* const* rank_workspaces, void* const* rank_areas, int rank, int world,
                                      int64_t num_tokens, void* output, void* stream);
+
+/*
+ * moe_b200_ep_combine for ranks that own several 32-expert shards each (for
+ * example all 8 shards of the 256 experts on fewer than 8 GPUs). Each rank
+ * runs one moe_b200_run per shard with output = NULL, each on its own
+ * workspace; shard_workspaces lists world * shards_per_rank workspaces,
+ * rank-major (rank q's shards at [q * shards_per_rank, (q + 1) *
+ * shards_per_rank)), as mapped in this process. The output is the bf16
+ * rounding of the fp32 sum of every shard's combine rows in that order.
+ * world * shards_per_rank <= 8. The status word written is that of this
+ * rank's first shard workspace. moe_b200_ep_combine is this call with
+ * shards_per_rank = 1. No reference counterpart.
+ */
+MOE_B200_API int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_rank,
+                                            void* const* rank_areas, int rank, int world, int64_t num_tokens,
+                                            void* output, void* stream);
+
+/*
+ * Device buffers that other processes of the node map through CUDA IPC, for
+ * the workspaces and EP areas above: plain cudaMalloc memory (one allocation
+ * per buffer, zero-filled, no multicast object), a 64-byte handle per
+ * buffer, opened in a peer process with peer access enabled. Set-up calls:
+ * alloc and open synchronise the device. No reference counterpart.
+ */
+#define MOE_B200_IPC_HANDLE_BYTES 64
+MOE_B200_API int moe_b200_ep_buffer_alloc(size_t bytes, void** buffer);
+MOE_B200_API int moe_b200_ep_buffer_free(void* buffer);
+MOE_B200_API int moe_b200_ipc_get_handle(const void* buffer, void* handle);
+MOE_B200_API int moe_b200_ipc_open_handle(const void* handle, void** buffer);
+MOE_B200_API int moe_b200_ipc_close_handle(void* buffer);
 
 /* ABI version of this header (bumped on any signature or struct layout change). */
 MOE_B200_API int moe_b200_abi_version(void);

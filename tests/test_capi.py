@@ -130,7 +130,7 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 6
+    assert lib.moe_b200_abi_version() == 7
 
 
 def test_widened_entry_points_reject_bad_arguments_without_a_device(lib):
@@ -160,3 +160,38 @@ def test_widened_entry_points_reject_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_run_bf16_hidden(p, p, 0, None, p, p, p, p, 0, 2.5, 4, p, p, big, None) == 1
     assert lib.moe_b200_run_bf16_hidden(p, p, 0, p, p, p, p, p, 0, 2.5, 4, p, p, 16, None) == 3
     assert lib.moe_b200_run_bf16_hidden(p, p, 0, p, p, p, p, p, 0, 2.5, 0, p, p, 16, None) == 0
+
+
+def test_ep_and_ipc_entry_points_reject_bad_arguments_without_a_device(lib):
+    """The expert-parallel combine, its IPC buffer helpers and the
+    allocation-free status reader check their arguments before any CUDA call."""
+    P = ctypes.c_void_p
+    buf = ctypes.create_string_buffer(4096 + 256)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    p = P(base)
+    arr = (P * 8)(*([p] * 8))
+    # shards: world * shards_per_rank must stay within 8, rank inside [0, world)
+    assert lib.moe_b200_ep_combine_shards(arr, 0, arr, 0, 2, 4, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(arr, 3, arr, 0, 4, 4, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(arr, 1, arr, 2, 2, 4, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(arr, 1, arr, 0, 9, 4, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(None, 1, arr, 0, 2, 4, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(arr, 4, arr, 0, 2, -1, p, None) == 1
+    assert lib.moe_b200_ep_combine_shards(arr, 4, arr, 0, 2, 4, P(base + 8), None) == 2    # misaligned output
+    mis = (P * 8)(*([P(base + 16)] * 8))
+    assert lib.moe_b200_ep_combine_shards(mis, 4, arr, 0, 2, 4, p, None) == 2            # misaligned workspace
+    assert lib.moe_b200_ep_combine_shards(arr, 4, mis, 0, 2, 4, p, None) == 2            # misaligned area
+    assert lib.moe_b200_ep_combine_shards(arr, 4, arr, 0, 2, 0, p, None) == 0            # T = 0 is a no-op
+    assert lib.moe_b200_ep_combine(arr, arr, 0, 2, 0, p, None) == 0
+    assert lib.moe_b200_ep_area_bytes(16) == 256 + (16 * 7168 * 2 + 255) // 256 * 256
+    assert lib.moe_b200_ep_area_bytes(-1) == 0
+    out = P()
+    assert lib.moe_b200_ep_buffer_alloc(0, ctypes.byref(out)) == 1
+    assert lib.moe_b200_ep_buffer_alloc(16, None) == 1
+    assert lib.moe_b200_ep_buffer_free(None) == 0
+    assert lib.moe_b200_ipc_get_handle(None, p) == 1
+    assert lib.moe_b200_ipc_get_handle(p, None) == 1
+    assert lib.moe_b200_ipc_open_handle(None, ctypes.byref(out)) == 1
+    assert lib.moe_b200_ipc_open_handle(p, None) == 1
+    assert lib.moe_b200_ipc_close_handle(None) == 0
+    assert lib.moe_b200_noalloc_read_status(None, None) == 1

@@ -49,6 +49,12 @@ def _noalloc(lib, inp, out):
     return code
 
 
+def _noalloc_status(lib) -> int:
+    st = ctypes.c_uint32(0)
+    lib.moe_b200_noalloc_read_status(ctypes.byref(st), torch.cuda.current_stream().cuda_stream)
+    return int(st.value)
+
+
 def test_noalloc_matches_regular_entry_point_twice(lib):
     import moe_host
 
@@ -57,10 +63,17 @@ def test_noalloc_matches_regular_entry_point_twice(lib):
         out = torch.full((T, workloads.H), float("nan"), dtype=torch.bfloat16, device="cuda")
         assert _noalloc(lib, inp, out) == 0
         torch.cuda.synchronize()
+        # the status word lives in the library's array; every bounded wait completed
+        assert _noalloc_status(lib) == 0
         ref = moe_host.run(*workloads.as_args(inp))
         torch.cuda.synchronize()
         ok, matched, max_err, ref_max = moe_oracle.output_close(out, ref, REL_TOL, MATCH_FRAC)
         assert ok, f"T={T}: matched {matched:.5f}, max err {max_err:.4g}, max|ref| {ref_max:.4g}"
+        if T == 5:  # one call also against the CPU oracle directly
+            cpu = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+            oref = moe_oracle.moe_forward(*workloads.as_args(cpu))
+            ok, matched, max_err, ref_max = moe_oracle.output_close(out.cpu(), oref, REL_TOL, MATCH_FRAC)
+            assert ok, f"oracle T={T}: matched {matched:.5f}, max err {max_err:.4g}, max|ref| {ref_max:.4g}"
 
 
 def test_noalloc_rejects_batches_beyond_its_limit(lib):
