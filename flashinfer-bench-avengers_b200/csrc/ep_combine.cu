@@ -11,14 +11,16 @@
 //   2. reduce this rank's 1/W slice of the token rows: for each row, the fp32
 //      rows of every shard of every rank are read (plain loads of peer memory
 //      over NVLink for the other ranks' shards), summed in fp32 in shard order
-//      (rank-major) and rounded once to bf16; the result is stored into the
-//      output staging area of every rank (plain stores to peer memory) --
-//      reduce-scatter and all-gather in one pass, with the sum formed before
-//      the single bf16 rounding;
+//      (rank-major) and rounded once to bf16; the result is stored into this
+//      rank's output and into the output staging area of every other rank
+//      (plain stores to peer memory) -- reduce-scatter and all-gather in one
+//      pass, with the sum formed before the single bf16 rounding;
 //   3. count this CTA's slice as written on every rank (release reduction at
 //      system scope), wait (bounded) until every CTA of every rank has
-//      written into this rank's staging area, and copy it to the caller's
-//      output.
+//      written into this rank's staging area, and copy the other ranks' rows
+//      to the caller's output.
+// With one rank (all shards on one GPU) only the reduction runs, straight
+// into the output, and the counters are not touched.
 // Counters only grow (the call number is kept in the EP area), so nothing
 // has to be cleared between calls and the sequence can be captured in a CUDA
 // graph. No multicast and no library kernel touches peer memory; every wait
@@ -46,6 +48,10 @@ constexpr uint32_t kStatusPoisoned = 1u << 8;      // an earlier combine on thes
 constexpr int kEpMaxRanks = 8;
 constexpr int kEpMaxSources = 8;                   // shards summed by one combine, over all ranks
 constexpr int kEpThreads = 256;
+// CTAs of the combine per SM. All of them must be resident at once (they
+// wait for each other), which __launch_bounds__ guarantees for two 256-thread
+// CTAs per SM when nothing else runs on the device.
+constexpr int kEpCtasPerSm = 2;
 
 // Layout of a rank's expert-parallel area (moe_b200_ep_area_bytes): the
 // counters sit at fixed offsets, so calls with different token counts find
@@ -83,14 +89,50 @@ __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-// Spins (bounded) until *p >= target. Returns false on timeout.
-__device__ __forceinline__ bool wait_at_least(const int* p, int target) {
+// Spins (bounded) until *p has reached target. The counters only grow and
+// wrap around after 2^32 increments, so "reached" is a signed difference,
+// valid while the two are less than 2^31 apart. Returns false on timeout.
+__device__ __forceinline__ bool wait_at_least(const int* p, uint32_t target) {
   const uint64_t t0 = globaltimer_ns();
   uint32_t spins = 0;
-  while (ld_acquire_sys(p) < target) {
+  while (static_cast<int32_t>(static_cast<uint32_t>(ld_acquire_sys(p)) - target) < 0) {
     if ((++spins & 63u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) return false;
   }
   return true;
+}
+
+// The fp32 sum over all sources of 8 columns of token t's rows, rounded to
+// bf16 (16 bytes). Every source's row index and data are loaded before the
+// sum, so up to 16 loads per thread are in flight; absent rows add +0.0,
+// which leaves the sum's bits as they are (the sum starts at +0.0).
+__device__ __forceinline__ uint4 reduce_octet(const EpParams& p, int t, int j) {
+  int row[kEpMaxSources];
+#pragma unroll
+  for (int q = 0; q < kEpMaxSources; ++q)
+    row[q] = q < p.sources ? (p.slot[q] != nullptr ? __ldg(p.slot[q] + t) : t) : -1;
+  float4 u[kEpMaxSources], v[kEpMaxSources];
+#pragma unroll
+  for (int q = 0; q < kEpMaxSources; ++q) {
+    u[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    v[q] = u[q];
+    if (row[q] >= 0) {
+      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row[q]) * kHidden) + 2 * j;
+      u[q] = src[0];
+      v[q] = src[1];
+    }
+  }
+  float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < kEpMaxSources; ++q) {
+    a[0] += u[q].x; a[1] += u[q].y; a[2] += u[q].z; a[3] += u[q].w;
+    a[4] += v[q].x; a[5] += v[q].y; a[6] += v[q].z; a[7] += v[q].w;
+  }
+  const __nv_bfloat162 b0 = __floats2bfloat162_rn(a[0], a[1]);
+  const __nv_bfloat162 b1 = __floats2bfloat162_rn(a[2], a[3]);
+  const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[4], a[5]);
+  const __nv_bfloat162 b3 = __floats2bfloat162_rn(a[6], a[7]);
+  return make_uint4(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1),
+                    *reinterpret_cast<const uint32_t*>(&b2), *reinterpret_cast<const uint32_t*>(&b3));
 }
 
 // A wait gave up: record it and poison every rank's area, so that no later
@@ -102,23 +144,37 @@ __device__ __forceinline__ void give_up(const EpParams& p) {
 
 }  // namespace
 
-__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
+__global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(EpParams p) {
   __shared__ int s_ok;
   pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
   const int W = p.world;
   const int T = p.num_tokens;
+  constexpr int kOcts = kHidden / 8;   // 8 columns (two float4 per source in, one 16-byte bf16 out)
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kEpThreads;
+  uint4* out = reinterpret_cast<uint4*>(p.out);
+
+  if (W == 1) {   // one rank: a plain reduction of its shards into the output
+    const int64_t items = static_cast<int64_t>(T) * kOcts;
+    for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items; it += stride) {
+      const int t = static_cast<int>(it / kOcts);
+      const int j = static_cast<int>(it % kOcts);
+      out[static_cast<int64_t>(t) * kOcts + j] = reduce_octet(p, t, j);
+    }
+    return;
+  }
+
   uint8_t* mine = p.area[p.rank];
   if (*reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0) {
     if (threadIdx.x == 0) atomicOr(p.status, kStatusPoisoned);
     return;
   }
-  const int call = *reinterpret_cast<volatile int*>(mine + EpArea::kCalls) + 1;
+  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) + 1u;
 
   // ---- 1. announce and wait for every rank -------------------------------
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x < W)
-    st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, call);
+    st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, static_cast<int>(call));
   if (threadIdx.x < W &&
       !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kFlags) + threadIdx.x, call)) {
     give_up(p);
@@ -127,76 +183,57 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(EpParams p) {
   __syncthreads();
   if (!s_ok) return;
 
-  // ---- 2. reduce this rank's rows, store them on every rank ---------------
-  constexpr int kOcts = kHidden / 8;   // 8 columns (two float4 in, one 16-byte bf16 out)
+  // ---- 2. reduce this rank's rows: into its own output, and into every
+  //         peer's staging area ---------------------------------------------
   const int r0 = static_cast<int>(static_cast<int64_t>(T) * p.rank / W);
   const int r1 = static_cast<int>(static_cast<int64_t>(T) * (p.rank + 1) / W);
   const int64_t items = static_cast<int64_t>(r1 - r0) * kOcts;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items;
-       it += static_cast<int64_t>(gridDim.x) * kEpThreads) {
+  for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items; it += stride) {
     const int t = r0 + static_cast<int>(it / kOcts);
     const int j = static_cast<int>(it % kOcts);
-    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    for (int q = 0; q < p.sources; ++q) {
-      const int row = p.slot[q] != nullptr ? p.slot[q][t] : t;
-      if (row < 0) continue;
-      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row) * kHidden) + 2 * j;
-      const float4 u = src[0], v = src[1];
-      a[0] += u.x; a[1] += u.y; a[2] += u.z; a[3] += u.w;
-      a[4] += v.x; a[5] += v.y; a[6] += v.z; a[7] += v.w;
-    }
-    const __nv_bfloat162 b0 = __floats2bfloat162_rn(a[0], a[1]);
-    const __nv_bfloat162 b1 = __floats2bfloat162_rn(a[2], a[3]);
-    const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[4], a[5]);
-    const __nv_bfloat162 b3 = __floats2bfloat162_rn(a[6], a[7]);
-    const uint4 o = make_uint4(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1),
-                               *reinterpret_cast<const uint32_t*>(&b2), *reinterpret_cast<const uint32_t*>(&b3));
+    const uint4 o = reduce_octet(p, t, j);
+    const int64_t off = static_cast<int64_t>(t) * kOcts + j;
+    out[off] = o;
     for (int q = 0; q < W; ++q)
-      reinterpret_cast<uint4*>(p.area[q] + EpArea::kStage + static_cast<int64_t>(t) * kHidden * 2)[j] = o;
+      if (q != p.rank) reinterpret_cast<uint4*>(p.area[q] + EpArea::kStage)[off] = o;
   }
 
-  // ---- 3. count this CTA's slice on every rank, wait for all, copy out -----
+  // ---- 3. count this CTA's slice on every rank, wait for all, copy the
+  //         other ranks' rows out of the staging area -----------------------
   __syncthreads();
   if (threadIdx.x < W) {
     __threadfence_system();
     red_release_sys_add(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kDone), 1);
   }
   if (threadIdx.x == 0 &&
-      !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone), call * W * static_cast<int>(gridDim.x))) {
+      !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone),
+                     call * static_cast<uint32_t>(W) * gridDim.x)) {
     give_up(p);
     s_ok = 0;
   }
   __syncthreads();
   if (s_ok) {
     const uint4* stage = reinterpret_cast<const uint4*>(mine + EpArea::kStage);
-    uint4* out = reinterpret_cast<uint4*>(p.out);
-    const int64_t n16 = static_cast<int64_t>(T) * kOcts;
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; i < n16;
-         i += static_cast<int64_t>(gridDim.x) * kEpThreads)
-      out[i] = stage[i];
+    const int64_t lo = static_cast<int64_t>(r0) * kOcts, hi = static_cast<int64_t>(r1) * kOcts;
+    const int64_t n16 = static_cast<int64_t>(T) * kOcts - (hi - lo);   // everything but this rank's rows
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; i < n16; i += stride) {
+      const int64_t k = i < lo ? i : i + (hi - lo);
+      out[k] = stage[k];
+    }
   }
   // The last CTA of this rank to finish advances the call number (every CTA
   // has read it by then).
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const int f = atomicAdd(reinterpret_cast<int*>(mine + EpArea::kFinished), 1) + 1;
-    if (f == call * static_cast<int>(gridDim.x)) *reinterpret_cast<volatile int*>(mine + EpArea::kCalls) = call;
+    const uint32_t f = atomicAdd(reinterpret_cast<unsigned int*>(mine + EpArea::kFinished), 1u) + 1u;
+    if (f == call * gridDim.x) *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) = call;
   }
 }
 
 }  // namespace moe
 
 using namespace moe;
-
-namespace {
-
-// CTAs of the combine: one constant for every call and rank, because the
-// counters accumulate W x (CTAs per call) per call and must keep the same
-// arithmetic across calls with different token counts.
-constexpr int kEpGrid = 128;
-
-}  // namespace
 
 extern "C" {
 
@@ -244,8 +281,15 @@ int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_ran
   p.world = world;
   p.sources = sources;
   p.num_tokens = static_cast<int>(num_tokens);
+  // The grid is the same for every call and rank (the ranks' GPUs are the
+  // same model): the counters accumulate W x (CTAs per call) per call, so the
+  // arithmetic must not change between calls with different token counts.
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
+    return MOE_B200_ERR_CUDA;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (launch_kernel(ep_combine_kernel, kEpGrid, kEpThreads, 0, s, true, p) != cudaSuccess)
+  if (launch_kernel(ep_combine_kernel, kEpCtasPerSm * sms, kEpThreads, 0, s, true, p) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   return MOE_B200_OK;
 }
