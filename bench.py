@@ -32,9 +32,12 @@ Extra points:
   the per-rank maximum is the figure). Both carry their own ep_check.
 * N=1 only: the decode sweep T in {1,4,16,64} (config 1; T=1 uses the first
   seed >= 1234 whose token picks a local expert, stated in the point), the
-  prefill point (config 2, T=4096 with 4 hot experts) and the CPU baselines
-  (the oracle over all active experts, median of 3 runs, for the headline
-  and for config 0).
+  prefill point (config 2, T=4096 with 4 hot experts), the reference
+  solution's own CUDA kernel timed on the same box and inputs at each of
+  those points (`reference_kernel`, built unchanged from its sources by
+  baseline/build_reference.py; "unavailable" when not built) and the CPU
+  baselines (the oracle over all active experts, median of 3 runs, for the
+  headline and for config 0).
 
 `--impl reference` times the reference algorithm on the host CPU (the
 reference solution has no CPU implementation, so its CPU restatement in
@@ -618,18 +621,65 @@ def point(T: int, variant: str, steps: int, warmup: int, flush, peaks, device, s
     return res
 
 
+def reference_kernel_point(T: int, variant: str, seed: int, steps: int, warmup: int, flush, device,
+                           ours_us: float) -> dict:
+    """The reference solution's own CUDA implementation (built unchanged from
+    its solution/cuda sources by baseline/build_reference.py) on the same
+    inputs as our point: device time of whole calls of its run(...) from a
+    start event to an end event on the stream (its call synchronises the
+    host mid-way and launches per-expert kernels from a host loop, so
+    that time is part of it), with our L2 policy. Its output is compared
+    with ours within the operator tolerance."""
+    import moe_host
+
+    sys.path.insert(0, os.path.join(ROOT, "baseline"))
+    import build_reference
+
+    if build_reference.built_path() is None:
+        return {"T": T, "unavailable": "reference extension not built (baseline/build_reference.py)"}
+    mod = build_reference.load_built()
+    inp = workloads.make_inputs(T, seed, device, variant)
+    st = routing_stats(inp)
+    args = workloads.as_args(inp)
+    do_flush = not weights_exceed_l2(st)
+    for _ in range(warmup):
+        out_ref = mod.run(*args)
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        if do_flush:
+            flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        out_ref = mod.run(*args)
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) * 1e3)
+    ours = moe_host.run(*args)
+    torch.cuda.synchronize()
+    err = (ours.float() - out_ref.float()).abs()
+    amax = float(out_ref.float().abs().max())
+    us = statistics.median(times)
+    return {"T": T, "variant": variant, "seed": seed, "reference_kernel_us": round(us, 2),
+            "ours_us": round(ours_us, 2), "speedup": round(us / ours_us, 2) if ours_us > 0 else None,
+            "E_act": st["E_act"], "sum_Tk": st["sum_Tk"],
+            "ours_vs_reference_matched": round(float((err <= REL_TOL * amax).float().mean()), 6)}
+
+
 def all_shard_point(T: int, variant: str, desc: str, steps: int, warmup: int, flush, peaks, device, group,
-                    world: int, rank: int) -> dict:
+                    world: int, rank: int, shards_per_rank: int | None = None) -> dict:
     """Configs 3 and 4: the whole layer over all 256 experts as 8 shards of
     32, 8/N shards per rank (offsets 32 * (rank * 8/N + s)), each shard its
     own layer call with its combine rows kept, then one NVLink combine.
     Total work is fixed ("strong" scaling); the time is the max over ranks.
     Reports every shard's routing statistics and time, each rank's shard and
-    combine times, the whole-layer roofline over N GPUs and an ep_check."""
+    combine times, the whole-layer roofline over N GPUs and an ep_check.
+    ``shards_per_rank`` below 8/N covers only the first N x that many shards
+    (a smaller case of the same calls, for profiling)."""
     import expert_parallel
     import torch.distributed as dist
 
-    spr = NUM_SHARDS // world
+    spr = NUM_SHARDS // world if shards_per_rank is None else shards_per_rank
     offsets = [32 * (rank * spr + s) for s in range(spr)]
     inps = [workloads.make_inputs(T, SEED, device, variant, off, 2.5, weight_seed=SEED + 1 + off // 32)
             for off in offsets]
@@ -683,6 +733,9 @@ def main() -> None:
                     help="headline configuration (default: config 1 decode, T=64)")
     ap.add_argument("--bf16-hidden", action="store_true",
                     help="bf16 hidden states quantised inside the layer (one GPU; the extras are skipped)")
+    ap.add_argument("--ep-point", default=None, metavar="T:S",
+                    help="only the expert-parallel point with T uniform tokens and S shards per rank "
+                         "(a smaller case of ep_t8192 for profiling); prints that point as the line")
     args = ap.parse_args()
     warmup = max(args.warmup, 3)
 
@@ -709,6 +762,19 @@ def main() -> None:
     moe_host.load_library()
     peaks = load_peaks()
     flush = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device=device)
+
+    if args.ep_point is not None:
+        T_ep, spr = (int(x) for x in args.ep_point.split(":"))
+        res = all_shard_point(T_ep, "uniform", f"expert-parallel point: T={T_ep}, {spr} shards per rank",
+                              args.steps, warmup, flush, peaks, device, group, world, rank, shards_per_rank=spr)
+        if rank == 0:
+            print(json.dumps({"metric": METRIC, "unit": UNIT, "value": res["us_per_call"], "n_gpus": world,
+                              "steps": args.steps, "warmup": warmup, "ep_point": res}), flush=True)
+        if group is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=group)
+            dist.destroy_process_group()
+        return
 
     HEADLINE_T, variant, desc = WORKLOADS[args.workload]
     offset = (32 * rank) % 256
@@ -841,6 +907,10 @@ def main() -> None:
             sweep.append(p)
         line["sweep"] = sweep
         line["prefill"] = point(4096, "hot", n_extra, warmup, flush, peaks, device)
+        # the reference's own Blackwell kernel on the same box and inputs
+        line["reference_kernel"] = [
+            reference_kernel_point(p["T"], p["variant"], p["seed"], n_extra, warmup, flush, device,
+                                   p["us_per_call"]) for p in sweep + [line["prefill"]]]
     if extras:
         line["ep_t8192"] = all_shard_point(
             8192, "uniform", "config3: T=8192, all 256 experts in 8 shards, NVLink combine", n_extra, warmup,

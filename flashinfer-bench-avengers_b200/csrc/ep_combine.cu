@@ -101,11 +101,25 @@ __device__ __forceinline__ bool wait_at_least(const int* p, uint32_t target) {
   return true;
 }
 
-// The fp32 sum over all sources of 8 columns of token t's rows, rounded to
-// bf16 (16 bytes). Every source's row index and data are loaded before the
-// sum, so up to 16 loads per thread are in flight; absent rows add +0.0,
-// which leaves the sum's bits as they are (the sum starts at +0.0).
-__device__ __forceinline__ uint4 reduce_octet(const EpParams& p, int t, int j) {
+// The fp32 sums over all sources of columns 4j .. 4j+3 and 3584+4j .. +3 of
+// token t's rows, rounded to bf16 (two 8-byte results): consecutive threads
+// take consecutive j, so every load instruction of a warp reads 512
+// contiguous bytes. Every source's row index and data are loaded before the
+// sum (up to 16 loads in flight per thread); absent rows add +0.0, which
+// leaves the sum's bits as they are (the sum starts at +0.0).
+struct Bf16Quads {
+  uint2 a, b;
+};
+
+__device__ __forceinline__ uint2 pack_bf16x4(float x, float y, float z, float w) {
+  const __nv_bfloat162 lo = __floats2bfloat162_rn(x, y);
+  const __nv_bfloat162 hi = __floats2bfloat162_rn(z, w);
+  return make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+}
+
+constexpr int kHalfQuads = kHidden / 8;   // 896: quads per half row
+
+__device__ __forceinline__ Bf16Quads reduce_quads(const EpParams& p, int t, int j) {
   int row[kEpMaxSources];
 #pragma unroll
   for (int q = 0; q < kEpMaxSources; ++q)
@@ -116,9 +130,9 @@ __device__ __forceinline__ uint4 reduce_octet(const EpParams& p, int t, int j) {
     u[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     v[q] = u[q];
     if (row[q] >= 0) {
-      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row[q]) * kHidden) + 2 * j;
-      u[q] = src[0];
-      v[q] = src[1];
+      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row[q]) * kHidden);
+      u[q] = src[j];
+      v[q] = src[kHalfQuads + j];
     }
   }
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -127,12 +141,14 @@ __device__ __forceinline__ uint4 reduce_octet(const EpParams& p, int t, int j) {
     a[0] += u[q].x; a[1] += u[q].y; a[2] += u[q].z; a[3] += u[q].w;
     a[4] += v[q].x; a[5] += v[q].y; a[6] += v[q].z; a[7] += v[q].w;
   }
-  const __nv_bfloat162 b0 = __floats2bfloat162_rn(a[0], a[1]);
-  const __nv_bfloat162 b1 = __floats2bfloat162_rn(a[2], a[3]);
-  const __nv_bfloat162 b2 = __floats2bfloat162_rn(a[4], a[5]);
-  const __nv_bfloat162 b3 = __floats2bfloat162_rn(a[6], a[7]);
-  return make_uint4(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1),
-                    *reinterpret_cast<const uint32_t*>(&b2), *reinterpret_cast<const uint32_t*>(&b3));
+  return {pack_bf16x4(a[0], a[1], a[2], a[3]), pack_bf16x4(a[4], a[5], a[6], a[7])};
+}
+
+// Stores the two results into a bf16 [T, 7168] row-major destination.
+__device__ __forceinline__ void store_quads(uint8_t* dst, int t, int j, const Bf16Quads& o) {
+  uint2* row = reinterpret_cast<uint2*>(dst + static_cast<int64_t>(t) * kHidden * 2);
+  row[j] = o.a;
+  row[kHalfQuads + j] = o.b;
 }
 
 // A wait gave up: record it and poison every rank's area, so that no later
@@ -149,16 +165,17 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
   pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
   const int W = p.world;
   const int T = p.num_tokens;
-  constexpr int kOcts = kHidden / 8;   // 8 columns (two float4 per source in, one 16-byte bf16 out)
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * kEpThreads;
-  uint4* out = reinterpret_cast<uint4*>(p.out);
+  // items (a token row and a quad index j < 896) fit in int32: T <= 2^18
+  const int stride = static_cast<int>(gridDim.x) * kEpThreads;
+  const int first = static_cast<int>(blockIdx.x) * kEpThreads + static_cast<int>(threadIdx.x);
+  uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
 
   if (W == 1) {   // one rank: a plain reduction of its shards into the output
-    const int64_t items = static_cast<int64_t>(T) * kOcts;
-    for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items; it += stride) {
-      const int t = static_cast<int>(it / kOcts);
-      const int j = static_cast<int>(it % kOcts);
-      out[static_cast<int64_t>(t) * kOcts + j] = reduce_octet(p, t, j);
+    const int items = T * kHalfQuads;
+    for (int it = first; it < items; it += stride) {
+      const int t = it / kHalfQuads;
+      const int j = it - t * kHalfQuads;
+      store_quads(out, t, j, reduce_quads(p, t, j));
     }
     return;
   }
@@ -187,15 +204,15 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
   //         peer's staging area ---------------------------------------------
   const int r0 = static_cast<int>(static_cast<int64_t>(T) * p.rank / W);
   const int r1 = static_cast<int>(static_cast<int64_t>(T) * (p.rank + 1) / W);
-  const int64_t items = static_cast<int64_t>(r1 - r0) * kOcts;
-  for (int64_t it = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; it < items; it += stride) {
-    const int t = r0 + static_cast<int>(it / kOcts);
-    const int j = static_cast<int>(it % kOcts);
-    const uint4 o = reduce_octet(p, t, j);
-    const int64_t off = static_cast<int64_t>(t) * kOcts + j;
-    out[off] = o;
+  const int items = (r1 - r0) * kHalfQuads;
+  for (int it = first; it < items; it += stride) {
+    const int rel = it / kHalfQuads;
+    const int t = r0 + rel;
+    const int j = it - rel * kHalfQuads;
+    const Bf16Quads o = reduce_quads(p, t, j);
+    store_quads(out, t, j, o);
     for (int q = 0; q < W; ++q)
-      if (q != p.rank) reinterpret_cast<uint4*>(p.area[q] + EpArea::kStage)[off] = o;
+      if (q != p.rank) store_quads(p.area[q] + EpArea::kStage, t, j, o);
   }
 
   // ---- 3. count this CTA's slice on every rank, wait for all, copy the
@@ -213,12 +230,14 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
   }
   __syncthreads();
   if (s_ok) {
+    // 16-byte units, 896 per row: everything but this rank's rows
     const uint4* stage = reinterpret_cast<const uint4*>(mine + EpArea::kStage);
-    const int64_t lo = static_cast<int64_t>(r0) * kOcts, hi = static_cast<int64_t>(r1) * kOcts;
-    const int64_t n16 = static_cast<int64_t>(T) * kOcts - (hi - lo);   // everything but this rank's rows
-    for (int64_t i = static_cast<int64_t>(blockIdx.x) * kEpThreads + threadIdx.x; i < n16; i += stride) {
-      const int64_t k = i < lo ? i : i + (hi - lo);
-      out[k] = stage[k];
+    uint4* out16 = reinterpret_cast<uint4*>(out);
+    const int lo = r0 * kHalfQuads, hi = r1 * kHalfQuads;
+    const int n16 = T * kHalfQuads - (hi - lo);
+    for (int i = first; i < n16; i += stride) {
+      const int k = i < lo ? i : i + (hi - lo);
+      out16[k] = stage[k];
     }
   }
   // The last CTA of this rank to finish advances the call number (every CTA

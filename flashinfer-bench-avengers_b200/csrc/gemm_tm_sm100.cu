@@ -163,6 +163,56 @@ __device__ __forceinline__ void tm_decode(int u, const int* s_unit_pre, const in
   t.kb1 = t.kb0 + per;
 }
 
+// GEMM2 units in groups of kG2BlockGroup W2 column blocks: (block group,
+// expert, block in group, token tile), token tiles fastest (K splits
+// fastest of all). Each unit red.adds into a 256-column block of its
+// tokens' combine rows; ordering by column block keeps that block of every
+// token's row in L2 while all experts add into it, where the expert-major
+// order re-fetched the combine rows from DRAM for every expert (78% of the
+// reduction sectors missed L2 in a T=4096 capture). The token tiles of one
+// (expert, block) still run side by side and share the W2 tile through L2.
+#ifndef MOE_B200_G2_BLOCK_GROUP
+#define MOE_B200_G2_BLOCK_GROUP 4
+#endif
+constexpr int kG2BlockGroup = MOE_B200_G2_BLOCK_GROUP;
+static_assert((kHiddenBlocks / 2) % kG2BlockGroup == 0, "block groups tile the 28 W2 column blocks");
+
+__device__ __forceinline__ void tm_decode_g2(int u, const int* s_unit_pre, const int* s_seg, const int* s_cnt,
+                                             int splits, int kblocks, TmTile& t) {
+  constexpr int kRowBlocks = kHiddenBlocks / 2;
+  const int per_tile = kRowBlocks * splits;            // units of one token tile in s_unit_pre
+  const int total_tiles = s_unit_pre[kExpertsLocal] / per_tile;
+  const int ks = u % splits;
+  const int rest = u / splits;
+  const int group_units = total_tiles * kG2BlockGroup;
+  const int bg = rest / group_units;
+  const int r = rest - bg * group_units;
+  int e = 0;
+#pragma unroll 1
+  while (s_unit_pre[e + 1] / per_tile * kG2BlockGroup <= r) ++e;
+  const int cnt = s_cnt[e];
+  const int nt = (cnt + 127) / 128;
+  const int local = r - s_unit_pre[e] / per_tile * kG2BlockGroup;
+  const int bi = local / nt;
+  const int tt = local - bi * nt;
+  t.e = e;
+  t.blk = bg * kG2BlockGroup + bi;
+  t.row0 = s_seg[e] + tt * 128;
+  t.nvalid = min(128, cnt - tt * 128);
+  const int per = kblocks / splits;
+  t.kb0 = ks * per;
+  t.kb1 = t.kb0 + per;
+}
+
+template <bool kG1>
+__device__ __forceinline__ void tm_unit(int u, const int* s_unit_pre, const int* s_seg, const int* s_cnt,
+                                        int splits, int kblocks, TmTile& t) {
+  if constexpr (kG1)
+    tm_decode(u, s_unit_pre, s_seg, s_cnt, splits, kblocks, t);
+  else
+    tm_decode_g2(u, s_unit_pre, s_seg, s_cnt, splits, kblocks, t);
+}
+
 }  // namespace
 
 template <bool kG1, int kStages>
@@ -306,7 +356,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       TmTile t;
-      tm_decode(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
+      tm_unit<kG1>(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
       int brow0, brow1, wrow0, wrow1;
       if constexpr (kG1) {
         brow0 = t.e * kGemm1Out + t.blk * kBlk;
@@ -476,7 +526,7 @@ __global__ void __launch_bounds__(TmTraits<kG1, kStages>::kThreads, 1)
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       TmTile t;
-      tm_decode(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
+      tm_unit<kG1>(u, s_unit_pre, s_seg, s_cnt, s_unit_pre[kExpertsLocal + 1], Tr::kKBlocks, t);
       const bool valid = r < t.nvalid;
       int my_tok = 0;
       float my_w = 0.f;
