@@ -10,12 +10,15 @@
 //
 // No division is executed in the common case:
 // * scale: s0 = amax * c with c = fp32(1/448), then one FMA correction
-//   s = fma(fma(-s0, 448, amax), c, s0). For every positive finite bf16
-//   amax whose quotient is a normal fp32 number this equals the IEEE
-//   quotient (checked exhaustively, all 31,392 such values); smaller amax
-//   take the division.
+//   s = fma(fma(-s0, 448, amax), c, s0): the residual-correction step of
+//   Markstein's FMA-based division (P. Markstein, "IA-64 and Elementary
+//   Functions", 2000), with the quotient estimate taken from the rounded
+//   reciprocal constant. For every positive finite bf16 amax whose quotient
+//   is a normal fp32 number this equals the IEEE quotient (checked
+//   exhaustively, all 31,392 such values); smaller amax take the division.
 // * values: inv = 1/scale from the hardware reciprocal estimate refined by
-//   one Newton step (error below 1 ulp), so |x| * inv is within 4 ulp of the
+//   one Newton-Raphson step for the reciprocal, inv' = inv + inv * (1 -
+//   scale * inv) (error below 1 ulp), so |x| * inv is within 4 ulp of the
 //   fp32 quotient. e4m3 rounding is monotonic: when the values 6 ulp below
 //   and above |x| * inv round to the same e4m3 value, that is the rounding
 //   of the quotient. Otherwise (a value within 6 ulp of an e4m3 rounding
