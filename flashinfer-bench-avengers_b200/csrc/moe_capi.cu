@@ -209,10 +209,19 @@ int grid_for(int64_t T, int bn, int row_blocks, int splits, int sm_count) {
   return static_cast<int>(units < sm_count ? units : sm_count);
 }
 
+// Selections supplied by the caller (moe_b200_run_routed): [T, top_k]
+// global expert ids and final weights; null for the routing rules.
+struct GivenPicks {
+  const int32_t* idx = nullptr;
+  const float* w = nullptr;
+};
+
 int launch_route(const float* logits, const void* bias, int bias_dtype, int T, float rsf,
                  int local_off, int32_t* topk_idx, float* topk_w, uint16_t* out, int method, int top_k,
-                 cudaStream_t s) {
+                 cudaStream_t s, const GivenPicks& given = GivenPicks{}) {
   RouteParams rp;
+  rp.given_idx = given.idx;
+  rp.given_w = given.w;
   rp.logits = logits;
   rp.bias = bias;
   rp.bias_is_fp32 = bias_dtype == MOE_B200_BIAS_FP32 ? 1 : 0;
@@ -259,7 +268,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
                const void* gemm1_weights,
                const float* gemm1_weights_scale, const void* gemm2_weights,
                const float* gemm2_weights_scale, int local_off, float rsf, int T, void* output,
-               uint8_t* ws, const moe_b200_workspace_layout& l, const DeviceInfo& di, cudaStream_t s) {
+               uint8_t* ws, const moe_b200_workspace_layout& l, const DeviceInfo& di, cudaStream_t s,
+               const GivenPicks& given = GivenPicks{}) {
   // Four K slices: 2048 units of ~0.9 MB keep the SMs evenly loaded; more
   // slices add red.add and unit-switch overhead.
   constexpr int kG1Splits = 4;
@@ -304,6 +314,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
   rp.out = nullptr;
   rp.method = method;
   rp.top_k = top_k;
+  rp.given_idx = given.idx;
+  rp.given_w = given.w;
   DecodeFrontParams dp;
   dp.counts = counts;
   dp.seg_off = seg_off;
@@ -384,21 +396,23 @@ using namespace moe;
 
 // A routing method and top_k the routing kernels support: DeepSeek-V3 with
 // its 8 picks, Llama4 with 1, the others with 1 to 8.
-static bool valid_routing(int method, int top_k) {
+static bool valid_routing(int method, int top_k, bool given_allowed = false) {
+  if (method == kRouteGiven && !given_allowed) return false;   // only through moe_b200_run_routed
   switch (method) {
     case MOE_B200_ROUTING_DEEPSEEK_V3: return top_k == kTopK;
     case MOE_B200_ROUTING_LLAMA4: return top_k == 1;
     case MOE_B200_ROUTING_DEFAULT:
     case MOE_B200_ROUTING_RENORMALIZE:
     case MOE_B200_ROUTING_RENORMALIZE_NAIVE:
-    case MOE_B200_ROUTING_TOPK: return top_k >= 1 && top_k <= kTopK;
+    case MOE_B200_ROUTING_TOPK:
+    case kRouteGiven: return top_k >= 1 && top_k <= kTopK;
     default: return false;
   }
 }
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 7; }
+int moe_b200_abi_version(void) { return 8; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {
@@ -491,14 +505,20 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
                      const void* gemm1_weights, const float* gemm1_weights_scale,
                      const void* gemm2_weights, const float* gemm2_weights_scale,
                      int64_t local_expert_offset, double routed_scaling_factor, int64_t num_tokens,
-                     void* output, void* workspace, size_t workspace_bytes, void* stream) {
+                     void* output, void* workspace, size_t workspace_bytes, void* stream,
+                     const GivenPicks& given = GivenPicks{}) {
   // ---- argument checks (no device work before they pass) -----------------
   if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (routing_bias_dtype != MOE_B200_BIAS_BF16 && routing_bias_dtype != MOE_B200_BIAS_FP32)
     return MOE_B200_ERR_INVALID_ARGUMENT;
-  if (!valid_routing(routing_method, top_k)) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (!valid_routing(routing_method, top_k, given.idx != nullptr || given.w != nullptr))
+    return MOE_B200_ERR_INVALID_ARGUMENT;
   if (num_tokens == 0) return MOE_B200_OK;
-  if (!routing_logits || (!routing_bias && routing_method == MOE_B200_ROUTING_DEEPSEEK_V3) || !hidden_states ||
+  const bool given_picks = routing_method == kRouteGiven;
+  if (given_picks ? (!given.idx || !given.w || !aligned(given.idx, 4) || !aligned(given.w, 4))
+                  : !routing_logits)
+    return given_picks && given.idx && given.w ? MOE_B200_ERR_MISALIGNED : MOE_B200_ERR_INVALID_ARGUMENT;
+  if ((!routing_bias && routing_method == MOE_B200_ROUTING_DEEPSEEK_V3) || !hidden_states ||
       (!hidden_bf16 && !hidden_states_scale) ||
       !gemm1_weights || !gemm1_weights_scale || !gemm2_weights || !gemm2_weights_scale || !workspace)
     return MOE_B200_ERR_INVALID_ARGUMENT;
@@ -544,7 +564,7 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
   if (plan.decode)
     return run_decode(routing_logits, routing_bias, routing_bias_dtype, routing_method, top_k, hidden_states,
                       hidden_states_scale, hidden_bf16, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_off,
-                      static_cast<float>(routed_scaling_factor), T, output, ws, l, di, s);
+                      static_cast<float>(routed_scaling_factor), T, output, ws, l, di, s, given);
 
   // ---- tensor maps ---------------------------------------------------------
   CUtensorMap tm_aperm, tm_w13, tm_w2, tm_chi, tm_clo;
@@ -580,7 +600,7 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
   mark_stage(1, s);
   st = launch_route(routing_logits, routing_bias, routing_bias_dtype, T,
                     static_cast<float>(routed_scaling_factor), local_off, topk_idx, topk_w,
-                    static_cast<uint16_t*>(output), routing_method, top_k, s);
+                    static_cast<uint16_t*>(output), routing_method, top_k, s, given);
   if (st != MOE_B200_OK) return st;
   mark_stage(2, s);
 
@@ -709,6 +729,19 @@ int moe_b200_run_routing(int routing_method, int top_k, const float* routing_log
                    hidden_states_scale, false, gemm1_weights, gemm1_weights_scale, gemm2_weights,
                    gemm2_weights_scale, local_expert_offset, routed_scaling_factor, num_tokens, output, workspace,
                    workspace_bytes, stream);
+}
+
+int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_w, int top_k, const void* hidden_states,
+                        const float* hidden_states_scale, const void* gemm1_weights,
+                        const float* gemm1_weights_scale, const void* gemm2_weights,
+                        const float* gemm2_weights_scale, int64_t local_expert_offset, int64_t num_tokens,
+                        void* output, void* workspace, size_t workspace_bytes, void* stream) {
+  GivenPicks given;
+  given.idx = topk_idx;
+  given.w = topk_w;
+  return run_layer(nullptr, nullptr, MOE_B200_BIAS_BF16, kRouteGiven, top_k, hidden_states, hidden_states_scale,
+                   false, gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale,
+                   local_expert_offset, 1.0, num_tokens, output, workspace, workspace_bytes, stream, given);
 }
 
 int moe_b200_run_bf16_hidden(const float* routing_logits, const void* routing_bias, int routing_bias_dtype,

@@ -18,6 +18,9 @@ enum RouteMethod : int {
   kRouteLlama4 = 3,             // top-1 -> sigmoid
   kRouteRenormalizeNaive = 4,   // softmax -> top-k -> renormalise
   kRouteTopK = 5,               // top-k, uniform weights
+  // Not a routing rule: the selections come from the caller
+  // (moe_b200_run_routed), e.g. the rows an all-to-all dispatch delivered.
+  kRouteGiven = 6,
 };
 // Expert id of the unused selection slots (k >= top_k): never a local expert.
 constexpr int kNoExpert = -(1 << 30);
@@ -34,6 +37,8 @@ struct RouteParams {
   uint16_t* out;            // [T, 7168] bf16 output: rows of tokens with no local pick are zeroed (or null)
   int method;               // RouteMethod
   int top_k;                // selections per token, 1..8 (8 for DeepSeek-V3, 1 for Llama4)
+  const int32_t* given_idx; // kRouteGiven: [T, top_k] global expert ids (anything else for none)
+  const float* given_w;     // kRouteGiven: [T, top_k] final weights
 };
 
 struct PermuteParams {

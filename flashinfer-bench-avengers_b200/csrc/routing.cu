@@ -308,9 +308,30 @@ __device__ __forceinline__ void route_token_simple(const RouteParams& p, int t, 
   }
 }
 
+// Selections given by the caller (kRouteGiven): lane k < top_k takes entry
+// k of token t as it is; the other slots hold kNoExpert and weight 0. No
+// logits are read and no scaling factor is applied.
+__device__ __forceinline__ void route_token_given(const RouteParams& p, int t, int lane, int& out_idx,
+                                                  float& out_w) {
+  int idx = kNoExpert;
+  float w = 0.f;
+  if (lane < p.top_k) {
+    idx = __ldg(p.given_idx + static_cast<int64_t>(t) * p.top_k + lane);
+    w = __ldg(p.given_w + static_cast<int64_t>(t) * p.top_k + lane);
+  }
+  out_idx = idx;
+  out_w = w;
+  if (lane < kTopK) {
+    p.topk_idx[t * kTopK + lane] = idx;
+    p.topk_w[t * kTopK + lane] = w;
+  }
+}
+
 __device__ __forceinline__ void route_token_any(const RouteParams& p, int t, int lane, int& out_idx, float& out_w) {
   if (p.method == kRouteDeepSeekV3)
     route_token(p, t, lane, out_idx, out_w);
+  else if (p.method == kRouteGiven)
+    route_token_given(p, t, lane, out_idx, out_w);
   else
     route_token_simple(p, t, lane, out_idx, out_w);
 }

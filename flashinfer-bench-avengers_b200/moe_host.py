@@ -72,6 +72,18 @@ class WorkspaceLayout(ctypes.Structure):
     ]
 
 
+class A2aLayout(ctypes.Structure):
+    _fields_ = [
+        ("total_bytes", ctypes.c_size_t),
+        ("send_slot", ctypes.c_size_t),
+        ("pick_row", ctypes.c_size_t),
+        ("slab_idx", ctypes.c_size_t),
+        ("slab_w", ctypes.c_size_t),
+        ("slab_scale", ctypes.c_size_t),
+        ("slab_rows", ctypes.c_size_t),
+    ]
+
+
 def _build_module():
     """This package's build.py, loaded by path (a top-level module named
     ``build`` could be another package's)."""
@@ -148,6 +160,22 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_run_noalloc.restype = ctypes.c_int
         lib.moe_b200_noalloc_read_status.argtypes = [ctypes.POINTER(ctypes.c_uint32), _P]
         lib.moe_b200_noalloc_read_status.restype = ctypes.c_int
+        lib.moe_b200_run_routed.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _P,
+                                            ctypes.c_size_t, _P]
+        lib.moe_b200_run_routed.restype = ctypes.c_int
+        lib.moe_b200_a2a_area_bytes.argtypes = [_I64, _I64]
+        lib.moe_b200_a2a_area_bytes.restype = ctypes.c_size_t
+        lib.moe_b200_a2a_get_layout.argtypes = [_I64, _I64, ctypes.POINTER(A2aLayout)]
+        lib.moe_b200_a2a_get_layout.restype = ctypes.c_int
+        lib.moe_b200_a2a_dispatch.argtypes = [_P, _P, _P, _P, _I64, _I64, _I64, ctypes.POINTER(ctypes.c_void_p),
+                                              ctypes.c_int, ctypes.c_int, ctypes.c_int, _P]
+        lib.moe_b200_a2a_dispatch.restype = ctypes.c_int
+        lib.moe_b200_a2a_combine.argtypes = [_P, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_void_p),
+                                             ctypes.c_int, ctypes.c_int, ctypes.c_int, _I64, _I64, _I64, _P, _P]
+        lib.moe_b200_a2a_combine.restype = ctypes.c_int
+        lib.moe_b200_a2a_read_status.argtypes = [_P, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int32),
+                                                 _P]
+        lib.moe_b200_a2a_read_status.restype = ctypes.c_int
         _lib = lib
         return lib
 
@@ -452,6 +480,126 @@ def ep_combine_shards(shard_workspace_ptrs: list[int], shards_per_rank: int, ran
                                                           int(num_tokens), output.data_ptr(), stream),
               "moe_b200_ep_combine_shards")
     return output
+
+
+def run_routed_ptrs(topk_idx_ptr: int, topk_w_ptr: int, top_k: int, hidden_ptr: int, hidden_scale_ptr: int,
+                    gemm1_weights, gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset: int,
+                    num_tokens: int, workspace: torch.Tensor, output: torch.Tensor | None = None) -> None:
+    """moe_b200_run_routed on device pointers (the rows of an all-to-all
+    receive slab): routing given as [T, top_k] ids / weights; with
+    ``output=None`` the fp32 combine rows stay in ``workspace``."""
+    for name, t, shape, dt in (("gemm1_weights", gemm1_weights, (E_LOCAL, 2 * I, H), torch.float8_e4m3fn),
+                               ("gemm1_weights_scale", gemm1_weights_scale, (E_LOCAL, GEMM1_OUT_BLOCKS, HIDDEN_BLOCKS),
+                                torch.float32),
+                               ("gemm2_weights", gemm2_weights, (E_LOCAL, H, I), torch.float8_e4m3fn),
+                               ("gemm2_weights_scale", gemm2_weights_scale, (E_LOCAL, HIDDEN_BLOCKS, INTER_BLOCKS),
+                                torch.float32)):
+        _check(isinstance(t, torch.Tensor) and t.is_cuda and tuple(t.shape) == shape and t.dtype == dt
+               and t.is_contiguous(), f"{name} must be a contiguous CUDA {dt} tensor of shape {shape}")
+    if output is not None:
+        _check(output.dtype == torch.bfloat16 and tuple(output.shape) == (int(num_tokens), H)
+               and output.is_contiguous(), f"output must be a contiguous bf16 [T, {H}] tensor")
+    dev = gemm1_weights.device
+    with torch.cuda.device(dev):
+        code = load_library().moe_b200_run_routed(
+            int(topk_idx_ptr), int(topk_w_ptr), int(top_k), int(hidden_ptr), int(hidden_scale_ptr),
+            gemm1_weights.data_ptr(), gemm1_weights_scale.data_ptr(), gemm2_weights.data_ptr(),
+            gemm2_weights_scale.data_ptr(), int(local_expert_offset), int(num_tokens),
+            output.data_ptr() if output is not None else None, workspace.data_ptr(), workspace.numel(),
+            torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_run_routed")
+
+
+def run_routed(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states, hidden_states_scale, gemm1_weights,
+               gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
+               output: torch.Tensor | None = None, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """The layer with given routing: topk_idx int32 / topk_w fp32 [T, top_k]
+    (global expert ids, final weights). Returns ``output`` (allocated when None)."""
+    _check(topk_idx.is_cuda and topk_idx.dtype == torch.int32 and topk_idx.dim() == 2 and topk_idx.is_contiguous(),
+           "topk_idx must be a contiguous CUDA int32 [T, top_k] tensor")
+    T, k = topk_idx.shape
+    _check(1 <= k <= TOP_K, f"top_k must be 1..{TOP_K}")
+    _check(topk_w.is_cuda and topk_w.dtype == torch.float32 and tuple(topk_w.shape) == (T, k)
+           and topk_w.is_contiguous(), "topk_w must be a contiguous CUDA float32 tensor shaped like topk_idx")
+    _check(hidden_states.is_cuda and hidden_states.dtype == torch.float8_e4m3fn and tuple(hidden_states.shape) == (T, H)
+           and hidden_states.is_contiguous(), f"hidden_states must be a contiguous float8_e4m3fn [T, {H}] tensor")
+    hs_scale = hidden_states_scale.contiguous()
+    _check(hs_scale.dtype == torch.float32 and tuple(hs_scale.shape) == (HIDDEN_BLOCKS, T),
+           f"hidden_states_scale must be float32 [{HIDDEN_BLOCKS}, T]")
+    dev = topk_idx.device
+    if output is None:
+        output = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    if T == 0:
+        return output
+    ws = workspace if workspace is not None else get_workspace(T, dev)
+    run_routed_ptrs(topk_idx.data_ptr(), topk_w.data_ptr(), k, hidden_states.data_ptr(), hs_scale.data_ptr(),
+                    gemm1_weights, gemm1_weights_scale.contiguous(), gemm2_weights, gemm2_weights_scale.contiguous(),
+                    local_expert_offset, T, ws, output)
+    return output
+
+
+def a2a_area_bytes(max_tokens: int, recv_capacity: int) -> int:
+    return int(load_library().moe_b200_a2a_area_bytes(int(max_tokens), int(recv_capacity)))
+
+
+def a2a_layout(max_tokens: int, recv_capacity: int) -> A2aLayout:
+    out = A2aLayout()
+    _raise_on(load_library().moe_b200_a2a_get_layout(int(max_tokens), int(recv_capacity), ctypes.byref(out)),
+              "moe_b200_a2a_get_layout")
+    return out
+
+
+def _ptr_array(ptrs) -> ctypes.Array:
+    return (ctypes.c_void_p * len(ptrs))(*[ctypes.c_void_p(int(p)) for p in ptrs])
+
+
+def a2a_dispatch(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states: torch.Tensor,
+                 hidden_states_scale: torch.Tensor, max_tokens: int, recv_capacity: int, rank_area_ptrs: list[int],
+                 rank: int, shards_per_rank: int) -> None:
+    """moe_b200_a2a_dispatch of this rank's T tokens (picks from moe_b200_route)."""
+    T = int(hidden_states.shape[0])
+    _check(tuple(topk_idx.shape) == (T, TOP_K) and topk_idx.dtype == torch.int32 and topk_idx.is_contiguous(),
+           "topk_idx must be int32 [T, 8]")
+    _check(tuple(topk_w.shape) == (T, TOP_K) and topk_w.dtype == torch.float32 and topk_w.is_contiguous(),
+           "topk_w must be float32 [T, 8]")
+    _check(hidden_states.dtype == torch.float8_e4m3fn and hidden_states.is_contiguous()
+           and tuple(hidden_states.shape) == (T, H), f"hidden_states must be e4m3 [T, {H}]")
+    _check(tuple(hidden_states_scale.shape) == (HIDDEN_BLOCKS, T) and hidden_states_scale.is_contiguous()
+           and hidden_states_scale.dtype == torch.float32, f"hidden_states_scale must be float32 [{HIDDEN_BLOCKS}, T]")
+    dev = hidden_states.device
+    with torch.cuda.device(dev):
+        code = load_library().moe_b200_a2a_dispatch(
+            topk_idx.data_ptr(), topk_w.data_ptr(), hidden_states.data_ptr(), hidden_states_scale.data_ptr(), T,
+            int(max_tokens), int(recv_capacity), _ptr_array(rank_area_ptrs), int(rank), len(rank_area_ptrs),
+            int(shards_per_rank), torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_a2a_dispatch")
+
+
+def a2a_combine(topk_idx: torch.Tensor, shard_workspace_ptrs: list[int], rank_area_ptrs: list[int], rank: int,
+                shards_per_rank: int, max_tokens: int, recv_capacity: int, output: torch.Tensor) -> torch.Tensor:
+    """moe_b200_a2a_combine into this rank's bf16 output [T, 7168]."""
+    T = int(topk_idx.shape[0])
+    _check(output.is_cuda and output.dtype == torch.bfloat16 and output.is_contiguous()
+           and tuple(output.shape) == (T, H), f"output must be a contiguous bf16 [T, {H}] tensor")
+    dev = output.device
+    with torch.cuda.device(dev):
+        code = load_library().moe_b200_a2a_combine(
+            topk_idx.data_ptr(), _ptr_array(shard_workspace_ptrs), _ptr_array(rank_area_ptrs), int(rank),
+            len(rank_area_ptrs), int(shards_per_rank), T, int(max_tokens), int(recv_capacity), output.data_ptr(),
+            torch.cuda.current_stream(dev).cuda_stream)
+    _raise_on(code, "moe_b200_a2a_combine")
+    return output
+
+
+def a2a_read_status(area: torch.Tensor) -> tuple[int, int]:
+    """(status bits, rows received) of this rank's last all-to-all call."""
+    st, rows = ctypes.c_uint32(0), ctypes.c_int32(0)
+    with torch.cuda.device(area.device):
+        code = load_library().moe_b200_a2a_read_status(area.data_ptr(), ctypes.byref(st), ctypes.byref(rows),
+                                                         torch.cuda.current_stream(area.device).cuda_stream)
+    if code not in (0, 7):
+        _raise_on(code, "moe_b200_a2a_read_status")
+    return int(st.value), int(rows.value)
 
 
 def run_noalloc(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,

@@ -353,6 +353,77 @@ MOE_B200_API int moe_b200_ipc_get_handle(const void* buffer, void* handle);
 MOE_B200_API int moe_b200_ipc_open_handle(const void* handle, void** buffer);
 MOE_B200_API int moe_b200_ipc_close_handle(void* buffer);
 
+/*
+ * moe_b200_run with the routing given by the caller instead of computed:
+ * topk_idx / topk_w are [T, top_k] (top_k 1..8) global expert ids and final
+ * weights (no routed_scaling_factor is applied); ids outside
+ * [local_expert_offset, local_expert_offset + 32) contribute nothing. The
+ * permutation, GEMMs and combine are those of moe_b200_run, on the same
+ * workspace size. Used on the rows an all-to-all dispatch delivered (below);
+ * the reference has no counterpart (it always routes itself,
+ * solution/cuda/main.cpp:50-57). Alignment: topk_idx and topk_w 4 bytes.
+ */
+MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_w, int top_k,
+                                     const void* hidden_states, const float* hidden_states_scale,
+                                     const void* gemm1_weights, const float* gemm1_weights_scale,
+                                     const void* gemm2_weights, const float* gemm2_weights_scale,
+                                     int64_t local_expert_offset, int64_t num_tokens, void* output,
+                                     void* workspace, size_t workspace_bytes, void* stream);
+
+/*
+ * Token-parallel expert parallelism: every rank holds its own tokens and owns
+ * shards_per_rank = 8 / world 32-expert shards (rank q owns global experts
+ * [32 S q, 32 S (q + 1))). No reference counterpart (the reference is
+ * single-GPU and has no all-to-all).
+ *
+ * Per rank, an area of moe_b200_a2a_area_bytes(max_tokens, recv_capacity)
+ * bytes that every rank maps (e.g. moe_b200_ep_buffer_alloc + IPC handles),
+ * zero before the first call; max_tokens and recv_capacity must be the same
+ * on every rank. recv_capacity rows bound what one rank can receive: world *
+ * max_tokens * 8 can never overflow. One layer call, on every rank, on one
+ * stream:
+ *   1. moe_b200_route on this rank's T tokens -> topk_idx, topk_w [T, 8];
+ *   2. moe_b200_a2a_dispatch: every pick (token row e4m3, its 56 block
+ *      scales, the expert id and weight) is stored into the receive slab of
+ *      the rank owning the expert, rows ordered by (source rank, token, pick);
+ *   3. per owned shard s: moe_b200_run_routed(slab_idx, slab_w, 1, slab_rows,
+ *      slab_scale, weights of s, 32 (S rank + s), recv_capacity, NULL,
+ *      workspace of s, ...), with the slab offsets of moe_b200_a2a_get_layout
+ *      (rows past the received count hold no pick);
+ *   4. moe_b200_a2a_combine: each own token's bf16 output is the fp32 sum, in
+ *      pick order, of its picks' combine rows read from the owning ranks'
+ *      workspaces (shard_workspaces: world * S, rank-major), rounded once.
+ * Every rank must make all four steps for every call, also with T = 0. The
+ * waits on peers give up after one second; then the area's status word gets
+ * bit 1 << 7 and every rank's area is poisoned (bit 1 << 8 on later calls)
+ * until each rank zeroes the first MOE_B200_A2A_COUNTER_BYTES of its area
+ * after a device synchronisation and a host barrier. A slab too small for
+ * what a rank received sets bit 1 << 9 (those picks are dropped).
+ * moe_b200_a2a_read_status reads the status word and the received row count
+ * (synchronises the stream).
+ */
+#define MOE_B200_A2A_COUNTER_BYTES 512
+typedef struct moe_b200_a2a_layout {
+  size_t total_bytes;
+  size_t send_slot;   /* int32[max_tokens, 8] index of each pick among this rank's picks for its destination */
+  size_t pick_row;    /* int32[max_tokens, 8] row of each pick in its destination's slab, -1 if none */
+  size_t slab_idx;    /* int32[recv_capacity] global expert id of each received row (none past the count) */
+  size_t slab_w;      /* fp32[recv_capacity] routing weight of each received row */
+  size_t slab_scale;  /* fp32[56, recv_capacity] block scales of the received rows */
+  size_t slab_rows;   /* e4m3[recv_capacity, 7168] received token rows */
+} moe_b200_a2a_layout;
+MOE_B200_API size_t moe_b200_a2a_area_bytes(int64_t max_tokens, int64_t recv_capacity);
+MOE_B200_API int moe_b200_a2a_get_layout(int64_t max_tokens, int64_t recv_capacity, moe_b200_a2a_layout* out);
+MOE_B200_API int moe_b200_a2a_dispatch(const int32_t* topk_idx, const float* topk_w, const void* hidden_states,
+                                       const float* hidden_states_scale, int64_t num_tokens, int64_t max_tokens,
+                                       int64_t recv_capacity, void* const* rank_areas, int rank, int world,
+                                       int shards_per_rank, void* stream);
+MOE_B200_API int moe_b200_a2a_combine(const int32_t* topk_idx, void* const* shard_workspaces,
+                                      void* const* rank_areas, int rank, int world, int shards_per_rank,
+                                      int64_t num_tokens, int64_t max_tokens, int64_t recv_capacity,
+                                      void* output, void* stream);
+MOE_B200_API int moe_b200_a2a_read_status(const void* area, uint32_t* status, int32_t* recv_rows, void* stream);
+
 /* ABI version of this header (bumped on any signature or struct layout change). */
 MOE_B200_API int moe_b200_abi_version(void);
 

@@ -207,7 +207,7 @@ def expert_forward(a_rows: torch.Tensor, w13_e, s13_e, w2_e, s2_e, return_c: boo
 def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
                 routed_scaling_factor, token_subset=None, experts=None, return_fp32=False,
-                routing_method=ROUTING_DEEPSEEK_V3, top_k=TOP_K):
+                routing_method=ROUTING_DEEPSEEK_V3, top_k=TOP_K, given=None):
     """Full layer on the CPU. Returns bf16 [T, 7168] (or fp32 with return_fp32).
 
     token_subset: optional 1-D index tensor; only those rows are computed
@@ -215,8 +215,19 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     experts: optional iterable of local expert ids to include (the others
     are skipped), used for bounded CPU-baseline samples.
     routing_method / top_k: another routing method of the family (route_method).
+    given: optional (topk_idx [T, k], topk_w [T, k]) used instead of routing
+    (global expert ids and final weights, as moe_b200_run_routed takes them).
     """
-    topk_idx, topk_w = route_method(routing_logits, routing_bias, routed_scaling_factor, routing_method, top_k)
+    if given is not None:
+        gi = torch.as_tensor(given[0]).to("cpu", torch.int64)
+        gw = torch.as_tensor(given[1]).to("cpu", torch.float32)
+        T0, k0 = gi.shape
+        topk_idx = torch.full((T0, TOP_K), -(1 << 30), dtype=torch.int64)
+        topk_w = torch.zeros(T0, TOP_K, dtype=torch.float32)
+        topk_idx[:, :k0] = gi
+        topk_w[:, :k0] = gw
+    else:
+        topk_idx, topk_w = route_method(routing_logits, routing_bias, routed_scaling_factor, routing_method, top_k)
     hs, hs_scale = hidden_states, hidden_states_scale
     if token_subset is not None:
         sub = torch.as_tensor(token_subset, dtype=torch.int64)
@@ -260,3 +271,88 @@ def output_close(out: torch.Tensor, ref: torch.Tensor, rel: float = 1e-2, frac: 
     tol = rel * ref_max
     matched = float((err <= tol).float().mean()) if r.numel() else 1.0
     return matched >= frac, matched, float(err.max()) if r.numel() else 0.0, ref_max
+
+
+# ---------------------------------------------------------------------------
+# Token-parallel expert parallelism (all-to-all dispatch / combine). The
+# reference is single-GPU and has no such step; this restates the semantics
+# the library's all-to-all kernels implement, so that tests can check them:
+# rank q of W owns S = 8 / W shards, i.e. global experts [32 S q, 32 S (q+1)).
+# ---------------------------------------------------------------------------
+def a2a_dest(expert: torch.Tensor, shards_per_rank: int) -> torch.Tensor:
+    """Destination rank of each global expert id (-1 for ids outside 0..255)."""
+    e = expert.to(torch.int64)
+    d = torch.div(e, E_LOCAL * shards_per_rank, rounding_mode="floor")
+    return torch.where((e >= 0) & (e < E_GLOBAL), d, torch.full_like(d, -1))
+
+
+def a2a_plan(topk_idx: torch.Tensor, world: int, shards_per_rank: int):
+    """Numbering of one rank's picks: (send_slot int64 [T, 8], counts int64
+    [W]). send_slot is the index of a pick among this rank's picks for the
+    same destination in (token, pick) order, -1 for none."""
+    dest = a2a_dest(topk_idx.reshape(-1), shards_per_rank)
+    slot = torch.full_like(dest, -1)
+    counts = torch.zeros(world, dtype=torch.int64)
+    for q in range(world):
+        hit = dest == q
+        slot[hit] = torch.arange(int(hit.sum()), dtype=torch.int64)
+        counts[q] = int(hit.sum())
+    return slot.view(topk_idx.shape), counts
+
+
+def a2a_slab(src_rank: int, count_matrix: torch.Tensor, dest_rank: int) -> int:
+    """First slab row of source src_rank's picks on dest_rank: the picks of
+    lower source ranks come first (count_matrix[src, dst])."""
+    return int(count_matrix[:src_rank, dest_rank].sum())
+
+
+@torch.no_grad()
+def token_parallel_forward(tokens: list, shard_weights: dict, world: int):
+    """The whole token-parallel layer on the CPU, every rank at once.
+
+    tokens[r]: rank r's dict (routing_logits, routing_bias, hidden_states,
+    hidden_states_scale, routed_scaling_factor). shard_weights[offset] =
+    (w13, s13, w2, s2) for the 8 shards. Returns (outputs, slabs): rank r's
+    fp32 output [T_r, 7168], and per destination q the received rows in slab
+    order as (source rank, token, pick, expert, weight). Each output row is
+    the sum, in pick order, of w * expert(x) over the token's picks.
+    """
+    S = (E_GLOBAL // E_LOCAL) // world
+    routes = [route(t["routing_logits"], t["routing_bias"], t["routed_scaling_factor"]) for t in tokens]
+    plans = [a2a_plan(idx, world, S) for idx, _ in routes]
+    M = torch.stack([c for _, c in plans])                     # [src, dst]
+    slabs = [[None] * int(M[:, q].sum()) for q in range(world)]
+    for r, ((idx, w), (slot, _)) in enumerate(zip(routes, plans)):
+        dest = a2a_dest(idx.reshape(-1), S).view(idx.shape)
+        for t in range(idx.shape[0]):
+            for k in range(TOP_K):
+                q = int(dest[t, k])
+                if q >= 0:
+                    slabs[q][a2a_slab(r, M, q) + int(slot[t, k])] = (r, t, k, int(idx[t, k]), float(w[t, k]))
+    # each destination runs its shards on its slab rows (one given pick each)
+    contrib = {}
+    for q in range(world):
+        rows = slabs[q]
+        if not rows:
+            continue
+        hs = torch.stack([tokens[r]["hidden_states"][t] for r, t, _, _, _ in rows])
+        sc = torch.stack([tokens[r]["hidden_states_scale"][:, t] for r, t, _, _, _ in rows], dim=1)
+        gi = torch.tensor([[e] for _, _, _, e, _ in rows], dtype=torch.int64)
+        gw = torch.tensor([[wt] for _, _, _, _, wt in rows], dtype=torch.float32)
+        for s in range(S):
+            off = E_LOCAL * (q * S + s)
+            w13, s13, w2, s2 = shard_weights[off]
+            y = moe_forward(None, None, hs, sc, w13, s13, w2, s2, off, 1.0, return_fp32=True, given=(gi, gw))
+            for j, (r, t, k, e, _) in enumerate(rows):
+                if off <= e < off + E_LOCAL:
+                    contrib[(r, t, k)] = y[j]
+    outs = []
+    for r, t_in in enumerate(tokens):
+        T = t_in["hidden_states"].shape[0]
+        out = torch.zeros(T, H, dtype=torch.float32)
+        for t in range(T):
+            for k in range(TOP_K):
+                if (r, t, k) in contrib:
+                    out[t] = out[t] + contrib[(r, t, k)]
+        outs.append(out)
+    return outs, slabs

@@ -130,7 +130,7 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 7
+    assert lib.moe_b200_abi_version() == 8
 
 
 def test_widened_entry_points_reject_bad_arguments_without_a_device(lib):
@@ -195,3 +195,40 @@ def test_ep_and_ipc_entry_points_reject_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_ipc_open_handle(p, None) == 1
     assert lib.moe_b200_ipc_close_handle(None) == 0
     assert lib.moe_b200_noalloc_read_status(None, None) == 1
+
+
+def test_token_parallel_entry_points_reject_bad_arguments_without_a_device(lib):
+    """The routed layer and the all-to-all entry points check their arguments
+    before any CUDA call."""
+    P = ctypes.c_void_p
+    buf = ctypes.create_string_buffer(4096 + 256)
+    base = (ctypes.addressof(buf) + 255) // 256 * 256
+    p = P(base)
+    big = 1 << 40
+    # the routed layer: given ids and weights are required, top_k 1..8
+    assert lib.moe_b200_run_routed(None, p, 1, p, p, p, p, p, p, 0, 4, p, p, big, None) == 1
+    assert lib.moe_b200_run_routed(p, None, 1, p, p, p, p, p, p, 0, 4, p, p, big, None) == 1
+    assert lib.moe_b200_run_routed(p, p, 0, p, p, p, p, p, p, 0, 4, p, p, big, None) == 1
+    assert lib.moe_b200_run_routed(p, p, 9, p, p, p, p, p, p, 0, 4, p, p, big, None) == 1
+    assert lib.moe_b200_run_routed(P(base + 2), p, 1, p, p, p, p, p, p, 0, 4, p, p, big, None) == 2
+    assert lib.moe_b200_run_routed(p, p, 1, p, p, p, p, p, p, 0, 4, p, p, 16, None) == 3
+    assert lib.moe_b200_run_routed(p, p, 1, p, p, p, p, p, p, 0, 0, p, p, 16, None) == 0
+    # the given-routing rule is not one of the public routing methods
+    assert lib.moe_b200_route_method(6, 1, p, p, 0, 4, 1.0, p, p, None) == 1
+    assert lib.moe_b200_run_routing(6, 1, p, p, 0, p, p, p, p, p, p, 0, 1.0, 4, p, p, big, None) == 1
+    # all-to-all: world x shards must cover the 8 shards, sizes in range
+    arr = (P * 8)(*([p] * 8))
+    assert lib.moe_b200_a2a_area_bytes(16, 128) > 512
+    assert lib.moe_b200_a2a_area_bytes(16, 0) == 0
+    assert lib.moe_b200_a2a_area_bytes(-1, 128) == 0
+    assert lib.moe_b200_a2a_dispatch(p, p, p, p, 4, 16, 128, arr, 0, 2, 2, None) == 1    # 2 x 2 != 8
+    assert lib.moe_b200_a2a_dispatch(p, p, p, p, 17, 16, 128, arr, 0, 2, 4, None) == 1   # T > max_tokens
+    assert lib.moe_b200_a2a_dispatch(p, p, p, p, 4, 16, 128, arr, 2, 2, 4, None) == 1    # rank out of range
+    assert lib.moe_b200_a2a_dispatch(None, p, p, p, 4, 16, 128, arr, 0, 2, 4, None) == 1
+    assert lib.moe_b200_a2a_dispatch(p, p, P(base + 8), p, 4, 16, 128, arr, 0, 2, 4, None) == 2
+    mis = (P * 8)(*([P(base + 16)] * 8))
+    assert lib.moe_b200_a2a_dispatch(p, p, p, p, 4, 16, 128, mis, 0, 2, 4, None) == 2
+    assert lib.moe_b200_a2a_combine(p, arr, arr, 0, 2, 4, 4, 16, 128, P(base + 8), None) == 2
+    assert lib.moe_b200_a2a_combine(p, None, arr, 0, 2, 4, 4, 16, 128, p, None) == 1
+    assert lib.moe_b200_a2a_combine(p, arr, arr, 0, 8, 2, 4, 16, 128, p, None) == 1     # 8 x 2 != 8
+    assert lib.moe_b200_a2a_read_status(None, None, None, None) == 1
