@@ -30,6 +30,10 @@ Extra points:
   work, "strong" scaling) and `stress` (config 4: T=16384 with Zipf(1.2)
   expert popularity, the same 8-shard layout; per-shard and per-rank times,
   the per-rank maximum is the figure). Both carry their own ep_check.
+  `token_parallel_t8192`: the same T=8192 batch split over the ranks (each
+  rank its own 8192/N tokens), all-to-all dispatch and combine
+  (TokenParallelEP), checked against the expert-parallel sum of every
+  shard's independent run.
 * N=1 only: the decode sweep T in {1,4,16,64} (config 1; T=1 uses the first
   seed >= 1234 whose token picks a local expert, stated in the point), the
   prefill point (config 2, T=4096 with 4 hot experts), the reference
@@ -721,6 +725,95 @@ def all_shard_point(T: int, variant: str, desc: str, steps: int, warmup: int, fl
     return res
 
 
+def token_parallel_point(T: int, steps: int, warmup: int, peaks, device, group, world: int, rank: int) -> dict:
+    """Token-parallel expert parallelism on the batch of config 3: rank r
+    holds rows [rT/N, (r+1)T/N) of the same T-token batch (each rank its own
+    tokens) and owns 8/N shards; one step is routing, the all-to-all
+    dispatch, the shards on the received rows and the all-to-all combine
+    (TokenParallelEP), replayed from a CUDA graph; time = max over ranks.
+    Checked against the expert-parallel sum of independent runs of every
+    shard on the whole batch (operator tolerance), status words clear."""
+    import expert_parallel
+    import moe_host
+    import torch.distributed as dist
+
+    spr = NUM_SHARDS // world
+    offsets = [32 * (rank * spr + s) for s in range(spr)]
+    full = [workloads.make_inputs(T, SEED, device, "uniform", off, 2.5, weight_seed=SEED + 1 + off // 32)
+            for off in offsets]
+    lo, hi = T * rank // world, T * (rank + 1) // world
+    f = full[0]
+    tok = {"routing_logits": f["routing_logits"][lo:hi].contiguous(), "routing_bias": f["routing_bias"],
+           "hidden_states": f["hidden_states"][lo:hi].contiguous(),
+           "hidden_states_scale": f["hidden_states_scale"][:, lo:hi].contiguous(), "routed_scaling_factor": 2.5}
+    shards = [(i["gemm1_weights"], i["gemm1_weights_scale"], i["gemm2_weights"], i["gemm2_weights_scale"])
+              for i in full]
+    Tmax = max(T * (q + 1) // world - T * q // world for q in range(world))
+    tp = expert_parallel.TokenParallelEP(Tmax, device, group)
+    out = torch.empty(hi - lo, 7168, dtype=torch.bfloat16, device=device)
+    try:
+        for _ in range(warmup):
+            tp.forward(tok, shards, out)
+        torch.cuda.synchronize()
+        stream = torch.cuda.Stream(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(stream):
+            with torch.cuda.graph(graph, stream=stream):
+                tp.forward(tok, shards, out)
+        for _ in range(warmup):
+            graph.replay()
+        torch.cuda.synchronize()
+        if group is not None:
+            dist.barrier(group=group)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+        for i in range(steps):
+            starts[i].record()
+            graph.replay()
+            ends[i].record()
+        torch.cuda.synchronize()
+        if group is not None:
+            dist.barrier(group=group)
+        us = statistics.mean(a.elapsed_time(b) for a, b in zip(starts, ends)) * 1e3
+        status = tp.status()
+        recv = tp.slab_rows()
+        del graph
+    finally:
+        tp.close()
+    # reference: every shard's independent run on the whole batch, summed over ranks
+    ref = None
+    for i in full:
+        part = moe_host.run(*workloads.as_args(i)).float()
+        ref = part if ref is None else ref + part
+    if world > 1:
+        dist.all_reduce(ref, group=group)
+    ref = ref[lo:hi]
+    err = (out.float() - ref).abs()
+    amax = float(ref.abs().max())
+    matched = float((err <= REL_TOL * amax).float().mean())
+    mine = torch.tensor([us, float(status), matched, float(recv), float(hi - lo)], dtype=torch.float64, device=device)
+    if world > 1:
+        allm = [torch.zeros_like(mine) for _ in range(world)]
+        dist.all_gather(allm, mine, group=group)
+    else:
+        allm = [mine]
+    st = 0
+    for v in allm:
+        st |= int(v[1])
+    us_max = max(float(v[0]) for v in allm)
+    lf = layer_flops(T * 8)
+    return {"T": T, "variant": "uniform", "n_gpus": world, "shards_per_rank": spr,
+            "workload": "token-parallel EP: each rank holds 1/N of the config-3 batch, all-to-all dispatch "
+                        "and combine over NVLink",
+            "scaling": "strong (all 256 experts, the same 8192 tokens at every N)", "us_per_call": round(us_max, 2),
+            "layer_TFLOPs": round(lf / (us_max * 1e-6) / 1e12, 2),
+            "per_rank": [{"rank": q, "us_per_call": round(float(v[0]), 2), "tokens": int(v[4]),
+                          "rows_received": int(v[3])} for q, v in enumerate(allm)],
+            "check": {"status": st, "matched": round(min(float(v[2]) for v in allm), 6),
+                      "reference": "fp32 sum of independent moe_b200_run outputs of every shard on the whole batch",
+                      "tolerance": f"|err| <= {REL_TOL} * max|ref| on >= {MATCH_FRAC} of elements"}}
+
+
 # --------------------------------------------------------------------- main
 def main() -> None:
     ap = argparse.ArgumentParser()
@@ -918,6 +1011,8 @@ def main() -> None:
         line["stress"] = all_shard_point(
             16384, "zipf", "config4 stress: T=16384, Zipf(1.2) expert popularity, all 256 experts in 8 shards",
             max(3, n_extra // 2), warmup, flush, peaks, device, group, world, rank)
+        line["token_parallel_t8192"] = token_parallel_point(8192, max(3, n_extra // 2), warmup, peaks, device,
+                                                            group, world, rank)
     if extras and world == 1:
         line["cpu_baseline"] = cpu_oracle_time(inp)
         c0 = workloads.make_inputs(16, 0, device)

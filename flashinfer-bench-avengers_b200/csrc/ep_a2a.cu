@@ -472,9 +472,10 @@ int moe_b200_a2a_combine(const int32_t* topk_idx, void* const* shard_workspaces,
   if (st != MOE_B200_OK) return st;
   if (shard_workspaces == nullptr || (num_tokens > 0 && (!topk_idx || !output))) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(output) % 16 != 0) return MOE_B200_ERR_MISALIGNED;
-  // every shard's layer ran on recv_capacity rows
+  // every shard's layer ran on recv_capacity rows with one given pick each
   moe_b200_workspace_layout l;
-  if (moe_b200_get_workspace_layout(recv_capacity, &l) != MOE_B200_OK) return MOE_B200_ERR_INVALID_ARGUMENT;
+  if (moe_b200_get_routed_workspace_layout(recv_capacity, 1, &l) != MOE_B200_OK)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
   for (int q = 0; q < world * shards_per_rank; ++q) {
     uint8_t* ws = static_cast<uint8_t*>(shard_workspaces[q]);
     if (ws == nullptr) return MOE_B200_ERR_INVALID_ARGUMENT;

@@ -65,14 +65,16 @@ struct Layout {
   moe_b200_workspace_layout l;
 };
 
-moe_b200_workspace_layout make_layout(int64_t T) {
+// `picks` is the most local picks a token can have: 8 for the routing rules,
+// top_k when the caller gives the routing (moe_b200_run_routed).
+moe_b200_workspace_layout make_layout(int64_t T, int picks = kTopK) {
   moe_b200_workspace_layout l;
   std::memset(&l, 0, sizeof(l));
   const Plan plan = choose_plan(T);
   // Permuted-row capacity: every (token, local expert) pair, the padding of
   // 32 segments to kSegAlign rows, and one 128-row tile of slack so tile
   // reads that run past the last segment stay inside the buffers.
-  const size_t cap = (static_cast<size_t>(T) * kTopK + kSegAlign - 1) / kSegAlign * kSegAlign +
+  const size_t cap = (static_cast<size_t>(T) * picks + kSegAlign - 1) / kSegAlign * kSegAlign +
                      kExpertsLocal * kSegAlign + 128;
   size_t off = 0;
   l.counts = off;
@@ -84,10 +86,13 @@ moe_b200_workspace_layout make_layout(int64_t T) {
   off = align_up(off + (kExpertsLocal + 1) * sizeof(int));
   l.chunk_counts = off;
   off = align_up(off + static_cast<size_t>((T + kPermChunk - 1) / kPermChunk) * (kExpertsLocal + 1) * sizeof(int));
+  // the routing writes 8 slots per token whatever `picks` is (with 8 picks
+  // cap is larger than 8 T, so this is cap)
+  const size_t topk_slots = std::max(cap, static_cast<size_t>(T) * kTopK);
   l.topk_idx = off;
-  off = align_up(off + cap * sizeof(int32_t));
+  off = align_up(off + topk_slots * sizeof(int32_t));
   l.topk_w = off;
-  off = align_up(off + cap * sizeof(float));
+  off = align_up(off + topk_slots * sizeof(float));
   l.perm_tok = off;
   off = align_up(off + cap * sizeof(int32_t));
   l.perm_w = off;
@@ -440,6 +445,18 @@ int moe_b200_get_workspace_layout(int64_t num_tokens, moe_b200_workspace_layout*
   return MOE_B200_OK;
 }
 
+size_t moe_b200_routed_workspace_bytes(int64_t num_tokens, int top_k) {
+  if (num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS || top_k < 1 || top_k > kTopK) return 0;
+  return make_layout(num_tokens, top_k).total_bytes;
+}
+
+int moe_b200_get_routed_workspace_layout(int64_t num_tokens, int top_k, moe_b200_workspace_layout* out) {
+  if (out == nullptr || num_tokens < 0 || num_tokens > MOE_B200_MAX_TOKENS || top_k < 1 || top_k > kTopK)
+    return MOE_B200_ERR_INVALID_ARGUMENT;
+  *out = make_layout(num_tokens, top_k);
+  return MOE_B200_OK;
+}
+
 const char* moe_b200_status_string(int status) {
   switch (status) {
     case MOE_B200_OK: return "ok";
@@ -527,7 +544,7 @@ static int run_layer(const float* routing_logits, const void* routing_bias, int 
       !aligned(hidden_states_scale, 4) || !aligned(gemm1_weights_scale, 4) ||
       !aligned(gemm2_weights_scale, 4) || !aligned(workspace, kAlign))
     return MOE_B200_ERR_MISALIGNED;
-  const moe_b200_workspace_layout l = make_layout(num_tokens);
+  const moe_b200_workspace_layout l = make_layout(num_tokens, given_picks ? top_k : kTopK);
   if (workspace_bytes < l.total_bytes) return MOE_B200_ERR_WORKSPACE_TOO_SMALL;
   DeviceInfo di;
   int st = current_device_info(&di);

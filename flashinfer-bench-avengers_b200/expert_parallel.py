@@ -286,7 +286,7 @@ class TokenParallelEP:
         self.shards_per_rank = NUM_SHARDS // world
         self.cap = int(recv_capacity) if recv_capacity is not None else world * self.max_tokens * 8
         a2a = moe_host.a2a_area_bytes(self.max_tokens, self.cap)
-        layer = moe_host.workspace_bytes(self.cap)
+        layer = moe_host.routed_workspace_bytes(self.cap, 1)
         if a2a == 0 or layer == 0:
             raise ValueError(f"max_tokens {max_tokens} / recv_capacity {self.cap} out of range")
         self.a2a_bytes = _round256(a2a)

@@ -163,6 +163,10 @@ def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.moe_b200_run_routed.argtypes = [_P, _P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _I64, _I64, _P, _P,
                                             ctypes.c_size_t, _P]
         lib.moe_b200_run_routed.restype = ctypes.c_int
+        lib.moe_b200_routed_workspace_bytes.argtypes = [_I64, ctypes.c_int]
+        lib.moe_b200_routed_workspace_bytes.restype = ctypes.c_size_t
+        lib.moe_b200_get_routed_workspace_layout.argtypes = [_I64, ctypes.c_int, ctypes.POINTER(WorkspaceLayout)]
+        lib.moe_b200_get_routed_workspace_layout.restype = ctypes.c_int
         lib.moe_b200_a2a_area_bytes.argtypes = [_I64, _I64]
         lib.moe_b200_a2a_area_bytes.restype = ctypes.c_size_t
         lib.moe_b200_a2a_get_layout.argtypes = [_I64, _I64, ctypes.POINTER(A2aLayout)]
@@ -191,6 +195,18 @@ def _raise_on(code: int, what: str) -> None:
 
 def workspace_bytes(num_tokens: int) -> int:
     return int(load_library().moe_b200_workspace_bytes(int(num_tokens)))
+
+
+def routed_workspace_bytes(num_tokens: int, top_k: int) -> int:
+    """Workspace of moe_b200_run_routed for T tokens of at most top_k picks."""
+    return int(load_library().moe_b200_routed_workspace_bytes(int(num_tokens), int(top_k)))
+
+
+def routed_workspace_layout(num_tokens: int, top_k: int) -> WorkspaceLayout:
+    out = WorkspaceLayout()
+    _raise_on(load_library().moe_b200_get_routed_workspace_layout(int(num_tokens), int(top_k), ctypes.byref(out)),
+              "moe_b200_get_routed_workspace_layout")
+    return out
 
 
 def workspace_layout(num_tokens: int) -> WorkspaceLayout:
@@ -531,7 +547,9 @@ def run_routed(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states, hidd
         output = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     if T == 0:
         return output
-    ws = workspace if workspace is not None else get_workspace(T, dev)
+    if workspace is None:
+        workspace = torch.empty(routed_workspace_bytes(T, k), dtype=torch.uint8, device=dev)
+    ws = workspace
     run_routed_ptrs(topk_idx.data_ptr(), topk_w.data_ptr(), k, hidden_states.data_ptr(), hs_scale.data_ptr(),
                     gemm1_weights, gemm1_weights_scale.contiguous(), gemm2_weights, gemm2_weights_scale.contiguous(),
                     local_expert_offset, T, ws, output)

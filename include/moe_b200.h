@@ -362,7 +362,13 @@ MOE_B200_API int moe_b200_ipc_close_handle(void* buffer);
  * workspace size. Used on the rows an all-to-all dispatch delivered (below);
  * the reference has no counterpart (it always routes itself,
  * solution/cuda/main.cpp:50-57). Alignment: topk_idx and topk_w 4 bytes.
+ * Its workspace is moe_b200_routed_workspace_bytes(T, top_k) bytes (a token
+ * has at most top_k picks, so the permuted buffers are top_k / 8 of those of
+ * moe_b200_run), laid out as moe_b200_get_routed_workspace_layout gives.
  */
+MOE_B200_API size_t moe_b200_routed_workspace_bytes(int64_t num_tokens, int top_k);
+MOE_B200_API int moe_b200_get_routed_workspace_layout(int64_t num_tokens, int top_k,
+                                                      moe_b200_workspace_layout* out);
 MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_w, int top_k,
                                      const void* hidden_states, const float* hidden_states_scale,
                                      const void* gemm1_weights, const float* gemm1_weights_scale,
@@ -389,7 +395,8 @@ MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_
  *   3. per owned shard s: moe_b200_run_routed(slab_idx, slab_w, 1, slab_rows,
  *      slab_scale, weights of s, 32 (S rank + s), recv_capacity, NULL,
  *      workspace of s, ...), with the slab offsets of moe_b200_a2a_get_layout
- *      (rows past the received count hold no pick);
+ *      (rows past the received count hold no pick) and workspaces of
+ *      moe_b200_routed_workspace_bytes(recv_capacity, 1) bytes;
  *   4. moe_b200_a2a_combine: each own token's bf16 output is the fp32 sum, in
  *      pick order, of its picks' combine rows read from the owning ranks'
  *      workspaces (shard_workspaces: world * S, rank-major), rounded once.

@@ -53,7 +53,7 @@ def _shard_rows(tp, s, rows):
     """fp32 combine rows of shard workspace s for slab rows `rows` (local)."""
     import moe_host
 
-    lay = moe_host.workspace_layout(tp.cap)
+    lay = moe_host.routed_workspace_layout(tp.cap, 1)
     ws = tp.workspaces[s]
     rows = rows.to(ws.device)
     if tp.cap > 64:
