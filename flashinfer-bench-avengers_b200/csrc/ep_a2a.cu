@@ -49,7 +49,8 @@ constexpr int kA2aThreads = 256;
 constexpr int kA2aCtasPerSm = 2;                     // all CTAs resident: they wait for each other
 constexpr int kPlanThreads = 1024;
 
-// Counter block of a rank's area (bytes [0, 256)) and the count matrix.
+// Counter block of a rank's area: counters in bytes [0, 256), the count
+// matrix in [256, 512).
 struct A2aCounters {
   static constexpr size_t kFlagsDispatch = 0;   // int32[8]: call announced by each source rank (plan)
   static constexpr size_t kDoneDispatch = 32;   // int32: CTAs (all ranks) that finished writing into this slab

@@ -175,6 +175,8 @@ def _worker(rank: int, world: int, port: int, sizes, results):
                 r = wl.make_routing_inputs(T_list[q], 500 + q, dev)
                 hs, sc = wl.make_hidden(T_list[q], 500 + q, dev)
                 toks.append(dict(r, hidden_states=hs, hidden_states_scale=sc))
+            for q in range(1, world):   # one model: every rank routes with the same bias
+                toks[q]["routing_bias"] = toks[0]["routing_bias"]
             Ttot = sum(T_list)
             # this rank's shard weights: every expert any token of any rank picks
             allr = torch.cat([toks[q]["routing_logits"] for q in range(world)])
