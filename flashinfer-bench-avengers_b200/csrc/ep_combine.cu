@@ -15,15 +15,19 @@
 //      rank's output and into the output staging area of every other rank
 //      (plain stores to peer memory) -- reduce-scatter and all-gather in one
 //      pass, with the sum formed before the single bf16 rounding;
-//   3. count this CTA's slice as written on every rank (release reduction at
-//      system scope), wait (bounded) until every CTA of every rank has
-//      written into this rank's staging area, and copy the other ranks' rows
-//      to the caller's output.
+//   3. count this CTA locally (after a system-scope fence over its peer
+//      stores); the last CTA of the rank to finish tells every rank with one
+//      release reduction at system scope; wait (bounded) until every rank
+//      has told this rank, and copy the other ranks' rows from the staging
+//      area to the caller's output.
 // With one rank (all shards on one GPU) only the reduction runs, straight
 // into the output, and the counters are not touched.
-// Counters only grow (the call number is kept in the EP area), so nothing
-// has to be cleared between calls and the sequence can be captured in a CUDA
-// graph. No multicast and no library kernel touches peer memory; every wait
+// The call number grows (it is kept in the EP area); the per-call counters
+// are cleared by the last CTA of each call, once no CTA of the call still
+// waits and before this rank can announce the next call, so nothing has to
+// be cleared between calls, the grid may follow the token count, and the
+// sequence can be captured in a CUDA graph. No multicast and no library
+// kernel touches peer memory; every wait
 // gives up after one second with a status bit instead of hanging. A wait that
 // gives up leaves the ranks' counters out of step, so it also marks every
 // rank's area as poisoned: every later combine on those areas returns at once
@@ -58,10 +62,11 @@ constexpr int kEpCtasPerSm = 2;
 // them in the same place. Bytes [0, kStage) are the counter block.
 struct EpArea {
   static constexpr size_t kFlags = 0;       // int32[kEpMaxRanks]: call number announced by each rank
-  static constexpr size_t kDone = 64;       // int32: CTAs (of all ranks) that wrote into this staging
-  static constexpr size_t kFinished = 68;   // int32: CTAs of this rank that finished a call
+  static constexpr size_t kDone = 64;       // int32: ranks that finished writing into this staging (this call)
+  static constexpr size_t kFinished = 68;   // int32: CTAs of this rank that finished this call
   static constexpr size_t kCalls = 72;      // int32: completed calls of this rank
   static constexpr size_t kPoison = 76;     // int32: nonzero once a combine on these areas gave up a wait
+  static constexpr size_t kWritten = 80;    // int32: CTAs of this rank that finished writing (this call)
   static constexpr size_t kStage = 256;     // bf16[T, 7168] output staging
 };
 static_assert(EpArea::kStage == MOE_B200_EP_COUNTER_BYTES, "counter block size in the header");
@@ -87,6 +92,12 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
 
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 // Spins (bounded) until *p has reached target. The counters only grow and
@@ -215,18 +226,22 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
       if (q != p.rank) store_quads(p.area[q] + EpArea::kStage, t, j, o);
   }
 
-  // ---- 3. count this CTA's slice on every rank, wait for all, copy the
-  //         other ranks' rows out of the staging area -----------------------
+  // ---- 3. count this CTA locally; the last CTA of this rank to finish
+  //         writing tells every rank (one release per peer); wait until every
+  //         rank has written this rank's staging, copy the other ranks' rows
+  //         out of it -------------------------------------------------------
   __syncthreads();
-  if (threadIdx.x < W) {
-    __threadfence_system();
-    red_release_sys_add(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kDone), 1);
-  }
-  if (threadIdx.x == 0 &&
-      !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone),
-                     call * static_cast<uint32_t>(W) * gridDim.x)) {
-    give_up(p);
-    s_ok = 0;
+  if (threadIdx.x == 0) {
+    __threadfence_system();   // this CTA's peer stores are visible system-wide
+    const int before = atom_add_acq_rel_gpu(reinterpret_cast<int*>(mine + EpArea::kWritten), 1);
+    if (before == static_cast<int>(gridDim.x) - 1) {
+      __threadfence_system();
+      for (int q = 0; q < W; ++q) red_release_sys_add(reinterpret_cast<int*>(p.area[q] + EpArea::kDone), 1);
+    }
+    if (!wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kDone), static_cast<uint32_t>(W))) {
+      give_up(p);
+      s_ok = 0;
+    }
   }
   __syncthreads();
   if (s_ok) {
@@ -240,13 +255,20 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
       out16[k] = stage[k];
     }
   }
-  // The last CTA of this rank to finish advances the call number (every CTA
-  // has read it by then).
+  // The last CTA of this rank to finish clears the per-call counters and
+  // advances the call number: every CTA has passed its waits by then, and no
+  // peer writes this area for the next call before this rank announces it.
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    const uint32_t f = atomicAdd(reinterpret_cast<unsigned int*>(mine + EpArea::kFinished), 1u) + 1u;
-    if (f == call * gridDim.x) *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) = call;
+    const int f = atom_add_acq_rel_gpu(reinterpret_cast<int*>(mine + EpArea::kFinished), 1) + 1;
+    if (f == static_cast<int>(gridDim.x)) {
+      *reinterpret_cast<volatile int*>(mine + EpArea::kWritten) = 0;
+      *reinterpret_cast<volatile int*>(mine + EpArea::kDone) = 0;
+      *reinterpret_cast<volatile int*>(mine + EpArea::kFinished) = 0;
+      __threadfence();
+      *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) = call;
+    }
   }
 }
 
@@ -300,15 +322,19 @@ int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_ran
   p.world = world;
   p.sources = sources;
   p.num_tokens = static_cast<int>(num_tokens);
-  // The grid is the same for every call and rank (the ranks' GPUs are the
-  // same model): the counters accumulate W x (CTAs per call) per call, so the
-  // arithmetic must not change between calls with different token counts.
+  // One thread per reduced item (a row's column quads j and 896 + j), at most
+  // two CTAs per SM (all resident at once: they wait on the peers). The
+  // per-call counters are cleared at the end of every call, so the grid may
+  // differ between calls.
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     return MOE_B200_ERR_CUDA;
+  const int64_t rows_per_rank = (num_tokens + world - 1) / world;
+  const int64_t want = (rows_per_rank * (kHidden / 8) + kEpThreads - 1) / kEpThreads;
+  const int grid = static_cast<int>(want < kEpCtasPerSm * sms ? (want > 0 ? want : 1) : kEpCtasPerSm * sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (launch_kernel(ep_combine_kernel, kEpCtasPerSm * sms, kEpThreads, 0, s, true, p) != cudaSuccess)
+  if (launch_kernel(ep_combine_kernel, grid, kEpThreads, 0, s, true, p) != cudaSuccess)
     return MOE_B200_ERR_CUDA;
   return MOE_B200_OK;
 }

@@ -39,6 +39,14 @@ struct Plan {
   bool token_major;  // prefill: token-major GEMMs (gemm_tm_sm100.cu)
 };
 
+// K splits of the decode GEMMs (work units per (expert, row block)).
+#ifndef MOE_B200_DECODE_G1_SPLITS
+#define MOE_B200_DECODE_G1_SPLITS 4
+#endif
+#ifndef MOE_B200_DECODE_G2_SPLITS
+#define MOE_B200_DECODE_G2_SPLITS 2
+#endif
+
 // From this many tokens per call the prefill (token-major) GEMMs are used.
 constexpr int64_t kTokenMajorMinTokens = 512;
 
@@ -277,8 +285,8 @@ int run_decode(const float* routing_logits, const void* routing_bias, int routin
                const GivenPicks& given = GivenPicks{}) {
   // Four K slices: 2048 units of ~0.9 MB keep the SMs evenly loaded; more
   // slices add red.add and unit-switch overhead.
-  constexpr int kG1Splits = 4;
-  constexpr int kG2Splits = 2;
+  constexpr int kG1Splits = MOE_B200_DECODE_G1_SPLITS;
+  constexpr int kG2Splits = MOE_B200_DECODE_G2_SPLITS;
   constexpr int kBN = 16;
   const int cap = static_cast<int>(l.cap_rows);
   int* counts = reinterpret_cast<int*>(ws + l.counts);
