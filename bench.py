@@ -76,6 +76,8 @@ WORKLOADS = {
     "prefill": (4096, "hot", "config2 prefill: one MoE layer call, T=4096, 4 hot local experts"),
 }
 NUM_SHARDS = 8
+DATA = ("synthetic, seeded (contest dataset unavailable); N(0,1) logits, N(0,0.1) bf16 bias, "
+        "e4m3 1x128 / 128x128 block-scaled N(0,1) activations and N(0,0.02) weights")
 REL_TOL = 1e-2
 MATCH_FRAC = 0.999
 
@@ -291,6 +293,21 @@ L2_BYTES = 126 * 1024 * 1024
 def weights_exceed_l2(st: dict) -> bool:
     """True when one call streams more than twice the L2 in expert weights."""
     return st["E_act"] * (W13_BYTES + W2_BYTES) > 2 * L2_BYTES
+
+
+def headline_config(desc: str, T: int, offset: int, st: dict, world: int, back_to_back: bool) -> dict:
+    """The `config` of the headline line; both arms print the same one (the
+    reference arm derives `st` and the L2 policy from the same routing)."""
+    return {"workload": f"{desc}, 32 local experts per GPU",
+            "T": T, "local_expert_offset": offset, "E_act": st["E_act"], "sum_Tk": st["sum_Tk"],
+            "parallelism": f"ep{world}" + (" + NVLink combine (peer loads/stores, one kernel)" if world > 1 else ""),
+            **({"hidden": "bf16, quantised per 1x128 block inside the row copy (moe_b200_run_bf16_hidden)"}
+               if BF16_HIDDEN else {}),
+            "l2": ("back to back: each call streams the active experts' weights "
+                   f"({st['E_act'] * (W13_BYTES + W2_BYTES) / 1e6:.0f} MB > 2 x 126 MB L2), so no "
+                   "weight byte is L2-resident from the previous call; value_l2_write_flushed is the "
+                   "same call after a 256 MB write flush" if back_to_back else
+                   "flushed (256 MB write) before every timed call")}
 
 
 # --bf16-hidden: the calls take bf16 hidden states (inp["hidden_bf16"]) and
@@ -964,19 +981,8 @@ def main() -> None:
         "scaling": "weak",
         "vs_baseline": None,
         "dtype": "fp8_e4m3 (fp32 accumulate)",
-        "data": "synthetic, seeded (contest dataset unavailable); N(0,1) logits, N(0,0.1) bf16 bias, "
-                "e4m3 1x128 / 128x128 block-scaled N(0,1) activations and N(0,0.02) weights",
-        "config": {"workload": f"{desc}, 32 local experts per GPU",
-                   "T": HEADLINE_T, "local_expert_offset": offset, "E_act": st["E_act"],
-                   "sum_Tk": st["sum_Tk"],
-                   "parallelism": f"ep{world}" + (" + NVLink combine (peer loads/stores, one kernel)" if world > 1 else ""),
-                   **({"hidden": "bf16, quantised per 1x128 block inside the row copy (moe_b200_run_bf16_hidden)"}
-                      if BF16_HIDDEN else {}),
-                   "l2": ("back to back: each call streams the active experts' weights "
-                          f"({st['E_act'] * (W13_BYTES + W2_BYTES) / 1e6:.0f} MB > 2 x 126 MB L2), so no "
-                          "weight byte is L2-resident from the previous call; value_l2_write_flushed is the "
-                          "same call after a 256 MB write flush" if back_to_back else
-                          "flushed (256 MB write) before every timed call")},
+        "data": DATA,
+        "config": headline_config(desc, HEADLINE_T, offset, st, world, back_to_back),
         "value_l2_write_flushed": round(float(flushed_ms) * 1e3, 2),
         "roofline": rl,
         "stages_us": {k: round(v * 1e3, 2) for k, v in stage.items()},
@@ -1046,6 +1052,13 @@ def run_reference(args, world: int, rank: int, warmup: int) -> None:
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     r = workloads.make_routing_inputs(HEADLINE_T, SEED, dev, variant, 0)
     active = moe_oracle.active_local_experts(r["routing_logits"].cpu(), r["routing_bias"].cpu(), 2.5, 0)
+    # the routing statistics of our arm's rank 0 (offset 0), from the
+    # restatement's routing: the line's config is our arm's
+    idx, _ = moe_oracle.route(r["routing_logits"].cpu(), r["routing_bias"].cpu(), 2.5)
+    le = idx.long()
+    local = (le >= 0) & (le < 32)
+    counts = torch.bincount(le[local], minlength=32)
+    st = {"T": HEADLINE_T, "E_act": int((counts > 0).sum()), "sum_Tk": int(counts.sum())}
     inp = workloads.make_inputs(HEADLINE_T, SEED, dev, variant, 0, 2.5, experts=active, weight_seed=SEED + 1)
     inp = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
     if dev == "cuda":
@@ -1065,8 +1078,8 @@ def run_reference(args, world: int, rank: int, warmup: int) -> None:
     line = {
         "metric": METRIC, "value": round(v, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": warmup, "ms_per_step": round(v / 1e3, 3), "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "fp32 (dequantised e4m3)", "data": "synthetic, seeded",
-        "config": {"workload": f"{desc}, 32 local experts", "T": HEADLINE_T},
+        "vs_baseline": None, "dtype": "fp32 (dequantised e4m3)", "data": DATA,
+        "config": headline_config(desc, HEADLINE_T, 0, st, world, weights_exceed_l2(st)),
         "impl": "reference",
         "cpu_baseline": base,
         "e2e": {"value": round(v, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
