@@ -22,6 +22,24 @@
 //      area to the caller's output.
 // With one rank (all shards on one GPU) only the reduction runs, straight
 // into the output, and the counters are not touched.
+// Decode-size calls (at most kEpLLMaxTokens tokens) on two or more ranks use
+// flagged lines instead of steps 1-3, so that no fence or counter sits on the
+// critical path (the fences and the two all-rank counts cost about 20 us at
+// 64 tokens, against a few microseconds of data): every 16-byte line carries
+// two 4-byte values, each followed by the call number, stored with one
+// 16-byte store and polled with one 16-byte load until both flags read the
+// call number (the scheme of NCCL's LL protocol).
+//   A. each rank sums its own shards' rows that another rank owns and stores
+//      them, as flagged fp32 lines, into the owner's receive slot for it;
+//   B. each rank forms its own rows: the ranks' partial sums in rank order
+//      (its own from its shards, the others' polled from its receive slots),
+//      one bf16 rounding, into its output and, as flagged bf16 lines, into
+//      every other rank's receive rows;
+//   C. each rank polls its receive rows for the other ranks' rows and copies
+//      them into its output.
+// A rank overwrites a peer's receive area for call c + 1 only after its own
+// call c has completed, which needed every line the peer had to read for
+// call c, so one receive area per rank suffices.
 // The call number grows (it is kept in the EP area); the per-call counters
 // are cleared by the last CTA of each call, once no CTA of the call still
 // waits and before this rank can announce the next call, so nothing has to
@@ -31,7 +49,8 @@
 // gives up after one second with a status bit instead of hanging. A wait that
 // gives up leaves the ranks' counters out of step, so it also marks every
 // rank's area as poisoned: every later combine on those areas returns at once
-// with a status bit, until every rank has zeroed its area's counter block.
+// with a status bit, until every rank has zeroed its whole area (the
+// counter block and the flagged lines, whose call numbers restart).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
@@ -56,10 +75,16 @@ constexpr int kEpThreads = 256;
 // wait for each other), which __launch_bounds__ guarantees for two 256-thread
 // CTAs per SM when nothing else runs on the device.
 constexpr int kEpCtasPerSm = 2;
+// Calls with at most this many tokens use the flagged-line protocol.
+constexpr int kEpLLMaxTokens = kDecodeMaxTokens;
+constexpr int kLLPartLines = kHidden / 2;                 // flagged fp32 lines per row (2 values each)
+constexpr int kLLOutLines = kHidden / 4;                  // flagged bf16 lines per row (4 values each)
+constexpr int kLLPartRows = kEpLLMaxTokens + kEpMaxRanks;  // W slots of ceil(T / W) rows
 
 // Layout of a rank's expert-parallel area (moe_b200_ep_area_bytes): the
-// counters sit at fixed offsets, so calls with different token counts find
-// them in the same place. Bytes [0, kStage) are the counter block.
+// counters and the flagged-line buffers sit at fixed offsets, so calls with
+// different token counts find them in the same place. Bytes [0, kCounters)
+// are the counter block.
 struct EpArea {
   static constexpr size_t kFlags = 0;       // int32[kEpMaxRanks]: call number announced by each rank
   static constexpr size_t kDone = 64;       // int32: ranks that finished writing into this staging (this call)
@@ -67,9 +92,15 @@ struct EpArea {
   static constexpr size_t kCalls = 72;      // int32: completed calls of this rank
   static constexpr size_t kPoison = 76;     // int32: nonzero once a combine on these areas gave up a wait
   static constexpr size_t kWritten = 80;    // int32: CTAs of this rank that finished writing (this call)
-  static constexpr size_t kStage = 256;     // bf16[T, 7168] output staging
+  static constexpr size_t kCounters = 256;  // end of the counter block
+  // flagged-line protocol: fp32 partial rows received from each rank (slot
+  // r at row r * ceil(T / W)), then the bf16 rows received from their owners
+  static constexpr size_t kLLPart = kCounters;
+  static constexpr size_t kLLOut = kLLPart + static_cast<size_t>(kLLPartRows) * kLLPartLines * 16;
+  static constexpr size_t kStage = kLLOut + static_cast<size_t>(kEpLLMaxTokens) * kLLOutLines * 16;   // bf16[T, 7168] output staging
 };
-static_assert(EpArea::kStage == MOE_B200_EP_COUNTER_BYTES, "counter block size in the header");
+static_assert(EpArea::kCounters == MOE_B200_EP_COUNTER_BYTES, "counter block size in the header");
+static_assert(EpArea::kStage % 256 == 0, "staging alignment");
 
 struct EpParams {
   uint8_t* area[kEpMaxRanks];          // each rank's EP area (this process's mapping)
@@ -92,12 +123,6 @@ __device__ __forceinline__ void st_release_sys(int* p, int v) {
 
 __device__ __forceinline__ void red_release_sys_add(int* p, int v) {
   asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ int atom_add_acq_rel_gpu(int* p, int v) {
-  int old;
-  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-  return old;
 }
 
 // Spins (bounded) until *p has reached target. The counters only grow and
@@ -146,11 +171,26 @@ __device__ __forceinline__ Bf16Quads reduce_quads(const EpParams& p, int t, int 
       v[q] = src[kHalfQuads + j];
     }
   }
+  // each rank's shards summed in shard order, then the ranks' sums in rank
+  // order (the order of the flagged-line protocol, whose partial sums are
+  // formed by their own ranks); with one shard per rank, or one rank, this
+  // is the plain sum in source order
+  const int S = p.sources / p.world;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  int in_rank = 0;
 #pragma unroll
   for (int q = 0; q < kEpMaxSources; ++q) {
-    a[0] += u[q].x; a[1] += u[q].y; a[2] += u[q].z; a[3] += u[q].w;
-    a[4] += v[q].x; a[5] += v[q].y; a[6] += v[q].z; a[7] += v[q].w;
+    b[0] += u[q].x; b[1] += u[q].y; b[2] += u[q].z; b[3] += u[q].w;
+    b[4] += v[q].x; b[5] += v[q].y; b[6] += v[q].z; b[7] += v[q].w;
+    if (q < p.sources && ++in_rank == S) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        a[i] += b[i];
+        b[i] = 0.f;
+      }
+      in_rank = 0;
+    }
   }
   return {pack_bf16x4(a[0], a[1], a[2], a[3]), pack_bf16x4(a[4], a[5], a[6], a[7])};
 }
@@ -163,41 +203,141 @@ __device__ __forceinline__ void store_quads(uint8_t* dst, int t, int j, const Bf
 }
 
 // A wait gave up: record it and poison every rank's area, so that no later
-// combine runs on counters that are out of step.
+// combine runs on counters (or flagged lines) that are out of step.
 __device__ __forceinline__ void give_up(const EpParams& p) {
   atomicOr(p.status, kStatusTimeoutPeer);
   for (int q = 0; q < p.world; ++q) st_release_sys(reinterpret_cast<int*>(p.area[q] + EpArea::kPoison), 1);
 }
 
-}  // namespace
+// One flagged line: values a and b, each followed by the call number.
+__device__ __forceinline__ void st_line(uint8_t* dst, uint32_t a, uint32_t b, uint32_t flag) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "r"(a), "r"(flag), "r"(b), "r"(flag)
+               : "memory");
+}
 
-__global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(EpParams p) {
-  __shared__ int s_ok;
-  pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
+// Polls a flagged line until both of its flags read `flag`; false once the
+// deadline (globaltimer) has passed.
+__device__ __forceinline__ bool ld_line(const uint8_t* src, uint32_t flag, uint64_t deadline, uint32_t& a,
+                                        uint32_t& b) {
+  for (uint32_t spins = 1;; ++spins) {
+    uint32_t x, f0, y, f1;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(x), "=r"(f0), "=r"(y), "=r"(f1)
+                 : "l"(src)
+                 : "memory");
+    if (f0 == flag && f1 == flag) {
+      a = x;
+      b = y;
+      return true;
+    }
+    if ((spins & 63u) == 0u && globaltimer_ns() > deadline) return false;
+  }
+}
+
+// Rows [row_lo(q), row_lo(q + 1)) of the T tokens belong to rank q.
+__device__ __forceinline__ int row_lo(int q, int T, int W) {
+  return static_cast<int>(static_cast<int64_t>(T) * q / W);
+}
+
+__device__ __forceinline__ int row_owner(int t, int T, int W) {
+  int q = static_cast<int>(static_cast<int64_t>(t) * W / T);
+  while (row_lo(q + 1, T, W) <= t) ++q;
+  while (row_lo(q, T, W) > t) --q;
+  return q;
+}
+
+// Flagged-line protocol (see the top of this file) for W >= 2 ranks and
+// T <= kEpLLMaxTokens; decode-size combine rows are indexed by token.
+// Returns false after giving up a wait (status set, areas poisoned).
+__device__ bool combine_lines(const EpParams& p, uint32_t call, int first, int stride) {
+  const int W = p.world, T = p.num_tokens, me = p.rank;
+  const int S = p.sources / W;   // shards per rank
+  const int mlo = row_lo(me, T, W), mhi = row_lo(me + 1, T, W);
+  const int nmine = mhi - mlo;
+  const int slot_rows = (T + W - 1) / W;
+  const uint64_t deadline = globaltimer_ns() + kWaitBudgetNs;
+  uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+  uint8_t* mine = p.area[me];
+
+  // ---- A. my partial sums of the other ranks' rows -> their receive slots
+  const int items_a = (T - nmine) * kLLPartLines;
+  for (int it = first; it < items_a; it += stride) {
+    const int r = it / kLLPartLines;
+    const int line = it - r * kLLPartLines;
+    const int t = r < mlo ? r : r + nmine;
+    const int q = row_owner(t, T, W);
+    float2 v = make_float2(0.f, 0.f);
+    for (int s = 0; s < S; ++s) {
+      const float2 y = reinterpret_cast<const float2*>(p.y[me * S + s] + static_cast<int64_t>(t) * kHidden)[line];
+      v.x += y.x;
+      v.y += y.y;
+    }
+    uint8_t* dst = p.area[q] + EpArea::kLLPart +
+                   (static_cast<size_t>(me * slot_rows + (t - row_lo(q, T, W))) * kLLPartLines + line) * 16;
+    st_line(dst, __float_as_uint(v.x), __float_as_uint(v.y), call);
+  }
+
+  // ---- B. my rows: sum of the ranks' partials in rank order, one rounding
+  const int items_b = nmine * kLLOutLines;
+  for (int it = first; it < items_b; it += stride) {
+    const int rr = it / kLLOutLines;
+    const int line = it - rr * kLLOutLines;   // columns 4 line .. 4 line + 3
+    const int t = mlo + rr;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int r = 0; r < W; ++r) {
+      float v[4];
+      if (r == me) {
+        v[0] = v[1] = v[2] = v[3] = 0.f;
+        for (int s = 0; s < S; ++s) {
+          const float4 y = reinterpret_cast<const float4*>(p.y[me * S + s] + static_cast<int64_t>(t) * kHidden)[line];
+          v[0] += y.x;
+          v[1] += y.y;
+          v[2] += y.z;
+          v[3] += y.w;
+        }
+      } else {
+        const uint8_t* src = mine + EpArea::kLLPart + (static_cast<size_t>(r * slot_rows + rr) * kLLPartLines + 2 * line) * 16;
+        uint32_t x0, x1, x2, x3;
+        if (!ld_line(src, call, deadline, x0, x1) || !ld_line(src + 16, call, deadline, x2, x3)) return false;
+        v[0] = __uint_as_float(x0);
+        v[1] = __uint_as_float(x1);
+        v[2] = __uint_as_float(x2);
+        v[3] = __uint_as_float(x3);
+      }
+      a[0] += v[0];
+      a[1] += v[1];
+      a[2] += v[2];
+      a[3] += v[3];
+    }
+    const uint2 o = pack_bf16x4(a[0], a[1], a[2], a[3]);
+    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * kHidden * 2)[line] = o;
+    for (int q = 0; q < W; ++q)
+      if (q != me)
+        st_line(p.area[q] + EpArea::kLLOut + (static_cast<size_t>(t) * kLLOutLines + line) * 16, o.x, o.y, call);
+  }
+
+  // ---- C. the other ranks' rows from my receive rows
+  const int items_c = (T - nmine) * kLLOutLines;
+  for (int it = first; it < items_c; it += stride) {
+    const int r = it / kLLOutLines;
+    const int line = it - r * kLLOutLines;
+    const int t = r < mlo ? r : r + nmine;
+    uint2 o;
+    if (!ld_line(mine + EpArea::kLLOut + (static_cast<size_t>(t) * kLLOutLines + line) * 16, call, deadline, o.x, o.y))
+      return false;
+    reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * kHidden * 2)[line] = o;
+  }
+  return true;
+}
+
+// Steps 1-3 (see the top of this file) for W >= 2 ranks. Returns the same
+// value in every thread of the CTA: false after giving up a wait (status set,
+// areas poisoned).
+__device__ bool combine_staged(const EpParams& p, uint32_t call, int first, int stride, int& s_ok) {
   const int W = p.world;
   const int T = p.num_tokens;
-  // items (a token row and a quad index j < 896) fit in int32: T <= 2^18
-  const int stride = static_cast<int>(gridDim.x) * kEpThreads;
-  const int first = static_cast<int>(blockIdx.x) * kEpThreads + static_cast<int>(threadIdx.x);
   uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
-
-  if (W == 1) {   // one rank: a plain reduction of its shards into the output
-    const int items = T * kHalfQuads;
-    for (int it = first; it < items; it += stride) {
-      const int t = it / kHalfQuads;
-      const int j = it - t * kHalfQuads;
-      store_quads(out, t, j, reduce_quads(p, t, j));
-    }
-    return;
-  }
-
   uint8_t* mine = p.area[p.rank];
-  if (*reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0) {
-    if (threadIdx.x == 0) atomicOr(p.status, kStatusPoisoned);
-    return;
-  }
-  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) + 1u;
-
   // ---- 1. announce and wait for every rank -------------------------------
   if (threadIdx.x == 0) s_ok = 1;
   __syncthreads();
@@ -209,7 +349,7 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
     s_ok = 0;
   }
   __syncthreads();
-  if (!s_ok) return;
+  if (!s_ok) return false;
 
   // ---- 2. reduce this rank's rows: into its own output, and into every
   //         peer's staging area ---------------------------------------------
@@ -255,6 +395,47 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
       out16[k] = stage[k];
     }
   }
+  return s_ok != 0;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(EpParams p) {
+  __shared__ int s_ok;
+  pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
+  const int W = p.world;
+  const int T = p.num_tokens;
+  // items (a token row and a quad index j < 896) fit in int32: T <= 2^18
+  const int stride = static_cast<int>(gridDim.x) * kEpThreads;
+  const int first = static_cast<int>(blockIdx.x) * kEpThreads + static_cast<int>(threadIdx.x);
+  uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
+
+  if (W == 1) {   // one rank: a plain reduction of its shards into the output
+    const int items = T * kHalfQuads;
+    for (int it = first; it < items; it += stride) {
+      const int t = it / kHalfQuads;
+      const int j = it - t * kHalfQuads;
+      store_quads(out, t, j, reduce_quads(p, t, j));
+    }
+    return;
+  }
+
+  uint8_t* mine = p.area[p.rank];
+  if (*reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0) {
+    if (threadIdx.x == 0) atomicOr(p.status, kStatusPoisoned);
+    return;
+  }
+  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) + 1u;
+
+  bool ok;
+  if (T <= kEpLLMaxTokens) {
+    ok = combine_lines(p, call, first, stride);
+    if (!ok) give_up(p);
+    ok = __syncthreads_or(ok ? 0 : 1) == 0;
+  } else {
+    ok = combine_staged(p, call, first, stride, s_ok);
+  }
+  if (!ok) return;
   // The last CTA of this rank to finish clears the per-call counters and
   // advances the call number: every CTA has passed its waits by then, and no
   // peer writes this area for the next call before this rank announces it.
@@ -330,8 +511,12 @@ int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_ran
   if (cudaGetDevice(&dev) != cudaSuccess ||
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0)
     return MOE_B200_ERR_CUDA;
+  // (flagged lines: one thread per line of the rows this rank sends, about
+  // T * 3584 lines, as the largest of the three phases)
   const int64_t rows_per_rank = (num_tokens + world - 1) / world;
-  const int64_t want = (rows_per_rank * (kHidden / 8) + kEpThreads - 1) / kEpThreads;
+  const int64_t items = (world > 1 && num_tokens <= kEpLLMaxTokens) ? num_tokens * kLLPartLines
+                                                                     : rows_per_rank * (kHidden / 8);
+  const int64_t want = (items + kEpThreads - 1) / kEpThreads;
   const int grid = static_cast<int>(want < kEpCtasPerSm * sms ? (want > 0 ? want : 1) : kEpCtasPerSm * sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (launch_kernel(ep_combine_kernel, grid, kEpThreads, 0, s, true, p) != cudaSuccess)

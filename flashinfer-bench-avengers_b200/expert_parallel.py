@@ -237,11 +237,12 @@ class NvlinkCombiner:
         return st
 
     def reset(self) -> None:
-        """Collective: clears every rank's combine counters after a combine
-        gave up a wait (status bits 1 << 7 / 1 << 8)."""
+        """Collective: clears every rank's EP area (combine counters and
+        flagged lines) after a combine gave up a wait (status bits 1 << 7 /
+        1 << 8)."""
         torch.cuda.synchronize(self.device)
         self.peers.barrier()
-        self.area[:256].zero_()
+        self.area.zero_()
         torch.cuda.synchronize(self.device)
         self.peers.barrier()
 

@@ -301,6 +301,11 @@ MOE_B200_API int moe_b200_noalloc_read_status(uint32_t* status, void* stream);
  * of the token rows in fp32 from every rank's combine rows (peer loads),
  * rounds once to bf16 and stores the rows into every rank's area (peer
  * stores); the ranks synchronise through counters at the start of the areas.
+ * Calls of at most 64 tokens instead exchange flagged lines (each 4-byte
+ * value stored next to the call number, polled until the number matches):
+ * every rank sends its partial sums of the rows another rank owns to that
+ * rank, the owner adds the ranks' partial sums in rank order, rounds once
+ * and sends the bf16 rows to every rank; no fence or counter is waited on.
  *
  *   rank_workspaces  host array of `world` pointers: rank q's workspace as
  *                    mapped in this process
@@ -309,13 +314,14 @@ MOE_B200_API int moe_b200_noalloc_read_status(uint32_t* status, void* stream);
  *
  * Every rank must call it once per layer call, on the stream of its
  * moe_b200_run, with the same num_tokens. Each EP area must be zero before
- * the first call (its counters only grow, so later calls need no clearing).
- * Each wait on a peer gives up after one second, sets status bit 1 << 7
- * (moe_b200_read_status) and marks every rank's area as poisoned: from then
- * on every combine on those areas returns at once with status bit 1 << 8 and
- * writes no output. To recover, every rank synchronises its device, zeroes
- * the first MOE_B200_EP_COUNTER_BYTES of its own area, and the ranks meet at
- * a host barrier before any of them calls the combine again.
+ * the first call (its counters and call numbers only grow, so later calls
+ * need no clearing). Each wait on a peer gives up after one second, sets
+ * status bit 1 << 7 (moe_b200_read_status) and marks every rank's area as
+ * poisoned: from then on every combine on those areas returns at once with
+ * status bit 1 << 8 and writes no output. To recover, every rank
+ * synchronises its device, zeroes its whole area (the counter block, the
+ * first MOE_B200_EP_COUNTER_BYTES, and the flagged lines after it), and the
+ * ranks meet at a host barrier before any of them calls the combine again.
  * Asynchronous, no host synchronisation.
  */
 #define MOE_B200_EP_COUNTER_BYTES 256
@@ -330,7 +336,9 @@ MOE_B200_API int moe_b200_ep_combine(void* const* rank_workspaces, void* const* 
  * workspace; shard_workspaces lists world * shards_per_rank workspaces,
  * rank-major (rank q's shards at [q * shards_per_rank, (q + 1) *
  * shards_per_rank)), as mapped in this process. The output is the bf16
- * rounding of the fp32 sum of every shard's combine rows in that order.
+ * rounding of an fp32 sum: each rank's shards summed in shard order, then
+ * those sums added in rank order (with one shard per rank, the plain sum in
+ * rank order).
  * world * shards_per_rank <= 8. The status word written is that of this
  * rank's first shard workspace. moe_b200_ep_combine is this call with
  * shards_per_rank = 1. No reference counterpart.

@@ -183,7 +183,10 @@ def test_ep_and_ipc_entry_points_reject_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_ep_combine_shards(arr, 4, mis, 0, 2, 4, p, None) == 2            # misaligned area
     assert lib.moe_b200_ep_combine_shards(arr, 4, arr, 0, 2, 0, p, None) == 0            # T = 0 is a no-op
     assert lib.moe_b200_ep_combine(arr, arr, 0, 2, 0, p, None) == 0
-    assert lib.moe_b200_ep_area_bytes(16) == 256 + (16 * 7168 * 2 + 255) // 256 * 256
+    # counter block, flagged-line buffers (72 rows of 3584 fp32 lines, 64 rows
+    # of 1792 bf16 lines, 16 bytes each), then the bf16 staging rows
+    lines = 72 * 3584 * 16 + 64 * 1792 * 16
+    assert lib.moe_b200_ep_area_bytes(16) == 256 + lines + (16 * 7168 * 2 + 255) // 256 * 256
     assert lib.moe_b200_ep_area_bytes(-1) == 0
     out = P()
     assert lib.moe_b200_ep_buffer_alloc(0, ctypes.byref(out)) == 1

@@ -3,8 +3,9 @@
 One process per GPU (up to four). In the first pass each rank owns one
 32-expert shard (local_expert_offset = 32 * rank); in the second, two
 shards each (offsets 64 * rank and 64 * rank + 32). The fused combine must
-equal, bit for bit, the bf16 rounding of the fp32 sum in shard order of the
-shards' own combine rows (read back from the workspaces and gathered), agree
+equal, bit for bit, the bf16 rounding of the fp32 sum of the shards' own
+combine rows (read back from the workspaces and gathered; each rank's shards
+summed in shard order, then those sums in rank order), agree
 with an independent run of every shard within the operator's tolerance, be
 identical on all ranks and leave the status words clear. The shared buffers
 are plain cudaMalloc memory mapped through CUDA IPC (no multicast object),
@@ -72,15 +73,19 @@ def _worker(rank: int, world: int, port: int, passes, results):
                     comb.forward_shards(tokens, shards, fused)
                 torch.cuda.synchronize()
                 status = comb.status()
-                # exact reference: every shard's fp32 combine rows, summed in
-                # shard order (rank-major), rounded once to bf16
+                # exact reference: every shard's fp32 combine rows, each
+                # rank's summed in shard order, those sums in rank order,
+                # rounded once to bf16 (T <= 64 takes the flagged-line
+                # protocol, larger T the staged one: both sum this way)
                 mine = torch.stack([_shard_rows(ws, T) for ws in comb.workspaces])
                 rows = [torch.empty_like(mine) for _ in range(world)]
                 dist.all_gather(rows, mine)
                 total = torch.zeros(T, 7168, dtype=torch.float32, device=dev)
                 for q in range(world):
+                    part = torch.zeros(T, 7168, dtype=torch.float32, device=dev)
                     for s in range(spr):
-                        total = total + rows[q][s]
+                        part = part + rows[q][s]
+                    total = total + part
                 exact = torch.equal(fused, total.to(torch.bfloat16))
                 # the standard tolerance against an independent run of each shard
                 ref = sum(moe_host.run(*workloads.as_args(i)).float() for i in inps)
@@ -106,9 +111,10 @@ def test_nvlink_combine_ranks():
 
     ctx = mp.get_context("spawn")
     results = ctx.Queue()
-    # one shard per rank: decode plan; compact combine rows; token-major GEMMs
+    # one shard per rank: decode plan (flagged lines, also with fewer tokens
+    # than ranks: some own no row); compact combine rows; token-major GEMMs
     # (K split, compact rows). Two shards per rank: decode and token-major.
-    passes = [(1, [(16, "uniform"), (200, "uniform"), (600, "uniform")]),
+    passes = [(1, [(16, "uniform"), (64, "uniform"), (3, "uniform"), (200, "uniform"), (600, "uniform")]),
               (2, [(16, "uniform"), (600, "uniform")])]
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, passes, results)) for r in range(world)]

@@ -4,8 +4,10 @@ The combine waits for every peer with a one-second limit. Here a second
 "rank" exists only as an EP area that nothing ever writes, so the wait for
 its announcement runs out (a flag that nothing sets; no fault, no trap):
 the call must report status bit 1 << 7, poison both areas, make the next
-combine return at once with bit 1 << 8, and after the counter blocks are
-zeroed a combine must work again and reproduce the layer's own output.
+combine return at once with bit 1 << 8, and after the areas are zeroed a
+combine must work again and reproduce the layer's own output. (T = 16 on two
+ranks takes the flagged-line protocol: the wait that runs out is the poll
+for the second rank's partial sums.)
 """
 from __future__ import annotations
 
@@ -49,10 +51,10 @@ def test_combine_gives_up_poisons_and_recovers(cuda_device):
     st = moe_host.read_status(ws)
     assert st == (1 << 8), hex(st)
     assert torch.isnan(out.float()).all()
-    # recovery: zero the counter blocks; a one-rank combine then equals the
-    # output the layer itself wrote from the same combine rows
+    # recovery: zero the areas; a one-rank combine then equals the output
+    # the layer itself wrote from the same combine rows
     for a in areas:
-        a[:256].zero_()
+        a.zero_()
     own = torch.empty_like(out)
     moe_host.run_dps(*args, own, workspace=ws)
     moe_host.ep_combine_shards([ws.data_ptr()], 1, [areas[0].data_ptr()], 0, T, out)
