@@ -5,13 +5,19 @@
 // own workspace) and leaves the fp32 combine rows in those workspaces
 // (output = NULL). This kernel then forms the bf16 output of the whole layer
 // on every rank in one launch:
+//   0. with several shards per rank, sum this rank's shards' rows in shard
+//      order into one fp32 row per token (its partial sum; local work, so
+//      that step 2 reads one partial per rank over NVLink instead of every
+//      shard's rows), and count the CTA when done;
 //   1. announce "my combine rows are final" to every peer (a release store at
-//      system scope of a call counter into the peer's flag array) and wait
-//      (bounded) until every peer has announced;
+//      system scope of a call counter into the peer's flag array, once every
+//      CTA of this rank has counted itself in step 0) and wait (bounded)
+//      until every peer has announced;
 //   2. reduce this rank's 1/W slice of the token rows: for each row, the fp32
-//      rows of every shard of every rank are read (plain loads of peer memory
-//      over NVLink for the other ranks' shards), summed in fp32 in shard order
-//      (rank-major) and rounded once to bf16; the result is stored into this
+//      rows of every shard of every rank (or every rank's partial sum) are
+//      read (plain loads of peer memory over NVLink for the other ranks'),
+//      summed in fp32 (each rank's shards in shard order, then the ranks in
+//      rank order) and rounded once to bf16; the result is stored into this
 //      rank's output and into the output staging area of every other rank
 //      (plain stores to peer memory) -- reduce-scatter and all-gather in one
 //      pass, with the sum formed before the single bf16 rounding;
@@ -92,6 +98,7 @@ struct EpArea {
   static constexpr size_t kCalls = 72;      // int32: completed calls of this rank
   static constexpr size_t kPoison = 76;     // int32: nonzero once a combine on these areas gave up a wait
   static constexpr size_t kWritten = 80;    // int32: CTAs of this rank that finished writing (this call)
+  static constexpr size_t kSummed = 84;     // int32: CTAs of this rank that finished its shard sums (this call)
   static constexpr size_t kCounters = 256;  // end of the counter block
   // flagged-line protocol: fp32 partial rows received from each rank (slot
   // r at row r * ceil(T / W)), then the bf16 rows received from their owners
@@ -106,6 +113,10 @@ struct EpParams {
   uint8_t* area[kEpMaxRanks];          // each rank's EP area (this process's mapping)
   const float* y[kEpMaxSources];       // each shard's fp32 combine rows, rank-major
   const int32_t* slot[kEpMaxSources];  // each shard's token -> combine row map, null: row = token
+  // Staged protocol with several shards per rank: each rank's fp32 sum of
+  // its own shards' rows, one row per token, in a region of its first shard
+  // workspace that the layer no longer needs (the permuted activation copy)
+  float* partial[kEpMaxRanks];
   uint16_t* out;                       // this rank's output, bf16 [T, 7168]
   uint32_t* status;                    // this rank's status word
   int rank, world, sources, num_tokens;
@@ -137,12 +148,9 @@ __device__ __forceinline__ bool wait_at_least(const int* p, uint32_t target) {
   return true;
 }
 
-// The fp32 sums over all sources of columns 4j .. 4j+3 and 3584+4j .. +3 of
-// token t's rows, rounded to bf16 (two 8-byte results): consecutive threads
-// take consecutive j, so every load instruction of a warp reads 512
-// contiguous bytes. Every source's row index and data are loaded before the
-// sum (up to 16 loads in flight per thread); absent rows add +0.0, which
-// leaves the sum's bits as they are (the sum starts at +0.0).
+// Column quads of a row: item (t, j) covers columns 4j .. 4j+3 and
+// 3584+4j .. +3 of token t; consecutive threads take consecutive j, so every
+// load instruction of a warp reads 512 contiguous bytes.
 struct Bf16Quads {
   uint2 a, b;
 };
@@ -155,44 +163,68 @@ __device__ __forceinline__ uint2 pack_bf16x4(float x, float y, float z, float w)
 
 constexpr int kHalfQuads = kHidden / 8;   // 896: quads per half row
 
-__device__ __forceinline__ Bf16Quads reduce_quads(const EpParams& p, int t, int j) {
+struct F32Quads {
+  float4 a, b;
+};
+
+// The fp32 sums (before rounding) of columns 4j .. 4j+3 and 3584+4j .. +3
+// of token t's rows over `n` sources: the shards q0 .. q0 + n - 1 (row map
+// p.slot), or with kPartials the ranks' partial sums (row = token). Every
+// source's row index and data are loaded before the sum (up to 16 loads in
+// flight per thread); absent rows add +0.0, which leaves the sum's bits as
+// they are (the sum starts at +0.0). Sources are summed in groups of
+// `group` (one rank's shards, in shard order), then the groups in order;
+// with one group, or groups of one, this is the plain sum in source order.
+template <bool kPartials>
+__device__ __forceinline__ F32Quads sum_quads(const EpParams& p, int t, int j, int q0, int n, int group) {
   int row[kEpMaxSources];
 #pragma unroll
-  for (int q = 0; q < kEpMaxSources; ++q)
-    row[q] = q < p.sources ? (p.slot[q] != nullptr ? __ldg(p.slot[q] + t) : t) : -1;
+  for (int q = 0; q < kEpMaxSources; ++q) {
+    if constexpr (kPartials) {
+      row[q] = q < n ? t : -1;
+    } else {
+      row[q] = q < n ? (p.slot[q0 + q] != nullptr ? __ldg(p.slot[q0 + q] + t) : t) : -1;
+    }
+  }
   float4 u[kEpMaxSources], v[kEpMaxSources];
 #pragma unroll
   for (int q = 0; q < kEpMaxSources; ++q) {
     u[q] = make_float4(0.f, 0.f, 0.f, 0.f);
     v[q] = u[q];
     if (row[q] >= 0) {
-      const float4* src = reinterpret_cast<const float4*>(p.y[q] + static_cast<int64_t>(row[q]) * kHidden);
+      const float* base = kPartials ? p.partial[q] : p.y[q0 + q];
+      const float4* src = reinterpret_cast<const float4*>(base + static_cast<int64_t>(row[q]) * kHidden);
       u[q] = src[j];
       v[q] = src[kHalfQuads + j];
     }
   }
-  // each rank's shards summed in shard order, then the ranks' sums in rank
-  // order (the order of the flagged-line protocol, whose partial sums are
-  // formed by their own ranks); with one shard per rank, or one rank, this
-  // is the plain sum in source order
-  const int S = p.sources / p.world;
   float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
   float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-  int in_rank = 0;
+  int in_group = 0;
 #pragma unroll
   for (int q = 0; q < kEpMaxSources; ++q) {
     b[0] += u[q].x; b[1] += u[q].y; b[2] += u[q].z; b[3] += u[q].w;
     b[4] += v[q].x; b[5] += v[q].y; b[6] += v[q].z; b[7] += v[q].w;
-    if (q < p.sources && ++in_rank == S) {
+    if (q < n && ++in_group == group) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         a[i] += b[i];
         b[i] = 0.f;
       }
-      in_rank = 0;
+      in_group = 0;
     }
   }
-  return {pack_bf16x4(a[0], a[1], a[2], a[3]), pack_bf16x4(a[4], a[5], a[6], a[7])};
+  return {make_float4(a[0], a[1], a[2], a[3]), make_float4(a[4], a[5], a[6], a[7])};
+}
+
+__device__ __forceinline__ Bf16Quads round_quads(const F32Quads& f) {
+  return {pack_bf16x4(f.a.x, f.a.y, f.a.z, f.a.w), pack_bf16x4(f.b.x, f.b.y, f.b.z, f.b.w)};
+}
+
+// The bf16 rounding of the sum over every shard of every rank: each rank's
+// shards in shard order, then the ranks in rank order.
+__device__ __forceinline__ Bf16Quads reduce_quads(const EpParams& p, int t, int j) {
+  return round_quads(sum_quads<false>(p, t, j, 0, p.sources, p.sources / p.world));
 }
 
 // Stores the two results into a bf16 [T, 7168] row-major destination.
@@ -338,11 +370,36 @@ __device__ bool combine_staged(const EpParams& p, uint32_t call, int first, int 
   const int T = p.num_tokens;
   uint8_t* out = reinterpret_cast<uint8_t*>(p.out);
   uint8_t* mine = p.area[p.rank];
-  // ---- 1. announce and wait for every rank -------------------------------
+  const int S = p.sources / W;
   if (threadIdx.x == 0) s_ok = 1;
+  // ---- 0. this rank's shard sums, one fp32 row per token ------------------
+  if (S > 1) {
+    float* dst = p.partial[p.rank];
+    const int n = T * kHalfQuads;
+    for (int it = first; it < n; it += stride) {
+      const int t = it / kHalfQuads;
+      const int j = it - t * kHalfQuads;
+      const F32Quads v = sum_quads<false>(p, t, j, p.rank * S, S, S);
+      float4* row = reinterpret_cast<float4*>(dst + static_cast<int64_t>(t) * kHidden);
+      row[j] = v.a;
+      row[kHalfQuads + j] = v.b;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();   // peers read the partial sums after the announcement
+      red_release_gpu_add(reinterpret_cast<int*>(mine + EpArea::kSummed), 1);
+    }
+  }
+  // ---- 1. announce and wait for every rank -------------------------------
   __syncthreads();
-  if (blockIdx.x == 0 && threadIdx.x < W)
-    st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, static_cast<int>(call));
+  if (blockIdx.x == 0 && threadIdx.x < W) {
+    if (S > 1 && !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kSummed), gridDim.x)) {
+      give_up(p);
+      s_ok = 0;
+    } else {
+      st_release_sys(reinterpret_cast<int*>(p.area[threadIdx.x] + EpArea::kFlags) + p.rank, static_cast<int>(call));
+    }
+  }
   if (threadIdx.x < W &&
       !wait_at_least(reinterpret_cast<const int*>(mine + EpArea::kFlags) + threadIdx.x, call)) {
     give_up(p);
@@ -360,7 +417,8 @@ __device__ bool combine_staged(const EpParams& p, uint32_t call, int first, int 
     const int rel = it / kHalfQuads;
     const int t = r0 + rel;
     const int j = it - rel * kHalfQuads;
-    const Bf16Quads o = reduce_quads(p, t, j);
+    // one partial sum per rank (step 0), or every shard's rows
+    const Bf16Quads o = S > 1 ? round_quads(sum_quads<true>(p, t, j, 0, W, 1)) : reduce_quads(p, t, j);
     store_quads(out, t, j, o);
     for (int q = 0; q < W; ++q)
       if (q != p.rank) store_quads(p.area[q] + EpArea::kStage, t, j, o);
@@ -447,6 +505,7 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
       *reinterpret_cast<volatile int*>(mine + EpArea::kWritten) = 0;
       *reinterpret_cast<volatile int*>(mine + EpArea::kDone) = 0;
       *reinterpret_cast<volatile int*>(mine + EpArea::kFinished) = 0;
+      *reinterpret_cast<volatile int*>(mine + EpArea::kSummed) = 0;
       __threadfence();
       *reinterpret_cast<volatile uint32_t*>(mine + EpArea::kCalls) = call;
     }
@@ -495,6 +554,11 @@ int moe_b200_ep_combine_shards(void* const* shard_workspaces, int shards_per_ran
     // decode-size calls keep one combine row per token
     p.slot[q] = num_tokens <= kDecodeMaxTokens ? nullptr : reinterpret_cast<const int32_t*>(ws + l.tok_slot);
   }
+  for (int q = 0; q < kEpMaxRanks; ++q)
+    p.partial[q] = q < world ? reinterpret_cast<float*>(static_cast<uint8_t*>(shard_workspaces[q * shards_per_rank]) +
+                                                        l.a_perm)
+                             : nullptr;
+  static_assert(sizeof(float) * kHidden <= 8 * kHidden, "a_perm holds one fp32 row per token");
   p.out = static_cast<uint16_t*>(output);
   // this rank's first shard workspace holds the status word the caller reads
   p.status = reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(shard_workspaces[rank * shards_per_rank]) +
