@@ -4,23 +4,30 @@
 // Here every rank holds its own tokens (different on every rank) and owns
 // S 32-expert shards: rank q owns global experts [32 S q, 32 S (q + 1)).
 // Each rank routes its own tokens (DeepSeek-V3, all 256 experts), then
-//   plan      (one CTA) numbers its picks per destination rank in (token,
-//             pick) order, writes its row of the send-count matrix into every
-//             rank's area and announces the call (release store, system scope);
-//   dispatch  waits for every rank's row, places each pick at row
-//             off(q, r) + slot of destination q's receive slab, where off is
-//             the exclusive sum over lower source ranks, and writes there by
-//             peer stores the wire format of one pick: the token's e4m3 row
-//             (7,168 B), its 56 block scales (into the slab's [56, R] scale
-//             matrix), the global expert id and the routing weight; then it
+//   plan      (one CTA) numbers, for every destination rank, its tokens with
+//             at least one pick there, in token order; writes its row of the
+//             send-count matrix into every rank's area and announces the call
+//             (release store, system scope);
+//   dispatch  waits for every rank's row, places token t's row for
+//             destination q at row off(q, r) + slot of q's receive slab, where
+//             off is the exclusive sum over lower source ranks, and writes
+//             there by peer stores the wire format of one (token, destination)
+//             row: the token's e4m3 row (7,168 B), its 56 block scales (into
+//             the slab's [56, R] scale matrix) and its eight picks with only
+//             those on q kept (others: no expert, weight 0); a token travels
+//             once to each rank it has picks on (DeepSeek-V3 keeps 4 groups of
+//             32 experts, so at most 4 ranks), not once per pick; then it
 //             counts its CTAs on every rank and waits for all of them;
 //   layer     moe_b200_run_routed on the slab, once per owned shard (each row
-//             is a token with one given pick; rows past the received count
-//             hold no pick), combine rows left in each shard's workspace;
+//             is a token with its picks on this rank; a shard takes those in
+//             its 32 experts, and its layer already sums them into one combine
+//             row; rows past the received count hold no pick), combine rows
+//             left in each shard's workspace;
 //   combine   announces, waits for every rank, and forms each own token's
-//             output as the fp32 sum of its picks' combine rows, read from the
-//             destination ranks' workspaces by peer loads, in pick order,
-//             rounded once to bf16.
+//             output as the fp32 sum of its combine rows on the destination
+//             ranks' shards (peer loads): each rank's shards in shard order,
+//             then the ranks in rank order (the order of the expert-parallel
+//             combine), rounded once to bf16.
 // The order of rows inside a slab depends only on the routing, so results do
 // not depend on timing. Counters only grow (signed-difference compares, so
 // they may wrap); every wait gives up after one second with a status bit and
@@ -74,13 +81,13 @@ moe_b200_a2a_layout a2a_layout(int64_t max_tokens, int64_t cap) {
   std::memset(&l, 0, sizeof(l));
   size_t off = A2aCounters::kEnd;
   l.send_slot = off;
-  off = align256(off + static_cast<size_t>(max_tokens) * kTopK * sizeof(int32_t));
-  l.pick_row = off;
-  off = align256(off + static_cast<size_t>(max_tokens) * kTopK * sizeof(int32_t));
+  off = align256(off + static_cast<size_t>(max_tokens) * kA2aMaxRanks * sizeof(int32_t));
+  l.dest_row = off;
+  off = align256(off + static_cast<size_t>(max_tokens) * kA2aMaxRanks * sizeof(int32_t));
   l.slab_idx = off;
-  off = align256(off + static_cast<size_t>(cap) * sizeof(int32_t));
+  off = align256(off + static_cast<size_t>(cap) * kTopK * sizeof(int32_t));
   l.slab_w = off;
-  off = align256(off + static_cast<size_t>(cap) * sizeof(float));
+  off = align256(off + static_cast<size_t>(cap) * kTopK * sizeof(float));
   l.slab_scale = off;
   off = align256(off + static_cast<size_t>(cap) * kHiddenBlocks * sizeof(float));
   l.slab_rows = off;
@@ -98,7 +105,7 @@ struct A2aParams {
   const float* y[kA2aMaxRanks];         // combine: every shard's fp32 combine rows, rank-major
   const int32_t* slot[kA2aMaxRanks];    // combine: each shard's row -> combine row map (null: row = row)
   uint16_t* out;                        // combine: this rank's output, bf16 [T, 7168]
-  size_t send_slot, pick_row, slab_idx, slab_w, slab_scale, slab_rows;   // area offsets
+  size_t send_slot, dest_row, slab_idx, slab_w, slab_scale, slab_rows;   // area offsets
   int rank, world, shards, num_tokens, cap;
 };
 
@@ -154,9 +161,9 @@ __device__ __forceinline__ uint2 pack_bf16x4(float x, float y, float z, float w)
 }  // namespace
 
 // ---------------------------------------------------------------- plan
-// One CTA: numbers this rank's picks per destination in (token, pick) order
-// (ballot ranks inside a warp, a per-destination scan over the warps), then
-// publishes the counts and the call.
+// One CTA: numbers, for every destination, this rank's tokens with a pick
+// there, in token order (ballot ranks inside a warp, a per-destination scan
+// over the warps), then publishes the counts and the call.
 __global__ void __launch_bounds__(kPlanThreads) a2a_plan_kernel(A2aParams p) {
   __shared__ int s_warp_cnt[kPlanThreads / 32][kA2aMaxRanks];
   __shared__ int s_running[kA2aMaxRanks];
@@ -176,15 +183,26 @@ __global__ void __launch_bounds__(kPlanThreads) a2a_plan_kernel(A2aParams p) {
   int32_t* send_slot = reinterpret_cast<int32_t*>(mine + p.send_slot);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t lt = (1u << lane) - 1u;
-  const int n = p.num_tokens * kTopK;
-  for (int base = 0; base < n; base += kPlanThreads) {
-    const int i = base + static_cast<int>(threadIdx.x);
-    const int q = i < n ? dest_rank(__ldg(p.topk_idx + i), p.shards) : -1;
-    int in_warp = 0;
-    for (int d = 0; d < W; ++d) {
-      const uint32_t m = __ballot_sync(0xffffffffu, q == d);
-      if (q == d) in_warp = __popc(m & lt);
-      if (lane == 0) s_warp_cnt[warp][d] = __popc(m);
+  const int T = p.num_tokens;
+  for (int base = 0; base < T; base += kPlanThreads) {
+    const int t = base + static_cast<int>(threadIdx.x);
+    uint32_t mask = 0;   // destinations this token has a pick on
+    if (t < T) {
+#pragma unroll
+      for (int k = 0; k < kTopK; ++k) {
+        const int q = dest_rank(__ldg(p.topk_idx + t * kTopK + k), p.shards);
+        if (q >= 0) mask |= 1u << q;
+      }
+    }
+    int in_warp[kA2aMaxRanks];
+#pragma unroll
+    for (int d = 0; d < kA2aMaxRanks; ++d) {
+      in_warp[d] = 0;
+      if (d < W) {
+        const uint32_t m = __ballot_sync(0xffffffffu, (mask >> d) & 1u);
+        in_warp[d] = __popc(m & lt);
+        if (lane == 0) s_warp_cnt[warp][d] = __popc(m);
+      }
     }
     __syncthreads();
     if (threadIdx.x < W) {   // exclusive scan over the warps, one destination per thread
@@ -197,7 +215,11 @@ __global__ void __launch_bounds__(kPlanThreads) a2a_plan_kernel(A2aParams p) {
       s_running[threadIdx.x] = run;
     }
     __syncthreads();
-    if (i < n) send_slot[i] = q >= 0 ? s_warp_cnt[warp][q] + in_warp : -1;
+    if (t < T) {
+#pragma unroll
+      for (int d = 0; d < kA2aMaxRanks; ++d)
+        send_slot[t * kA2aMaxRanks + d] = (d < W && ((mask >> d) & 1u)) ? s_warp_cnt[warp][d] + in_warp[d] : -1;
+    }
     __syncthreads();
   }
   // this rank's row of the count matrix into every rank's area, then the call
@@ -244,27 +266,27 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_dispatch_kerne
   }
   __syncthreads();
 
-  // one warp per pick: row (448 x 16 B), 56 scales, expert id and weight
+  // one warp per (token, destination): row (448 x 16 B), 56 scales and the
+  // token's picks on that destination (the other picks: no expert)
   const int32_t* send_slot = reinterpret_cast<const int32_t*>(mine + p.send_slot);
-  int32_t* pick_row = reinterpret_cast<int32_t*>(mine + p.pick_row);
+  int32_t* dest_row = reinterpret_cast<int32_t*>(mine + p.dest_row);
   const int lane = threadIdx.x & 31;
   const int warps = static_cast<int>(gridDim.x) * (kA2aThreads / 32);
-  const int n = p.num_tokens * kTopK;
+  const int n = p.num_tokens * kA2aMaxRanks;
   for (int i = static_cast<int>(blockIdx.x) * (kA2aThreads / 32) + (threadIdx.x >> 5); i < n; i += warps) {
-    const int e = __ldg(p.topk_idx + i);
-    const int q = dest_rank(e, p.shards);
+    const int t = i / kA2aMaxRanks;
+    const int q = i - t * kA2aMaxRanks;
     const int slot = send_slot[i];
     int j = -1;
-    if (q >= 0 && slot >= 0) {
+    if (q < W && slot >= 0) {
       j = s_off[q] + slot;
       if (j >= p.cap) {
         if (lane == 0) set_status(p, kStatusRecvOverflow);
         j = -1;
       }
     }
-    if (lane == 0) pick_row[i] = j;
+    if (lane == 0) dest_row[i] = j;
     if (j < 0) continue;
-    const int t = i / kTopK;
     uint8_t* dst = p.area[q];
     const uint4* src_row = reinterpret_cast<const uint4*>(p.hidden + static_cast<int64_t>(t) * kHidden);
     uint4* dst_row = reinterpret_cast<uint4*>(dst + p.slab_rows + static_cast<int64_t>(j) * kHidden);
@@ -276,9 +298,12 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_dispatch_kerne
     float* dst_scale = reinterpret_cast<float*>(dst + p.slab_scale);
     for (int b = lane; b < kHiddenBlocks; b += 32)
       dst_scale[static_cast<int64_t>(b) * p.cap + j] = __ldg(p.hidden_scale + static_cast<int64_t>(b) * p.num_tokens + t);
-    if (lane == 0) {
-      reinterpret_cast<int32_t*>(dst + p.slab_idx)[j] = e;
-      reinterpret_cast<float*>(dst + p.slab_w)[j] = __ldg(p.topk_w + i);
+    if (lane < kTopK) {
+      const int e = __ldg(p.topk_idx + t * kTopK + lane);
+      const bool here = dest_rank(e, p.shards) == q;
+      reinterpret_cast<int32_t*>(dst + p.slab_idx)[static_cast<int64_t>(j) * kTopK + lane] = here ? e : kNoExpert;
+      reinterpret_cast<float*>(dst + p.slab_w)[static_cast<int64_t>(j) * kTopK + lane] =
+          here ? __ldg(p.topk_w + t * kTopK + lane) : 0.f;
     }
   }
   // rows past the received count carry no pick (the layer skips them)
@@ -286,10 +311,11 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_dispatch_kerne
   if (s_recv > p.cap && blockIdx.x == 0 && threadIdx.x == 0) set_status(p, kStatusRecvOverflow);
   int32_t* my_idx = reinterpret_cast<int32_t*>(mine + p.slab_idx);
   float* my_w = reinterpret_cast<float*>(mine + p.slab_w);
-  for (int r = recv + static_cast<int>(blockIdx.x) * kA2aThreads + static_cast<int>(threadIdx.x); r < p.cap;
-       r += static_cast<int>(gridDim.x) * kA2aThreads) {
-    my_idx[r] = kNoExpert;
-    my_w[r] = 0.f;
+  const int64_t pad = static_cast<int64_t>(p.cap - recv) * kTopK;
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * kA2aThreads + threadIdx.x; r < pad;
+       r += static_cast<int64_t>(gridDim.x) * kA2aThreads) {
+    my_idx[static_cast<int64_t>(recv) * kTopK + r] = kNoExpert;
+    my_w[static_cast<int64_t>(recv) * kTopK + r] = 0.f;
   }
   if (blockIdx.x == 0 && threadIdx.x == 0) *ctr(mine, A2aCounters::kRecvRows) = recv;
 
@@ -325,10 +351,12 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_combine_kernel
   }
   __syncthreads();
   if (s_ok) {
-    // token t, column quads j and 896 + j: the fp32 rows of its picks, in
-    // pick order, from the shards that computed them
+    // token t, column quads j and 896 + j: its combine rows on every shard of
+    // every destination rank (sources rank-major: shard sh = q * S + s),
+    // each rank's shards summed in shard order, then the ranks in rank order
     constexpr int kHalfQuads = kHidden / 8;
-    const int32_t* pick_row = reinterpret_cast<const int32_t*>(mine + p.pick_row);
+    const int32_t* dest_row = reinterpret_cast<const int32_t*>(mine + p.dest_row);
+    const int S = p.shards;
     const int items = p.num_tokens * kHalfQuads;
     for (int it = static_cast<int>(blockIdx.x) * kA2aThreads + static_cast<int>(threadIdx.x); it < items;
          it += static_cast<int>(gridDim.x) * kA2aThreads) {
@@ -336,32 +364,37 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_combine_kernel
       const int j = it - t * kHalfQuads;
       const float* src[kTopK];
 #pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        src[k] = nullptr;
-        const int e = __ldg(p.topk_idx + t * kTopK + k);
-        const int q = dest_rank(e, p.shards);
-        const int r = pick_row[t * kTopK + k];
-        if (q >= 0 && r >= 0) {
-          const int sh = q * p.shards + (e / kExpertsLocal) % p.shards;
+      for (int sh = 0; sh < kTopK; ++sh) {   // W * S = 8 shards
+        src[sh] = nullptr;
+        const int r = dest_row[t * kA2aMaxRanks + sh / S];
+        if (r >= 0) {
           const int row = p.slot[sh] != nullptr ? p.slot[sh][r] : r;
-          if (row >= 0) src[k] = p.y[sh] + static_cast<int64_t>(row) * kHidden;
+          if (row >= 0) src[sh] = p.y[sh] + static_cast<int64_t>(row) * kHidden;
         }
       }
       float4 u[kTopK], v[kTopK];
 #pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        u[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-        v[k] = u[k];
-        if (src[k] != nullptr) {
-          u[k] = reinterpret_cast<const float4*>(src[k])[j];
-          v[k] = reinterpret_cast<const float4*>(src[k])[kHalfQuads + j];
+      for (int sh = 0; sh < kTopK; ++sh) {
+        u[sh] = make_float4(0.f, 0.f, 0.f, 0.f);
+        v[sh] = u[sh];
+        if (src[sh] != nullptr) {
+          u[sh] = reinterpret_cast<const float4*>(src[sh])[j];
+          v[sh] = reinterpret_cast<const float4*>(src[sh])[kHalfQuads + j];
         }
       }
       float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float b[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int k = 0; k < kTopK; ++k) {
-        a[0] += u[k].x; a[1] += u[k].y; a[2] += u[k].z; a[3] += u[k].w;
-        a[4] += v[k].x; a[5] += v[k].y; a[6] += v[k].z; a[7] += v[k].w;
+      for (int sh = 0; sh < kTopK; ++sh) {
+        b[0] += u[sh].x; b[1] += u[sh].y; b[2] += u[sh].z; b[3] += u[sh].w;
+        b[4] += v[sh].x; b[5] += v[sh].y; b[6] += v[sh].z; b[7] += v[sh].w;
+        if ((sh + 1) % S == 0) {
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            a[c] += b[c];
+            b[c] = 0.f;
+          }
+        }
       }
       uint2* orow = reinterpret_cast<uint2*>(p.out + static_cast<int64_t>(t) * kHidden);
       orow[j] = pack_bf16x4(a[0], a[1], a[2], a[3]);
@@ -412,7 +445,7 @@ int a2a_params(void* const* rank_areas, int rank, int world, int shards_per_rank
   }
   const moe_b200_a2a_layout l = a2a_layout(max_tokens, cap);
   p->send_slot = l.send_slot;
-  p->pick_row = l.pick_row;
+  p->dest_row = l.dest_row;
   p->slab_idx = l.slab_idx;
   p->slab_w = l.slab_w;
   p->slab_scale = l.slab_scale;
@@ -473,9 +506,9 @@ int moe_b200_a2a_combine(const int32_t* topk_idx, void* const* shard_workspaces,
   if (st != MOE_B200_OK) return st;
   if (shard_workspaces == nullptr || (num_tokens > 0 && (!topk_idx || !output))) return MOE_B200_ERR_INVALID_ARGUMENT;
   if (reinterpret_cast<uintptr_t>(output) % 16 != 0) return MOE_B200_ERR_MISALIGNED;
-  // every shard's layer ran on recv_capacity rows with one given pick each
+  // every shard's layer ran on recv_capacity rows of up to 8 given picks
   moe_b200_workspace_layout l;
-  if (moe_b200_get_routed_workspace_layout(recv_capacity, 1, &l) != MOE_B200_OK)
+  if (moe_b200_get_routed_workspace_layout(recv_capacity, kTopK, &l) != MOE_B200_OK)
     return MOE_B200_ERR_INVALID_ARGUMENT;
   for (int q = 0; q < world * shards_per_rank; ++q) {
     uint8_t* ws = static_cast<uint8_t*>(shard_workspaces[q]);

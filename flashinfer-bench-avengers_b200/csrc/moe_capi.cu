@@ -435,7 +435,7 @@ static bool valid_routing(int method, int top_k, bool given_allowed = false) {
 
 extern "C" {
 
-int moe_b200_abi_version(void) { return 8; }
+int moe_b200_abi_version(void) { return 9; }
 
 int moe_b200_set_stage_events(void* const* events, int num_events) {
   if (events == nullptr) {

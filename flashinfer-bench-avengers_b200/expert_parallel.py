@@ -260,18 +260,20 @@ class TokenParallelEP:
     different batch on every rank) and owns S = 8 / world 32-expert shards:
     rank q owns global experts [32 S q, 32 S (q + 1)). One ``forward``:
     route the own tokens over all 256 experts (moe_b200_route), dispatch
-    every pick to the rank owning its expert (moe_b200_a2a_dispatch: the
-    token's e4m3 row, its 56 block scales, expert id and weight, written by
-    peer stores into that rank's receive slab), run each owned shard on the
-    received rows with the given routing (moe_b200_run_routed; its combine
-    rows stay in the shard's workspace), and combine (moe_b200_a2a_combine:
-    each own token's output is the fp32 sum, in pick order, of its picks'
-    rows read from the owning ranks, rounded once to bf16).
+    every token once to each rank it has picks on (moe_b200_a2a_dispatch:
+    the token's e4m3 row, its 56 block scales and its picks on that rank,
+    written by peer stores into that rank's receive slab), run each owned
+    shard on the received rows with the given routing (moe_b200_run_routed
+    with 8 picks per row; its combine rows stay in the shard's workspace),
+    and combine (moe_b200_a2a_combine: each own token's output is the fp32
+    sum of its combine rows on the destination ranks' shards, each rank's
+    shards in shard order and then the ranks in rank order, rounded once to
+    bf16).
 
     Each rank's PeerBuffers buffer holds the all-to-all area (counters,
     send plan, receive slab of ``recv_capacity`` rows) and one layer
     workspace per shard sized for the slab. ``recv_capacity`` defaults to
-    world * max_tokens * 8, which can never overflow. Every rank must call
+    world * max_tokens, which can never overflow. Every rank must call
     ``forward`` the same number of times (with any token count up to
     ``max_tokens``, also zero). ``close`` is collective.
     """
@@ -285,9 +287,9 @@ class TokenParallelEP:
             raise ValueError(f"world size {world} must divide {NUM_SHARDS}")
         self.max_tokens = int(max_tokens)
         self.shards_per_rank = NUM_SHARDS // world
-        self.cap = int(recv_capacity) if recv_capacity is not None else world * self.max_tokens * 8
+        self.cap = int(recv_capacity) if recv_capacity is not None else world * self.max_tokens
         a2a = moe_host.a2a_area_bytes(self.max_tokens, self.cap)
-        layer = moe_host.routed_workspace_bytes(self.cap, 1)
+        layer = moe_host.routed_workspace_bytes(self.cap, 8)
         if a2a == 0 or layer == 0:
             raise ValueError(f"max_tokens {max_tokens} / recv_capacity {self.cap} out of range")
         self.a2a_bytes = _round256(a2a)
@@ -349,18 +351,19 @@ class TokenParallelEP:
         base = self.peers.buf.data_ptr()
         lay = self.layout
         for s, (w13, s13, w2, s2) in enumerate(shards):
-            moe_host.run_routed_ptrs(base + lay.slab_idx, base + lay.slab_w, 1, base + lay.slab_rows,
+            moe_host.run_routed_ptrs(base + lay.slab_idx, base + lay.slab_w, 8, base + lay.slab_rows,
                                      base + lay.slab_scale, w13, s13, w2, s2,
                                      E_LOCAL * (self.rank * self.shards_per_rank + s), self.cap,
                                      self.workspaces[s])
         return moe_host.a2a_combine(idx, self.ws_ptrs, self.area_ptrs, self.rank, self.shards_per_rank,
                                     self.max_tokens, self.cap, out)
 
-    def pick_rows(self, T: int) -> torch.Tensor:
-        """int32 [T, 8]: the slab row of each of this rank's picks on its
-        destination (-1 for none), from the last dispatch."""
+    def dest_rows(self, T: int) -> torch.Tensor:
+        """int32 [T, world]: the slab row of each of this rank's tokens on
+        every destination rank (-1 where it has no pick), from the last
+        dispatch."""
         lay = self.layout
-        return self.area[lay.pick_row: lay.pick_row + 4 * T * 8].view(torch.int32).view(T, 8)
+        return self.area[lay.dest_row: lay.dest_row + 4 * T * 8].view(torch.int32).view(T, 8)[:, :self.world]
 
     def close(self) -> None:
         """Collective: unmaps the peers' buffers and frees this rank's."""

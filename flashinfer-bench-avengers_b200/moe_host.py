@@ -76,7 +76,7 @@ class A2aLayout(ctypes.Structure):
     _fields_ = [
         ("total_bytes", ctypes.c_size_t),
         ("send_slot", ctypes.c_size_t),
-        ("pick_row", ctypes.c_size_t),
+        ("dest_row", ctypes.c_size_t),
         ("slab_idx", ctypes.c_size_t),
         ("slab_w", ctypes.c_size_t),
         ("slab_scale", ctypes.c_size_t),

@@ -393,21 +393,24 @@ MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_
  * Per rank, an area of moe_b200_a2a_area_bytes(max_tokens, recv_capacity)
  * bytes that every rank maps (e.g. moe_b200_ep_buffer_alloc + IPC handles),
  * zero before the first call; max_tokens and recv_capacity must be the same
- * on every rank. recv_capacity rows bound what one rank can receive: world *
- * max_tokens * 8 can never overflow. One layer call, on every rank, on one
- * stream:
+ * on every rank. recv_capacity rows bound what one rank can receive (a row
+ * per token that has a pick on it): world * max_tokens can never overflow.
+ * One layer call, on every rank, on one stream:
  *   1. moe_b200_route on this rank's T tokens -> topk_idx, topk_w [T, 8];
- *   2. moe_b200_a2a_dispatch: every pick (token row e4m3, its 56 block
- *      scales, the expert id and weight) is stored into the receive slab of
- *      the rank owning the expert, rows ordered by (source rank, token, pick);
- *   3. per owned shard s: moe_b200_run_routed(slab_idx, slab_w, 1, slab_rows,
+ *   2. moe_b200_a2a_dispatch: every token is stored once into the receive
+ *      slab of each rank it has a pick on (its e4m3 row, its 56 block scales
+ *      and its 8 picks with only those on that rank kept, the others "no
+ *      expert" with weight 0), rows ordered by (source rank, token);
+ *   3. per owned shard s: moe_b200_run_routed(slab_idx, slab_w, 8, slab_rows,
  *      slab_scale, weights of s, 32 (S rank + s), recv_capacity, NULL,
  *      workspace of s, ...), with the slab offsets of moe_b200_a2a_get_layout
  *      (rows past the received count hold no pick) and workspaces of
- *      moe_b200_routed_workspace_bytes(recv_capacity, 1) bytes;
- *   4. moe_b200_a2a_combine: each own token's bf16 output is the fp32 sum, in
- *      pick order, of its picks' combine rows read from the owning ranks'
- *      workspaces (shard_workspaces: world * S, rank-major), rounded once.
+ *      moe_b200_routed_workspace_bytes(recv_capacity, 8) bytes;
+ *   4. moe_b200_a2a_combine: each own token's bf16 output is the fp32 sum of
+ *      its combine rows on every shard of every rank it was sent to (each
+ *      rank's shards in shard order, then the ranks in rank order), read from
+ *      the owning ranks' workspaces (shard_workspaces: world * S,
+ *      rank-major), rounded once.
  * Every rank must make all four steps for every call, also with T = 0. The
  * waits on peers give up after one second; then the area's status word gets
  * bit 1 << 7 and every rank's area is poisoned (bit 1 << 8 on later calls)
@@ -420,10 +423,10 @@ MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_
 #define MOE_B200_A2A_COUNTER_BYTES 512
 typedef struct moe_b200_a2a_layout {
   size_t total_bytes;
-  size_t send_slot;   /* int32[max_tokens, 8] index of each pick among this rank's picks for its destination */
-  size_t pick_row;    /* int32[max_tokens, 8] row of each pick in its destination's slab, -1 if none */
-  size_t slab_idx;    /* int32[recv_capacity] global expert id of each received row (none past the count) */
-  size_t slab_w;      /* fp32[recv_capacity] routing weight of each received row */
+  size_t send_slot;   /* int32[max_tokens, 8] per destination rank: index of the token among this rank's tokens sent there, -1 if none */
+  size_t dest_row;    /* int32[max_tokens, 8] per destination rank: the token's row in that rank's slab, -1 if none */
+  size_t slab_idx;    /* int32[recv_capacity, 8] global expert ids of each received row's picks (none past the count) */
+  size_t slab_w;      /* fp32[recv_capacity, 8] their routing weights */
   size_t slab_scale;  /* fp32[56, recv_capacity] block scales of the received rows */
   size_t slab_rows;   /* e4m3[recv_capacity, 7168] received token rows */
 } moe_b200_a2a_layout;

@@ -287,21 +287,33 @@ def a2a_dest(expert: torch.Tensor, shards_per_rank: int) -> torch.Tensor:
 
 
 def a2a_plan(topk_idx: torch.Tensor, world: int, shards_per_rank: int):
-    """Numbering of one rank's picks: (send_slot int64 [T, 8], counts int64
-    [W]). send_slot is the index of a pick among this rank's picks for the
-    same destination in (token, pick) order, -1 for none."""
-    dest = a2a_dest(topk_idx.reshape(-1), shards_per_rank)
-    slot = torch.full_like(dest, -1)
+    """Numbering of one rank's (token, destination) rows: (send_slot int64
+    [T, W], counts int64 [W]). send_slot[t, q] is the index of token t among
+    this rank's tokens that have a pick on rank q, in token order, -1 where
+    it has none (a token travels once to each rank it has picks on)."""
+    dest = a2a_dest(topk_idx, shards_per_rank).view(topk_idx.shape)
+    T = topk_idx.shape[0]
+    slot = torch.full((T, world), -1, dtype=torch.int64)
     counts = torch.zeros(world, dtype=torch.int64)
     for q in range(world):
-        hit = dest == q
-        slot[hit] = torch.arange(int(hit.sum()), dtype=torch.int64)
+        hit = (dest == q).any(dim=1)
+        slot[hit, q] = torch.arange(int(hit.sum()), dtype=torch.int64)
         counts[q] = int(hit.sum())
-    return slot.view(topk_idx.shape), counts
+    return slot, counts
+
+
+def a2a_row_picks(topk_idx: torch.Tensor, topk_w: torch.Tensor, t: int, dest_rank: int, shards_per_rank: int):
+    """The picks a (token, destination) row carries: token t's 8 slots, only
+    those on dest_rank kept (the others: no expert, weight 0)."""
+    dest = a2a_dest(topk_idx[t], shards_per_rank)
+    here = dest == dest_rank
+    ids = torch.where(here, topk_idx[t].to(torch.int64), torch.full_like(topk_idx[t], NO_EXPERT, dtype=torch.int64))
+    ws = torch.where(here, topk_w[t].to(torch.float32), torch.zeros(TOP_K, dtype=torch.float32))
+    return ids, ws
 
 
 def a2a_slab(src_rank: int, count_matrix: torch.Tensor, dest_rank: int) -> int:
-    """First slab row of source src_rank's picks on dest_rank: the picks of
+    """First slab row of source src_rank's rows on dest_rank: the rows of
     lower source ranks come first (count_matrix[src, dst])."""
     return int(count_matrix[:src_rank, dest_rank].sum())
 
@@ -314,8 +326,11 @@ def token_parallel_forward(tokens: list, shard_weights: dict, world: int):
     hidden_states_scale, routed_scaling_factor). shard_weights[offset] =
     (w13, s13, w2, s2) for the 8 shards. Returns (outputs, slabs): rank r's
     fp32 output [T_r, 7168], and per destination q the received rows in slab
-    order as (source rank, token, pick, expert, weight). Each output row is
-    the sum, in pick order, of w * expert(x) over the token's picks.
+    order as (source rank, token, expert ids [8], weights [8]). Each
+    destination's shards run on its rows with the rows' picks; a token's
+    output is the sum of its rows' results on every shard of every rank it
+    was sent to, each rank's shards in shard order, then the ranks in rank
+    order (rows of a shard without a pick there add zeros).
     """
     S = (E_GLOBAL // E_LOCAL) // world
     routes = [route(t["routing_logits"], t["routing_bias"], t["routed_scaling_factor"]) for t in tokens]
@@ -323,36 +338,37 @@ def token_parallel_forward(tokens: list, shard_weights: dict, world: int):
     M = torch.stack([c for _, c in plans])                     # [src, dst]
     slabs = [[None] * int(M[:, q].sum()) for q in range(world)]
     for r, ((idx, w), (slot, _)) in enumerate(zip(routes, plans)):
-        dest = a2a_dest(idx.reshape(-1), S).view(idx.shape)
         for t in range(idx.shape[0]):
-            for k in range(TOP_K):
-                q = int(dest[t, k])
-                if q >= 0:
-                    slabs[q][a2a_slab(r, M, q) + int(slot[t, k])] = (r, t, k, int(idx[t, k]), float(w[t, k]))
-    # each destination runs its shards on its slab rows (one given pick each)
+            for q in range(world):
+                if int(slot[t, q]) >= 0:
+                    ids, ws = a2a_row_picks(idx, w, t, q, S)
+                    slabs[q][a2a_slab(r, M, q) + int(slot[t, q])] = (r, t, ids, ws)
+    # each destination runs its shards on its slab rows (their picks given)
     contrib = {}
     for q in range(world):
         rows = slabs[q]
         if not rows:
             continue
-        hs = torch.stack([tokens[r]["hidden_states"][t] for r, t, _, _, _ in rows])
-        sc = torch.stack([tokens[r]["hidden_states_scale"][:, t] for r, t, _, _, _ in rows], dim=1)
-        gi = torch.tensor([[e] for _, _, _, e, _ in rows], dtype=torch.int64)
-        gw = torch.tensor([[wt] for _, _, _, _, wt in rows], dtype=torch.float32)
+        hs = torch.stack([tokens[r]["hidden_states"][t] for r, t, _, _ in rows])
+        sc = torch.stack([tokens[r]["hidden_states_scale"][:, t] for r, t, _, _ in rows], dim=1)
+        gi = torch.stack([ids for _, _, ids, _ in rows])
+        gw = torch.stack([ws for _, _, _, ws in rows])
         for s in range(S):
             off = E_LOCAL * (q * S + s)
             w13, s13, w2, s2 = shard_weights[off]
             y = moe_forward(None, None, hs, sc, w13, s13, w2, s2, off, 1.0, return_fp32=True, given=(gi, gw))
-            for j, (r, t, k, e, _) in enumerate(rows):
-                if off <= e < off + E_LOCAL:
-                    contrib[(r, t, k)] = y[j]
+            for j, (r, t, _, _) in enumerate(rows):
+                contrib[(r, t, q, s)] = y[j]
     outs = []
     for r, t_in in enumerate(tokens):
         T = t_in["hidden_states"].shape[0]
         out = torch.zeros(T, H, dtype=torch.float32)
         for t in range(T):
-            for k in range(TOP_K):
-                if (r, t, k) in contrib:
-                    out[t] = out[t] + contrib[(r, t, k)]
+            for q in range(world):
+                part = torch.zeros(H, dtype=torch.float32)
+                for s in range(S):
+                    if (r, t, q, s) in contrib:
+                        part = part + contrib[(r, t, q, s)]
+                out[t] = out[t] + part
         outs.append(out)
     return outs, slabs

@@ -130,7 +130,7 @@ def test_run_rejects_bad_arguments_without_a_device(lib):
     assert lib.moe_b200_route(None, None, 0, 4, 2.5, None, None, None) == 1
     assert lib.moe_b200_route(p, p, 0, 0, 2.5, p, p, None) == 0
     assert lib.moe_b200_set_stage_events(None, 0) == 0
-    assert lib.moe_b200_abi_version() == 8
+    assert lib.moe_b200_abi_version() == 9
 
 
 def test_widened_entry_points_reject_bad_arguments_without_a_device(lib):

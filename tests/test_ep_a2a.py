@@ -1,20 +1,22 @@
 """Token-parallel expert parallelism (all-to-all dispatch and combine) on B200s.
 
-Single GPU: world 1 owns all 8 shards, so every pick is dispatched to this
-GPU's own slab; that exercises the plan, the wire format, the routed layer
-on the slab and the pick-order combine without a peer. Checked: the slab
-rows, scales, expert ids and weights against the oracle's numbering of the
-picks (bit for bit), the output bit for bit against the fp32 sum in pick
-order of the picks' combine rows read back from the shard workspaces, within
-the operator tolerance of the oracle's restatement of the whole token-parallel
-layer, and the same on a second call (the counters advance).
+Single GPU: world 1 owns all 8 shards, so every token is dispatched to this
+GPU's own slab as one row with all its picks; that exercises the plan, the
+wire format, the routed layer on the slab and the combine without a peer.
+Checked: the slab rows, scales, expert ids and weights against the oracle's
+numbering of the (token, destination) rows (bit for bit), the output bit for
+bit against the fp32 sum in shard order of the token's combine rows read
+back from the shard workspaces, within the operator tolerance of the
+oracle's restatement of the whole token-parallel layer, and the same on a
+second call (the counters advance).
 
 2-4 GPUs: every rank has its own tokens (a different batch per rank) and 8/W
 shards; each rank's output must match, within the operator tolerance, the
 expert-parallel layer (NvlinkCombiner) run by every rank on the gathered
-batch of all ranks' tokens, be bit-identical to the pick-order fp32 sum of
-the picks' rows read back over peer memory, and leave the status words
-clear. Skipped below two GPUs.
+batch of all ranks' tokens, be bit-identical to the fp32 sum of the token's
+combine rows read back over peer memory (each rank's shards in shard order,
+then the ranks in rank order), and leave the status words clear. Skipped
+below two GPUs.
 """
 from __future__ import annotations
 
@@ -53,30 +55,26 @@ def _shard_rows(tp, s, rows):
     """fp32 combine rows of shard workspace s for slab rows `rows` (local)."""
     import moe_host
 
-    lay = moe_host.routed_workspace_layout(tp.cap, 1)
+    lay = moe_host.routed_workspace_layout(tp.cap, 8)
     ws = tp.workspaces[s]
     rows = rows.to(ws.device)
-    if tp.cap > 64:
-        slot = ws[lay.tok_slot: lay.tok_slot + 4 * tp.cap].view(torch.int32).long()
-        rows = slot[rows]
     y = ws[lay.y_acc: lay.y_acc + 4 * 7168 * tp.cap].view(torch.float32).view(tp.cap, 7168)
+    if tp.cap > 64:   # compact combine rows; a slab row without a pick here has none (zeros)
+        slot = ws[lay.tok_slot: lay.tok_slot + 4 * tp.cap].view(torch.int32).long()[rows]
+        return torch.where((slot >= 0)[:, None], y[slot.clamp(min=0)], torch.zeros_like(y[:1])).cpu()
     return y[rows].cpu()
 
 
 def _readback(tp, T):
-    """fp32 sum in pick order of the picks' combine rows (one GPU owns all
-    shards): the value the combine must round to bf16."""
-    idx = tp.topk_idx[:T].cpu().long()
-    rows = tp.pick_rows(T).cpu().long()
+    """fp32 sum in shard order of each token's combine rows (one GPU owns all
+    shards, every token is one slab row): the value the combine must round
+    to bf16."""
+    rows = tp.dest_rows(T)[:, 0].cpu().long()
     total = torch.zeros(T, 7168, dtype=torch.float32)
-    for k in range(8):
-        contrib = torch.empty(T, 7168, dtype=torch.float32)
-        for s in range(8):
-            sel = (idx[:, k] // 32) == s
-            if bool(sel.any()):
-                contrib[sel] = _shard_rows(tp, s, rows[sel, k])
-        total = total + contrib
-    return total
+    part = torch.zeros(T, 7168, dtype=torch.float32)
+    for s in range(8):
+        part = part + _shard_rows(tp, s, rows)
+    return total + part
 
 
 @pytest.mark.parametrize("T", [40, 520])
@@ -96,27 +94,27 @@ def test_token_parallel_single_gpu(cuda_device, T):
         tp.forward(tok, shards, out)
         torch.cuda.synchronize()
         assert tp.status() == 0
-        assert tp.slab_rows() == 8 * T
-        # the slab: the oracle's numbering of the picks, the wire format
+        assert tp.slab_rows() == T
+        # the slab: the oracle's numbering of the (token, destination) rows,
+        # the wire format (one rank: every token is a row with all its picks)
         idx = tp.topk_idx[:T].cpu()
         w = tp.topk_w[:T].cpu()
         slot, counts = moe_oracle.a2a_plan(idx, 1, 8)
-        assert int(counts[0]) == 8 * T
-        rows = tp.pick_rows(T).cpu().long()
+        assert int(counts[0]) == T
+        rows = tp.dest_rows(T).cpu().long()
         assert torch.equal(rows, slot)
         lay = tp.layout
         area = tp.area
-        s_idx = area[lay.slab_idx: lay.slab_idx + 4 * tp.cap].view(torch.int32).cpu()
-        s_w = area[lay.slab_w: lay.slab_w + 4 * tp.cap].view(torch.float32).cpu()
+        s_idx = area[lay.slab_idx: lay.slab_idx + 4 * 8 * tp.cap].view(torch.int32).view(tp.cap, 8).cpu()
+        s_w = area[lay.slab_w: lay.slab_w + 4 * 8 * tp.cap].view(torch.float32).view(tp.cap, 8).cpu()
         s_rows = area[lay.slab_rows: lay.slab_rows + tp.cap * 7168].view(tp.cap, 7168).cpu()
         s_sc = area[lay.slab_scale: lay.slab_scale + 4 * 56 * tp.cap].view(torch.float32).view(56, tp.cap).cpu()
-        flat = slot.flatten()
-        tok_of = torch.arange(T).repeat_interleave(8)
-        assert torch.equal(s_idx[flat], idx.flatten())
-        assert torch.equal(s_w[flat], w.flatten())
-        assert torch.equal(s_rows[flat], tok["hidden_states"].view(torch.uint8).cpu()[tok_of])
-        assert torch.equal(s_sc[:, flat], tok["hidden_states_scale"].cpu()[:, tok_of])
-        # the output: the pick-order sum of the picks' combine rows, rounded once
+        r0 = slot[:, 0]
+        assert torch.equal(s_idx[r0], idx)
+        assert torch.equal(s_w[r0], w)
+        assert torch.equal(s_rows[r0], tok["hidden_states"].view(torch.uint8).cpu())
+        assert torch.equal(s_sc[:, r0], tok["hidden_states_scale"].cpu())
+        # the output: the shard-order sum of the token's combine rows, rounded once
         exact = _readback(tp, T)
         assert torch.equal(out.cpu(), exact.to(torch.bfloat16))
         # against the oracle's token-parallel restatement (one rank)
@@ -198,28 +196,31 @@ def _worker(rank: int, world: int, port: int, sizes, results):
                 tp.forward(tok, shards, out)
             torch.cuda.synchronize()
             status = tp.status()
-            # pick-order fp32 sum of the picks' rows: every source sends where
-            # its picks went, every destination returns those rows from its
-            # own workspaces (local reads), the source sums them in pick order
-            idx = tp.topk_idx[:T_list[rank]].cpu().long()
-            rows = tp.pick_rows(T_list[rank]).cpu().long()
+            # the fp32 sum of each token's combine rows: every source says
+            # where its tokens went, every destination returns each of its
+            # shards' rows for them from its own workspaces (local reads),
+            # the source sums each rank's shards in shard order, then the
+            # ranks in rank order
+            rows = tp.dest_rows(T_list[rank]).cpu().long()
             asks = [None] * world
-            dist.all_gather_object(asks, (idx, rows))
+            dist.all_gather_object(asks, rows)
             answers = {}
-            for src, (s_idx, s_rows) in enumerate(asks):
-                for t in range(s_idx.shape[0]):
-                    for k in range(8):
-                        e = int(s_idx[t, k])
-                        if e // (32 * S) == rank:
-                            answers[(src, t, k)] = _shard_rows(tp, (e // 32) % S, s_rows[t, k:k + 1])[0]
+            for src, s_rows in enumerate(asks):
+                for t in range(s_rows.shape[0]):
+                    r = int(s_rows[t, rank])
+                    if r >= 0:
+                        for s in range(S):
+                            answers[(src, t, s)] = _shard_rows(tp, s, torch.tensor([r]))[0]
             replies = [None] * world
             dist.all_gather_object(replies, answers)
             exact = torch.zeros(T_list[rank], 7168, dtype=torch.float32)
-            for k in range(8):
-                for t in range(T_list[rank]):
-                    for rep in replies:
-                        if (rank, t, k) in rep:
-                            exact[t] = exact[t] + rep[(rank, t, k)]
+            for t in range(T_list[rank]):
+                for q, rep in enumerate(replies):
+                    part = torch.zeros(7168, dtype=torch.float32)
+                    for s in range(S):
+                        if (rank, t, s) in rep:
+                            part = part + rep[(rank, t, s)]
+                    exact[t] = exact[t] + part
             is_exact = torch.equal(out.cpu(), exact.to(torch.bfloat16))
             tp.close()
             # expert-parallel reference on the gathered batch of all ranks' tokens

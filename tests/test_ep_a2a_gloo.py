@@ -1,13 +1,15 @@
 """Token-parallel expert parallelism on CPU: two gloo ranks with different
 tokens, each owning four 32-expert shards, run the all-to-all protocol the
-library's kernels implement -- per-destination numbering of the picks
-(moe_oracle.a2a_plan), the exchange of the count matrix, receive slabs in
-(source rank, token, pick) order, the shards run on their slab rows with the
-given routing, and each token's output as the sum of its picks' rows in pick
-order -- with the CPU oracle as the layer. Each rank's result must equal the
-single-process restatement (moe_oracle.token_parallel_forward) bit for bit
-and the sum over all 8 shards of the ordinary layer on the rank's own tokens
-within fp32 rounding."""
+library's kernels implement -- per-destination numbering of the tokens that
+have picks there (moe_oracle.a2a_plan), the exchange of the count matrix,
+receive slabs of one row per (token, destination) in (source rank, token)
+order carrying the token's picks on that destination, the shards run on
+their slab rows with those picks, and each token's output as the sum of its
+rows' results (each rank's shards in shard order, then the ranks in rank
+order) -- with the CPU oracle as the layer. Each rank's result must equal
+the single-process restatement (moe_oracle.token_parallel_forward) bit for
+bit and the sum over all 8 shards of the ordinary layer on the rank's own
+tokens within fp32 rounding."""
 from __future__ import annotations
 
 import os
@@ -69,43 +71,47 @@ def _worker(rank, port, q):
         rows = [torch.zeros(WORLD, dtype=torch.int64) for _ in range(WORLD)]
         dist.all_gather(rows, counts)
         M = torch.stack(rows)
-        # dispatch: wire format of one pick = (token row, 56 scales, expert, weight)
-        dest = moe_oracle.a2a_dest(idx, SHARDS)
+        # dispatch: wire format of one (token, destination) row = (token row,
+        # 56 scales, its 8 picks with those on the destination kept)
         outgoing = [[] for _ in range(WORLD)]
         for t in range(idx.shape[0]):
-            for k in range(8):
-                d = int(dest[t, k])
+            for d in range(WORLD):
+                if int(slot[t, d]) < 0:
+                    continue
+                ids, ws = moe_oracle.a2a_row_picks(idx, w, t, d, SHARDS)
                 # e4m3 rows travel as their bytes (pickling keeps plain dtypes)
-                outgoing[d].append((int(slot[t, k]), t, k, mine["hidden_states"][t].view(torch.uint8).clone(),
-                                    mine["hidden_states_scale"][:, t].clone(), int(idx[t, k]), float(w[t, k])))
+                outgoing[d].append((int(slot[t, d]), t, mine["hidden_states"][t].view(torch.uint8).clone(),
+                                    mine["hidden_states_scale"][:, t].clone(), ids, ws))
         sent = [None] * WORLD
         dist.all_gather_object(sent, outgoing)
         slab = [None] * int(M[:, rank].sum())
         for src in range(WORLD):
-            for s_, t, k, row, sc, e, wt in sent[src][rank]:
-                slab[moe_oracle.a2a_slab(src, M, rank) + s_] = (src, t, k, row, sc, e, wt)
+            for s_, t, row, sc, ids, ws in sent[src][rank]:
+                slab[moe_oracle.a2a_slab(src, M, rank) + s_] = (src, t, row, sc, ids, ws)
         assert all(x is not None for x in slab)
-        # this rank's shards on its slab rows, routing given (one pick per row)
-        hs = torch.stack([x[3] for x in slab]).view(torch.float8_e4m3fn)
-        sc = torch.stack([x[4] for x in slab], dim=1)
-        gi = torch.tensor([[x[5]] for x in slab], dtype=torch.int64)
-        gw = torch.tensor([[x[6]] for x in slab], dtype=torch.float32)
+        # this rank's shards on its slab rows, the rows' picks given
+        hs = torch.stack([x[2] for x in slab]).view(torch.float8_e4m3fn)
+        sc = torch.stack([x[3] for x in slab], dim=1)
+        gi = torch.stack([x[4] for x in slab])
+        gw = torch.stack([x[5] for x in slab])
         back = {}
         for s in range(SHARDS):
             off = 32 * (rank * SHARDS + s)
             y = moe_oracle.moe_forward(None, None, hs, sc, *weights[off], off, 1.0, return_fp32=True, given=(gi, gw))
             for j, x in enumerate(slab):
-                if off <= x[5] < off + 32:
-                    back[(x[0], x[1], x[2])] = y[j]
-        # combine: each token's picks' rows, in pick order
+                back[(x[0], x[1], rank, s)] = y[j]
+        # combine: each token's rows, each rank's shards in shard order, then
+        # the ranks in rank order
         gathered = [None] * WORLD
         dist.all_gather_object(gathered, back)
         out = torch.zeros(idx.shape[0], 7168)
         for t in range(idx.shape[0]):
-            for k in range(8):
-                for g in gathered:
-                    if (rank, t, k) in g:
-                        out[t] = out[t] + g[(rank, t, k)]
+            for d in range(WORLD):
+                part = torch.zeros(7168)
+                for s in range(SHARDS):
+                    if (rank, t, d, s) in gathered[d]:
+                        part = part + gathered[d][(rank, t, d, s)]
+                out[t] = out[t] + part
         q.put((rank, out.numpy().tobytes(), M.numpy().tobytes()))
     finally:
         dist.destroy_process_group()
@@ -144,7 +150,12 @@ def test_token_parallel_protocol_on_gloo():
     all_tokens = [_tokens(r) for r in range(WORLD)]
     weights = _shard_weights(_needed(all_tokens))
     ref, slabs = moe_oracle.token_parallel_forward(all_tokens, weights, WORLD)
-    assert sum(len(s) for s in slabs) == 8 * sum(TOKENS)
+    # one row per (token, rank it has picks on): at most 4 ranks (4 groups)
+    dests = 0
+    for t_in in all_tokens:
+        idx, _ = moe_oracle.route(t_in["routing_logits"], t_in["routing_bias"], 2.5)
+        dests += int((torch.nn.functional.one_hot(moe_oracle.a2a_dest(idx, SHARDS), WORLD).sum(1) > 0).sum())
+    assert sum(len(s) for s in slabs) == dests
     for r in range(WORLD):
         assert torch.equal(got[r][0], ref[r])
         # the same layer as expert parallelism on the rank's own tokens: the
