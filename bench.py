@@ -623,6 +623,24 @@ def first_seed_with_local_pick(T: int, device, seed: int = SEED) -> int:
     raise RuntimeError("no seed with a local pick")
 
 
+def fixed_latency_split(p: dict, steps: int, warmup: int, flush, peaks, device) -> dict:
+    """Where a decode call's time goes beyond its weight bytes: the same
+    call with local_expert_offset 256, where no pick is local (routing, the
+    permutation, the GEMM launches that find no unit, the zero output),
+    against the call's bytes at the measured HBM peak."""
+    inp = workloads.make_inputs(p["T"], p["seed"], device, "uniform")
+    inp["local_expert_offset"] = 256
+    r = time_step([inp], steps, warmup, flush, do_flush=True, flushed_too=False)
+    empty_us = statistics.mean(r["call_ms"]) * 1e3
+    del r["out"]
+    bytes_us = p["roofline_us"]
+    return {"empty_call_us": round(empty_us, 2), "empty_call": "same tokens, local_expert_offset 256",
+            "bytes_at_hbm_peak_us": round(bytes_us, 2),
+            "rest_us": round(p["us_per_call"] - empty_us - bytes_us, 2),
+            "note": "us_per_call = empty_call_us (fixed latency) + bytes_at_hbm_peak_us + rest_us "
+                    "(streaming below peak and the stage hand-offs)"}
+
+
 def point(T: int, variant: str, steps: int, warmup: int, flush, peaks, device, seed=SEED) -> dict:
     inp = workloads.make_inputs(T, seed, device, variant)
     st = routing_stats(inp)
@@ -1003,6 +1021,8 @@ def main() -> None:
             p = point(T, "uniform", n_extra, warmup, flush, peaks, device, seed=seed)
             if T == 1:
                 p["seed_rule"] = f"first seed >= {SEED} whose token picks a local expert"
+            if T <= 16:
+                p["fixed_latency_split"] = fixed_latency_split(p, n_extra, warmup, flush, peaks, device)
             sweep.append(p)
         line["sweep"] = sweep
         line["prefill"] = point(4096, "hot", n_extra, warmup, flush, peaks, device)
