@@ -86,6 +86,7 @@ constexpr int kEpLLMaxTokens = kDecodeMaxTokens;
 constexpr int kLLPartLines = kHidden / 2;                 // flagged fp32 lines per row (2 values each)
 constexpr int kLLOutLines = kHidden / 4;                  // flagged bf16 lines per row (4 values each)
 constexpr int kLLPartRows = kEpLLMaxTokens + kEpMaxRanks;  // W slots of ceil(T / W) rows
+constexpr int kLLPollGroup = 4;                            // peers whose lines are loaded together
 
 // Layout of a rank's expert-parallel area (moe_b200_ep_area_bytes): the
 // counters and the flagged-line buffers sit at fixed offsets, so calls with
@@ -247,6 +248,16 @@ __device__ __forceinline__ void st_line(uint8_t* dst, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
+// One load of a flagged line (values in x and z, flags in y and w).
+__device__ __forceinline__ uint4 ld_line_once(const uint8_t* src) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(src)
+               : "memory");
+  return v;
+}
+
 // Polls a flagged line until both of its flags read `flag`; false once the
 // deadline (globaltimer) has passed.
 __device__ __forceinline__ bool ld_line(const uint8_t* src, uint32_t flag, uint64_t deadline, uint32_t& a,
@@ -316,30 +327,52 @@ __device__ bool combine_lines(const EpParams& p, uint32_t call, int first, int s
     const int line = it - rr * kLLOutLines;   // columns 4 line .. 4 line + 3
     const int t = mlo + rr;
     float a[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int r = 0; r < W; ++r) {
-      float v[4];
-      if (r == me) {
-        v[0] = v[1] = v[2] = v[3] = 0.f;
-        for (int s = 0; s < S; ++s) {
-          const float4 y = reinterpret_cast<const float4*>(p.y[me * S + s] + static_cast<int64_t>(t) * kHidden)[line];
-          v[0] += y.x;
-          v[1] += y.y;
-          v[2] += y.z;
-          v[3] += y.w;
+    // Ranks in groups of four: the lines of a group's peers are all loaded
+    // before any flag is checked (one round trip per group instead of one
+    // per line); only lines not yet written are polled again.
+    for (int r0 = 0; r0 < W; r0 += kLLPollGroup) {
+      uint4 l0[kLLPollGroup], l1[kLLPollGroup];
+#pragma unroll
+      for (int i = 0; i < kLLPollGroup; ++i) {
+        const int r = r0 + i;
+        if (r < W && r != me) {
+          const uint8_t* src =
+              mine + EpArea::kLLPart + (static_cast<size_t>(r * slot_rows + rr) * kLLPartLines + 2 * line) * 16;
+          l0[i] = ld_line_once(src);
+          l1[i] = ld_line_once(src + 16);
         }
-      } else {
-        const uint8_t* src = mine + EpArea::kLLPart + (static_cast<size_t>(r * slot_rows + rr) * kLLPartLines + 2 * line) * 16;
-        uint32_t x0, x1, x2, x3;
-        if (!ld_line(src, call, deadline, x0, x1) || !ld_line(src + 16, call, deadline, x2, x3)) return false;
-        v[0] = __uint_as_float(x0);
-        v[1] = __uint_as_float(x1);
-        v[2] = __uint_as_float(x2);
-        v[3] = __uint_as_float(x3);
       }
-      a[0] += v[0];
-      a[1] += v[1];
-      a[2] += v[2];
-      a[3] += v[3];
+#pragma unroll
+      for (int i = 0; i < kLLPollGroup; ++i) {
+        const int r = r0 + i;
+        if (r >= W) continue;
+        float v[4];
+        if (r == me) {
+          v[0] = v[1] = v[2] = v[3] = 0.f;
+          for (int s = 0; s < S; ++s) {
+            const float4 y =
+                reinterpret_cast<const float4*>(p.y[me * S + s] + static_cast<int64_t>(t) * kHidden)[line];
+            v[0] += y.x;
+            v[1] += y.y;
+            v[2] += y.z;
+            v[3] += y.w;
+          }
+        } else {
+          const uint8_t* src =
+              mine + EpArea::kLLPart + (static_cast<size_t>(r * slot_rows + rr) * kLLPartLines + 2 * line) * 16;
+          uint32_t x0 = l0[i].x, x1 = l0[i].z, x2 = l1[i].x, x3 = l1[i].z;
+          if (!(l0[i].y == call && l0[i].w == call) && !ld_line(src, call, deadline, x0, x1)) return false;
+          if (!(l1[i].y == call && l1[i].w == call) && !ld_line(src + 16, call, deadline, x2, x3)) return false;
+          v[0] = __uint_as_float(x0);
+          v[1] = __uint_as_float(x1);
+          v[2] = __uint_as_float(x2);
+          v[3] = __uint_as_float(x3);
+        }
+        a[0] += v[0];
+        a[1] += v[1];
+        a[2] += v[2];
+        a[3] += v[3];
+      }
     }
     const uint2 o = pack_bf16x4(a[0], a[1], a[2], a[3]);
     reinterpret_cast<uint2*>(out + static_cast<int64_t>(t) * kHidden * 2)[line] = o;
