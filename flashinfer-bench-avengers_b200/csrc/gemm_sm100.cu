@@ -98,7 +98,8 @@ struct GemmTraits {
   static constexpr int kOffUnitPre = kOffMisc + 16;
   static constexpr int kOffSeg = kOffUnitPre + 34 * 4;
   static constexpr int kOffCnt = kOffSeg + 34 * 4;
-  static constexpr int kOffUnits = kOffCnt + 32 * 4;
+  static constexpr int kOffSplits = kOffCnt + 32 * 4;
+  static constexpr int kOffUnits = kOffSplits + 32 * 4;
   static constexpr int kOffEpi = kOffUnits + kUnitSlots * 4;
   // epilogue scratch: red[4][BN] | inv[BN] | tok[BN] | w[BN]
   static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
@@ -114,12 +115,15 @@ struct Tile {
   int e, blk, ks, tt, row0, nvalid, kb0, kb1;
 };
 
+// Unit u -> tile. Units run expert by expert; within an expert token tile
+// fastest, then K slice, then row block. s_splits[e] is expert e's K slices.
 template <int BN, int kKBlocks>
 __device__ __forceinline__ void decode_tile(int u, const int* s_unit_pre, const int* s_seg,
-                                            const int* s_cnt, int splits, Tile& t) {
+                                            const int* s_cnt, const int* s_splits, Tile& t) {
   int e = 0;
 #pragma unroll 1
   while (s_unit_pre[e + 1] <= u) ++e;
+  const int splits = s_splits[e];
   const int cnt = s_cnt[e];
   const int nt = (cnt + BN - 1) / BN;
   int local = u - s_unit_pre[e];
@@ -246,6 +250,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   int* s_unit_pre = reinterpret_cast<int*>(smem + Tr::kOffUnitPre);
   int* s_seg = reinterpret_cast<int*>(smem + Tr::kOffSeg);
   int* s_cnt = reinterpret_cast<int*>(smem + Tr::kOffCnt);
+  int* s_splits = reinterpret_cast<int*>(smem + Tr::kOffSplits);
   float* s_red = reinterpret_cast<float*>(smem + Tr::kOffEpi);   // [4][BN]
   float* s_inv = s_red + 4 * BN;                                 // [BN]
   int* s_ctok = reinterpret_cast<int*>(s_inv + BN);              // [BN]
@@ -300,7 +305,15 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     // that is still running
     const int lo = __ldcg(p.seg_off + lane);
     const int cnt = __ldcg(p.counts + lane);
-    const int units = ((cnt + BN - 1) / BN) * Tr::kRowBlocks * splits;
+    // The last tail_experts active experts run tail_splits K slices: the
+    // final wave of units is then shorter, so fewer SMs idle at the end.
+    int my_splits = splits;
+    if (p.tail_splits > splits) {
+      const uint32_t active = __ballot_sync(0xffffffffu, cnt > 0);
+      const int later = __popc(active & ~((2u << lane) - 1u));   // active experts after this one
+      if (cnt > 0 && later < p.tail_experts) my_splits = p.tail_splits;
+    }
+    const int units = ((cnt + BN - 1) / BN) * Tr::kRowBlocks * my_splits;
     int incl = units;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -310,6 +323,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     s_unit_pre[lane + 1] = incl;
     s_seg[lane] = lo;
     s_cnt[lane] = cnt;
+    s_splits[lane] = my_splits;
     if (lane == 0) s_unit_pre[0] = 0;
   }
   tc_fence_before();
@@ -330,7 +344,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
     int pre_issued = 0;
     if (u >= 0 && early_tables) {
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
       const int nkb = t.kb1 - t.kb0;
       const int rot = (t.blk * 5 + t.e * 3) % nkb;
       pre_issued = nkb < kStages ? nkb : kStages;
@@ -375,7 +389,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
       int arow0, arow1 = 0, wrow0, wrow1 = 0;
       if constexpr (Tr::kIsG1) {
         arow0 = t.e * kGemm1Out + t.blk * kBlk;
@@ -479,7 +493,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&full_bar[stage]), ph, s_abort, p.status, kStatusTimeoutMma) ||
             !mbar_wait(smem_u32(&acce_bar[abuf]), aph ^ 1, s_abort, p.status, kStatusTimeoutMma)) {
@@ -526,7 +540,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
       for (int kb = t.kb0; kb < t.kb1; ++kb) {
         if (!mbar_wait(smem_u32(&sraw_bar[slot]), sph, s_abort, p.status, kStatusTimeoutScale)) {
           ok = false;
@@ -620,7 +634,7 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       if (++uslot == Tr::kUnitSlots) { uslot = 0; uph ^= 1; }
       if (u < 0) break;
       Tile t;
-      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, splits, t);
+      decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
       // per-column data for the final epilogue, loaded early
       int my_tok = 0;
       float my_w = 0.f;

@@ -135,6 +135,8 @@ struct GemmParams {
   int num_tokens;           // T
   int cap;                  // row capacity of the permuted buffers (8T)
   int splits;               // K slices per output tile
+  int tail_splits;          // K slices of the last tail_experts active experts (<= splits: off)
+  int tail_experts;
   uint8_t* c_hi;            // [cap, 2048] e4m3
   uint8_t* c_lo;            // [cap, 2048] e4m3
   float* c_scale;           // [16, cap] written by kGemm1Fused / swiglu_quant
