@@ -101,11 +101,11 @@ struct GemmTraits {
   static constexpr int kOffSplits = kOffCnt + 32 * 4;
   static constexpr int kOffUnits = kOffSplits + 32 * 4;
   static constexpr int kOffEpi = kOffUnits + kUnitSlots * 4;
-  // epilogue scratch: red[4][BN] | inv[BN] | tok[BN] | w[BN]
-  static constexpr int kEpiBytes = (4 * BN + 3 * BN) * 4;
+  // epilogue scratch (GEMM1 fused epilogue): red[4][BN] | inv[BN]
+  static constexpr int kEpiBytes = (4 * BN + BN) * 4;
   static constexpr int kSmemBytes = kOffEpi + kEpiBytes + 1024;  // + alignment slack
 
-  static_assert(BN % 16 == 0 && BN >= 16 && kMmaN <= 256, "BN");
+  static_assert(BN % 16 == 0 && BN >= 16 && kMmaN <= 256 && kColsPerLane <= 2, "BN");
   static_assert(2 * kAccCols <= 512, "two accumulator buffers must fit in TMEM");
   static_assert(kEpiWarps % 4 == 0 && kCPT >= 16 && kCPT % 16 == 0, "epilogue column split");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
@@ -253,8 +253,6 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
   int* s_splits = reinterpret_cast<int*>(smem + Tr::kOffSplits);
   float* s_red = reinterpret_cast<float*>(smem + Tr::kOffEpi);   // [4][BN]
   float* s_inv = s_red + 4 * BN;                                 // [BN]
-  int* s_ctok = reinterpret_cast<int*>(s_inv + BN);              // [BN]
-  float* s_cw = reinterpret_cast<float*>(s_ctok + BN);           // [BN]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -635,13 +633,21 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
       if (u < 0) break;
       Tile t;
       decode_tile<BN, Tr::kKBlocks>(u, s_unit_pre, s_seg, s_cnt, s_splits, t);
-      // per-column data for the final epilogue, loaded early
-      int my_tok = 0;
-      float my_w = 0.f;
-      if constexpr (!Tr::kIsG1) {
-        if (et < BN && et < t.nvalid) {
-          my_tok = p.perm_row[t.row0 + et];
-          my_w = p.perm_w[t.row0 + et];
+      // per-column data for the final epilogue, loaded early by every
+      // epilogue warp itself (lane l: columns l and l + 32), so the warps
+      // share nothing through shared memory and need no barrier
+      int my_tok[Tr::kColsPerLane];
+      float my_w[Tr::kColsPerLane];
+#pragma unroll
+      for (int i = 0; i < Tr::kColsPerLane; ++i) {
+        my_tok[i] = 0;
+        my_w[i] = 0.f;
+        if constexpr (!Tr::kIsG1) {
+          const int c = lane + 32 * i;
+          if (c < BN && c < t.nvalid) {
+            my_tok[i] = p.perm_row[t.row0 + c];
+            my_w[i] = p.perm_w[t.row0 + c];
+          }
         }
       }
 #pragma unroll
@@ -729,18 +735,16 @@ __global__ void __launch_bounds__(GemmTraits<kKind, BN, kStages, kEpiWarps>::kTh
           }
         }
       } else {
-        named_bar_sync(1, kEpiThreads);
-        if (et < BN) {
-          s_ctok[et] = my_tok;
-          s_cw[et] = my_w;
-        }
-        named_bar_sync(1, kEpiThreads);
         const int col = t.blk * Tr::kNumA * kBlk + row_in_tile;
 #pragma unroll
         for (int c = 0; c < CPT; ++c) {
-          if (col0 + c < t.nvalid) {
-            float* dst = p.y_acc + static_cast<int64_t>(s_ctok[col0 + c]) * kHidden + col;
-            const float w = s_cw[col0 + c];
+          // column col0 + c's token row and weight, from the lane that loaded them
+          const int cc = col0 + c;
+          const int reg = Tr::kColsPerLane > 1 ? cc / 32 : 0;
+          const int tok = __shfl_sync(0xffffffffu, reg == 0 ? my_tok[0] : my_tok[Tr::kColsPerLane - 1], cc & 31);
+          const float w = __shfl_sync(0xffffffffu, reg == 0 ? my_w[0] : my_w[Tr::kColsPerLane - 1], cc & 31);
+          if (cc < t.nvalid) {
+            float* dst = p.y_acc + static_cast<int64_t>(tok) * kHidden + col;
             red_add_f32(dst, acc0[c] * w);
             if constexpr (Tr::kNumA == 2) red_add_f32(dst + kBlk, acc1[c] * w);
           }
