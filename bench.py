@@ -99,7 +99,7 @@ PUBLISHED_US = {1: 551.0, 7: 1034.0, 14: 1609.0, 15: 850.0, 16: 1727.0, 32: 2803
 # DRAM traffic per launch (dram__bytes_read.sum + dram__bytes_write.sum) from
 # the ncu captures summarised in profiles/, keyed by (kernel, T) of the bench
 # workloads; None when no capture of that launch exists.
-NCU_TRAFFIC_BYTES = {("gemm1", 64): 472_753_920 + 6_198_016, ("gemm1", 4096): 860_626_688 + 72_598_016}
+NCU_TRAFFIC_BYTES = {("gemm1", 64): 472_752_896 + 9_058_048, ("gemm1", 4096): 860_626_688 + 72_598_016}
 
 
 def load_peaks() -> dict:
