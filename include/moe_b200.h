@@ -314,8 +314,9 @@ MOE_B200_API int moe_b200_noalloc_read_status(uint32_t* status, void* stream);
  *
  * Every rank must call it once per layer call, on the stream of its
  * moe_b200_run, with the same num_tokens. Each EP area must be zero before
- * the first call (its counters and call numbers only grow, so later calls
- * need no clearing). Each wait on a peer gives up after one second, sets
+ * the first call; later calls need no clearing (the call number kept in the
+ * area grows with every call, and each call's last CTA clears the per-call
+ * counters itself). Each wait on a peer gives up after one second, sets
  * status bit 1 << 7 (moe_b200_read_status) and marks every rank's area as
  * poisoned: from then on every combine on those areas returns at once with
  * status bit 1 << 8 and writes no output. To recover, every rank
