@@ -326,6 +326,17 @@ class TokenParallelEP:
             st |= moe_host.read_status(ws)
         return st
 
+    def reset(self) -> None:
+        """Collective: clears every rank's counter block after an all-to-all
+        wait gave up (status bits 1 << 7 / 1 << 8); call numbers restart."""
+        import moe_host
+
+        torch.cuda.synchronize(self.device)
+        self.peers.barrier()
+        self.area[:moe_host.A2A_COUNTER_BYTES].zero_()
+        torch.cuda.synchronize(self.device)
+        self.peers.barrier()
+
     def forward(self, token_inputs: dict, shards: list, out: torch.Tensor) -> torch.Tensor:
         """token_inputs: this rank's routing_logits [T, 256], routing_bias,
         hidden_states e4m3 [T, 7168], hidden_states_scale [56, T],

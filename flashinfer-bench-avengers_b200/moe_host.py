@@ -29,6 +29,10 @@ MAX_TOKENS = 262144
 # Calls with at least this many tokens run the token-major prefill GEMMs
 # (kTokenMajorMinTokens, moe_capi.cu).
 TOKEN_MAJOR_MIN_TOKENS = 512
+# Sizes of the counter blocks at the start of an EP area and of an
+# all-to-all area (MOE_B200_EP_COUNTER_BYTES, MOE_B200_A2A_COUNTER_BYTES).
+EP_COUNTER_BYTES = 256
+A2A_COUNTER_BYTES = 512
 
 BIAS_BF16 = 0
 BIAS_FP32 = 1

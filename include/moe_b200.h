@@ -394,7 +394,9 @@ MOE_B200_API int moe_b200_run_routed(const int32_t* topk_idx, const float* topk_
  * Per rank, an area of moe_b200_a2a_area_bytes(max_tokens, recv_capacity)
  * bytes that every rank maps (e.g. moe_b200_ep_buffer_alloc + IPC handles),
  * zero before the first call; max_tokens and recv_capacity must be the same
- * on every rank. recv_capacity rows bound what one rank can receive (a row
+ * on every rank, and so must the GPUs' SM counts (dispatch runs two CTAs per
+ * SM, and each rank waits until every rank's CTAs have written into its
+ * slab, counting them as world x its own grid). recv_capacity rows bound what one rank can receive (a row
  * per token that has a pick on it): world * max_tokens can never overflow.
  * One layer call, on every rank, on one stream:
  *   1. moe_b200_route on this rank's T tokens -> topk_idx, topk_w [T, 8];

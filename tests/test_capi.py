@@ -38,6 +38,19 @@ def test_header_declares_the_entry_points():
         assert n in names
 
 
+def test_host_constants_match_the_header():
+    import moe_host
+
+    text = open(HEADER).read()
+
+    def define(name):
+        return int(re.search(rf"#define\s+{name}\s+(\d+)", text).group(1))
+
+    assert moe_host.MAX_TOKENS == define("MOE_B200_MAX_TOKENS")
+    assert moe_host.EP_COUNTER_BYTES == define("MOE_B200_EP_COUNTER_BYTES")
+    assert moe_host.A2A_COUNTER_BYTES == define("MOE_B200_A2A_COUNTER_BYTES")
+
+
 def test_library_exports_every_declared_symbol(lib):
     for name in declared_functions():
         assert hasattr(lib, name), f"{name} declared in moe_b200.h but not exported"
