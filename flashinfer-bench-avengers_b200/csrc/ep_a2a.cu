@@ -237,15 +237,21 @@ __global__ void __launch_bounds__(kPlanThreads) a2a_plan_kernel(A2aParams p) {
 // ---------------------------------------------------------------- dispatch
 __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_dispatch_kernel(A2aParams p) {
   __shared__ int s_ok;
+  __shared__ int s_live;
   __shared__ int s_off[kA2aMaxRanks];
   __shared__ int s_recv;
   pdl_wait();   // the plan kernel has published this rank's counts
   const int W = p.world;
   uint8_t* mine = p.area[p.rank];
-  if (poisoned(p)) return;   // the plan kernel has set the status bit
-  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + A2aCounters::kCalls) + 1u;
-  if (threadIdx.x == 0) s_ok = 1;
+  // the poison word is read once for the CTA (a peer may set it meanwhile),
+  // so every thread takes the same path through the barriers below
+  if (threadIdx.x == 0) {
+    s_live = poisoned(p) ? 0 : 1;
+    s_ok = 1;
+  }
   __syncthreads();
+  if (!s_live) return;   // the plan kernel has set the status bit
+  const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + A2aCounters::kCalls) + 1u;
   if (threadIdx.x < W &&
       !wait_at_least(ctr(mine, A2aCounters::kFlagsDispatch) + threadIdx.x, call)) {
     give_up(p);
@@ -333,16 +339,21 @@ __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_dispatch_kerne
 // ---------------------------------------------------------------- combine
 __global__ void __launch_bounds__(kA2aThreads, kA2aCtasPerSm) a2a_combine_kernel(A2aParams p) {
   __shared__ int s_ok;
+  __shared__ int s_live;
   pdl_wait();   // this rank's layer calls on its slab have completed
   const int W = p.world;
   uint8_t* mine = p.area[p.rank];
-  if (poisoned(p)) {
+  // one read of the poison word for the CTA, as in the dispatch
+  if (threadIdx.x == 0) {
+    s_live = poisoned(p) ? 0 : 1;
+    s_ok = 1;
+  }
+  __syncthreads();
+  if (!s_live) {
     if (threadIdx.x == 0) set_status(p, kStatusPoisoned);
     return;
   }
   const uint32_t call = *reinterpret_cast<volatile uint32_t*>(mine + A2aCounters::kCalls) + 1u;
-  if (threadIdx.x == 0) s_ok = 1;
-  __syncthreads();
   if (blockIdx.x == 0 && threadIdx.x < W)
     st_release_sys(ctr(p.area[threadIdx.x], A2aCounters::kFlagsCombine) + p.rank, static_cast<int>(call));
   if (threadIdx.x < W && !wait_at_least(ctr(mine, A2aCounters::kFlagsCombine) + threadIdx.x, call)) {

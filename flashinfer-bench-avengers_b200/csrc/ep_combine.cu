@@ -493,6 +493,7 @@ __device__ bool combine_staged(const EpParams& p, uint32_t call, int first, int 
 
 __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(EpParams p) {
   __shared__ int s_ok;
+  __shared__ int s_poisoned;
   pdl_wait();   // this rank's layer calls (their GEMM2 reductions) have completed
   const int W = p.world;
   const int T = p.num_tokens;
@@ -512,7 +513,11 @@ __global__ void __launch_bounds__(kEpThreads, kEpCtasPerSm) ep_combine_kernel(Ep
   }
 
   uint8_t* mine = p.area[p.rank];
-  if (*reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0) {
+  // one read for the whole CTA: a peer may poison the area meanwhile, and
+  // every thread must take the same path (barriers below)
+  if (threadIdx.x == 0) s_poisoned = *reinterpret_cast<volatile int*>(mine + EpArea::kPoison) != 0;
+  __syncthreads();
+  if (s_poisoned) {
     if (threadIdx.x == 0) atomicOr(p.status, kStatusPoisoned);
     return;
   }
