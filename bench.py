@@ -576,14 +576,20 @@ def cpu_oracle_time(inp: dict, runs: int = 3) -> dict:
         cpu_inp[k] = host
     cargs = workloads.as_args(cpu_inp)
     moe_oracle.moe_forward(*cargs)   # warm-up
-    times = []
+    times, route_times = [], []
     for _ in range(runs):
         t0 = time.perf_counter()
         moe_oracle.moe_forward(*cargs)
         times.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        moe_oracle.route(cpu_inp["routing_logits"], cpu_inp["routing_bias"], inp["routed_scaling_factor"])
+        route_times.append(time.perf_counter() - t0)
     T = inp["routing_logits"].shape[0]
-    return {"value": round(statistics.median(times) * 1e6, 1), "unit": UNIT, "cores": torch.get_num_threads(),
+    total_us = statistics.median(times) * 1e6
+    route_us = statistics.median(route_times) * 1e6
+    return {"value": round(total_us, 1), "unit": UNIT, "cores": torch.get_num_threads(),
             "kind": "port", "runs_s": [round(t, 3) for t in times],
+            "routing_us": round(route_us, 1), "experts_us": round(total_us - route_us, 1),
             "sample": f"T={T}, all {len(active)} active experts (the whole call), median of {runs} runs "
                       f"after one warm-up"}
 
@@ -1044,6 +1050,14 @@ def main() -> None:
         c0 = workloads.make_inputs(16, 0, device)
         line["cpu_baseline_config0"] = cpu_oracle_time(c0)
         del c0
+        # the other two sizes of the CPU baseline, on the sweep's T=1 inputs
+        # and the prefill point's
+        pts = []
+        for T, variant, seed in ((1, "uniform", line["sweep"][0]["seed"]), (4096, "hot", SEED)):
+            ci = workloads.make_inputs(T, seed, device, variant)
+            pts.append({"T": T, "variant": variant, "seed": seed, **cpu_oracle_time(ci)})
+            del ci
+        line["cpu_baseline_points"] = pts
 
     if group is not None:
         dist.barrier(group=group)
