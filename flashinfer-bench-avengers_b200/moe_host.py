@@ -242,6 +242,16 @@ def _check(cond: bool, msg: str) -> None:
         raise RuntimeError(msg)
 
 
+def _check_same_cuda_device(**tensors) -> None:
+    """Every tensor is a CUDA tensor on the first one's device (the kernels
+    dereference their pointers on that device)."""
+    dev = None
+    for name, t in tensors.items():
+        _check(isinstance(t, torch.Tensor) and t.is_cuda, f"{name} must be a CUDA tensor")
+        dev = t.device if dev is None else dev
+        _check(t.device == dev, f"{name} must be on {dev}")
+
+
 def _check_inputs(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                   gemm1_weights_scale, gemm2_weights, gemm2_weights_scale) -> int:
     """Checks the layer inputs; hidden_states_scale None means bf16 hidden
@@ -516,6 +526,9 @@ def run_routed_ptrs(topk_idx_ptr: int, topk_w_ptr: int, top_k: int, hidden_ptr: 
                                 torch.float32)):
         _check(isinstance(t, torch.Tensor) and t.is_cuda and tuple(t.shape) == shape and t.dtype == dt
                and t.is_contiguous(), f"{name} must be a contiguous CUDA {dt} tensor of shape {shape}")
+    _check_same_cuda_device(gemm1_weights=gemm1_weights, gemm1_weights_scale=gemm1_weights_scale,
+                            gemm2_weights=gemm2_weights, gemm2_weights_scale=gemm2_weights_scale,
+                            workspace=workspace, **({"output": output} if output is not None else {}))
     if output is not None:
         _check(output.dtype == torch.bfloat16 and tuple(output.shape) == (int(num_tokens), H)
                and output.is_contiguous(), f"output must be a contiguous bf16 [T, {H}] tensor")
@@ -579,6 +592,8 @@ def a2a_dispatch(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states: to
                  hidden_states_scale: torch.Tensor, max_tokens: int, recv_capacity: int, rank_area_ptrs: list[int],
                  rank: int, shards_per_rank: int) -> None:
     """moe_b200_a2a_dispatch of this rank's T tokens (picks from moe_b200_route)."""
+    _check_same_cuda_device(topk_idx=topk_idx, topk_w=topk_w, hidden_states=hidden_states,
+                            hidden_states_scale=hidden_states_scale)
     T = int(hidden_states.shape[0])
     _check(tuple(topk_idx.shape) == (T, TOP_K) and topk_idx.dtype == torch.int32 and topk_idx.is_contiguous(),
            "topk_idx must be int32 [T, 8]")
@@ -600,7 +615,10 @@ def a2a_dispatch(topk_idx: torch.Tensor, topk_w: torch.Tensor, hidden_states: to
 def a2a_combine(topk_idx: torch.Tensor, shard_workspace_ptrs: list[int], rank_area_ptrs: list[int], rank: int,
                 shards_per_rank: int, max_tokens: int, recv_capacity: int, output: torch.Tensor) -> torch.Tensor:
     """moe_b200_a2a_combine into this rank's bf16 output [T, 7168]."""
+    _check_same_cuda_device(topk_idx=topk_idx, output=output)
     T = int(topk_idx.shape[0])
+    _check(tuple(topk_idx.shape) == (T, TOP_K) and topk_idx.dtype == torch.int32 and topk_idx.is_contiguous(),
+           "topk_idx must be int32 [T, 8]")
     _check(output.is_cuda and output.dtype == torch.bfloat16 and output.is_contiguous()
            and tuple(output.shape) == (T, H), f"output must be a contiguous bf16 [T, {H}] tensor")
     dev = output.device

@@ -34,6 +34,22 @@ def test_run_requires_cuda_tensors(cpu_args):
         moe_host.run(*cpu_args)
 
 
+def test_all_to_all_wrappers_require_cuda_tensors():
+    """The token-parallel dispatch and combine refuse host tensors before
+    any library call (their kernels would dereference host pointers)."""
+    import moe_host
+
+    T = 4
+    idx = torch.zeros(T, 8, dtype=torch.int32)
+    w = torch.zeros(T, 8)
+    hs = torch.zeros(T, 7168, dtype=torch.float8_e4m3fn)
+    sc = torch.ones(56, T)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        moe_host.a2a_dispatch(idx, w, hs, sc, T, 2 * T, [0, 0], 0, 4)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        moe_host.a2a_combine(idx, [0] * 8, [0, 0], 0, 4, T, 2 * T, torch.zeros(T, 7168, dtype=torch.bfloat16))
+
+
 def test_check_inputs_shapes_and_dtypes(cpu_args, monkeypatch):
     import moe_host
 
